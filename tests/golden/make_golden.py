@@ -1,0 +1,253 @@
+"""Generate the committed golden fixtures under tests/golden/.
+
+Run in a container that has the reference checkout (it is read, never
+modified):
+
+    python tests/golden/make_golden.py /root/reference
+
+Fixtures:
+
+* ``codec_cases.npz`` — small BF16 tensors (seeded normal, all-zero, constant,
+  ragged sizes, tiny sizes, random bit patterns), their exponent / sign+mantissa
+  planes, their LZ4HC-9 and LZ4-fast chunk blocks produced by liblz4 (the
+  reference codec library), and the bytes liblz4 decodes them back to.
+* ``qwen_block.npz`` / ``deepseek_block.npz`` — inputs are regenerated from
+  seeds by the tests; the fixture holds the outputs of the reference's own
+  ``customized/qwen.py`` Qwen2MoEBlock and ``customized/deepseek.py``
+  DeepseekMoEBlock (with the ``MoEGate`` / ``DeepseekV2MLP`` classes of
+  ``models/deepseek/modeling_deepseek.py``).  Their expert dispatcher is
+  replaced by a CPU stand-in that runs each expert module on its gathered
+  tokens, which is what ``ExpertDispatcher::GPUExecFunc`` computes
+  (``csrc/dispatcher/expert_module.cpp:39-50``), returning results in expert
+  order.
+"""
+from __future__ import annotations
+
+import ast
+import hashlib
+import importlib.util
+import os
+import sys
+import types
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, REPO)
+sys.path.insert(0, os.path.join(REPO, "zipmoe-icml26_b200"))
+
+from oracle import codec  # noqa: E402
+from zmoe import synthetic as syn  # noqa: E402
+
+
+def digest(*tensors) -> str:
+    h = hashlib.sha256()
+    for t in tensors:
+        if isinstance(t, torch.Tensor):
+            t = t.detach().contiguous().view(torch.uint8).numpy() if t.dtype != torch.uint8 else t.numpy()
+        h.update(np.ascontiguousarray(t).tobytes())
+    return h.hexdigest()
+
+
+# ---------------------------------------------------------------------------
+# codec
+# ---------------------------------------------------------------------------
+def codec_cases():
+    gen = torch.Generator().manual_seed(0)
+    cases = {
+        "normal_64x256": (torch.randn(64, 256, generator=gen) * 0.02).to(torch.bfloat16),
+        "normal_ragged_37x53": (torch.randn(37, 53, generator=gen) * 0.08).to(torch.bfloat16),
+        "zeros_32x512": torch.zeros(32, 512, dtype=torch.bfloat16),
+        "const_16x1000": torch.full((16, 1000), 0.0123, dtype=torch.bfloat16),
+        "tiny_1": torch.tensor([1.5], dtype=torch.bfloat16),
+        "tiny_5": torch.tensor([1.0, -2.0, 3.0, 0.0, -0.5], dtype=torch.bfloat16),
+        "random_bits_4099": torch.randint(0, 65536, (4099,), generator=gen, dtype=torch.int32)
+        .to(torch.int16).view(torch.bfloat16),
+        "normal_32x2048": (torch.randn(32, 2048, generator=gen) * 0.02).to(torch.bfloat16),
+    }
+    out = {}
+    names = []
+    for name, t in cases.items():
+        bits = codec.bf16_bits(t)
+        out[name + "__bits"] = bits
+        for chunks in (1, 3, 5):
+            if bits.size < chunks:
+                continue
+            for cod in ("LZ4HC", "LZ4"):
+                key = f"{name}__c{chunks}__{cod}"
+                blocks, osz, sm = codec.encode_tensor(bits, chunks, cod, 9, 5)
+                exp_dec = np.concatenate([codec.lz4_decompress(b, o) for b, o in zip(blocks, osz)])
+                assert np.array_equal(exp_dec, codec.split_planes(bits)[0])
+                out[key + "__osz"] = np.array(osz, dtype=np.int64)
+                out[key + "__csz"] = np.array([len(b) for b in blocks], dtype=np.int64)
+                out[key + "__blocks"] = np.frombuffer(b"".join(blocks), dtype=np.uint8)
+                names.append(key)
+    out["names"] = np.array(names)
+    out["tensors"] = np.array(list(cases))
+    out["lz4_version"] = np.array(codec.lz4_version())
+    np.savez_compressed(os.path.join(HERE, "codec_cases.npz"), **out)
+    print("codec cases:", len(names))
+
+
+# ---------------------------------------------------------------------------
+# MoE blocks from the reference's Python
+# ---------------------------------------------------------------------------
+class _CPUExecutor:
+    """Stand-in for ExpertExecutor.dispatch_local (experts/expert_executor.py:40-84)."""
+
+    def __init__(self, block):
+        self.block = block
+
+    def dispatch_local(self, hidden_states, router_mask, layer_id):
+        mask = router_mask.view(-1, router_mask.shape[-1])
+        h = hidden_states.view(-1, hidden_states.shape[-1])
+        res = []
+        for e in range(mask.shape[-1]):
+            tok = mask[:, e].bool()
+            if int(tok.sum()) == 0:
+                continue
+            res.append((self.block.experts[e](h[tok]), layer_id, e, 1))
+        return res
+
+
+def _load_qwen(ref):
+    spec = importlib.util.spec_from_file_location("ref_qwen_block", os.path.join(ref, "customized", "qwen.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def _load_deepseek(ref):
+    """Build MoEGate / DeepseekV2MLP from modeling_deepseek.py's class bodies
+    (the module itself imports symbols newer transformers dropped) and load
+    customized/deepseek.py against them."""
+    src = open(os.path.join(ref, "models", "deepseek", "modeling_deepseek.py")).read()
+    tree = ast.parse(src)
+    keep = [n for n in tree.body if isinstance(n, ast.ClassDef) and n.name in ("MoEGate", "DeepseekV2MLP")]
+    import math
+    import torch.nn.functional as F
+    from torch import nn
+    from torch.nn import init
+    from transformers.activations import ACT2FN
+    ns = {"torch": torch, "nn": nn, "F": F, "math": math, "init": init, "ACT2FN": ACT2FN}
+    exec(compile(ast.Module(body=keep, type_ignores=[]), "modeling_deepseek.py", "exec"), ns)
+    models_pkg = types.ModuleType("models")
+    ds_pkg = types.ModuleType("models.deepseek")
+    ds_pkg.MoEGate = ns["MoEGate"]
+    ds_pkg.DeepseekV2MLP = ns["DeepseekV2MLP"]
+    models_pkg.deepseek = ds_pkg
+    sys.modules["models"] = models_pkg
+    sys.modules["models.deepseek"] = ds_pkg
+    nv = types.ModuleType("nvtx")
+    nv.annotate = lambda *a, **k: (lambda f: f)
+    sys.modules.setdefault("nvtx", nv)
+    ex_pkg = types.ModuleType("experts")
+    ex_mod = types.ModuleType("experts.expert_executor")
+    ex_mod.ExpertExecutor = object
+    ex_pkg.expert_executor = ex_mod
+    sys.modules["experts"] = ex_pkg
+    sys.modules["experts.expert_executor"] = ex_mod
+    spec = importlib.util.spec_from_file_location("ref_deepseek_block", os.path.join(ref, "customized", "deepseek.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+QWEN_SMALL = syn.LayerShape(hidden=256, num_experts=8, inter=64, topk=4, kind=0,
+                            shared_inter=128, shared_gate=True)
+DEEPSEEK_SMALL = syn.LayerShape(hidden=256, num_experts=8, inter=64, topk=3, kind=0,
+                                shared_inter=128, shared_gate=False, scaling=1.0)
+
+
+def small_inputs(s: syn.LayerShape, tokens: int):
+    w = syn.expert_weights(s, 1, std=0.05, seed=10)[0]
+    wr, sg = syn.router_weights(s, std=0.05, seed=12)
+    sh = syn.shared_weights(s, std=0.05, seed=14)
+    x = syn.activations(tokens, s.hidden, seed=11)
+    return x, wr, sg, w, sh
+
+
+def qwen_block(ref, tokens=24):
+    from transformers import Qwen2MoeConfig
+    mod = _load_qwen(ref)
+    s = QWEN_SMALL
+    cfg = Qwen2MoeConfig(hidden_size=s.hidden, num_experts=s.num_experts, num_experts_per_tok=s.topk,
+                         moe_intermediate_size=s.inter, shared_expert_intermediate_size=s.shared_inter,
+                         norm_topk_prob=False, hidden_act="silu")
+    blk = mod.Qwen2MoEBlock(cfg).to(torch.bfloat16).eval()
+    x, wr, sg, w, sh = small_inputs(s, tokens)
+    with torch.no_grad():
+        blk.gate.weight.copy_(wr)
+        blk.shared_expert_gate.weight.copy_(sg)
+        for e in range(s.num_experts):
+            blk.experts[e].gate_proj.weight.copy_(w[e][0])
+            blk.experts[e].up_proj.weight.copy_(w[e][1])
+            blk.experts[e].down_proj.weight.copy_(w[e][2])
+        blk.shared_expert.gate_proj.weight.copy_(sh[0])
+        blk.shared_expert.up_proj.weight.copy_(sh[1])
+        blk.shared_expert.down_proj.weight.copy_(sh[2])
+        blk.expert_executor = _CPUExecutor(blk)
+        blk.layer_id = 0
+        y = blk(x.view(1, tokens, s.hidden)).view(tokens, s.hidden)
+        logits = blk.gate(x)
+        rw = torch.softmax(logits, dim=1, dtype=torch.float)
+        tw, ti = torch.topk(rw, s.topk, dim=-1)
+    np.savez_compressed(os.path.join(HERE, "qwen_block.npz"),
+                        out=y.float().numpy(), topk_idx=ti.numpy().astype(np.int32),
+                        topk_w=tw.numpy(), logits=logits.float().numpy(),
+                        input_digest=np.array(digest(x, wr, sg, *w[0], *sh)), tokens=np.array(tokens))
+    print("qwen block:", tuple(y.shape))
+
+
+def deepseek_block(ref, tokens=24):
+    mod = _load_deepseek(ref)
+    s = DEEPSEEK_SMALL
+
+    class Cfg:
+        pass
+
+    cfg = Cfg()
+    cfg.model_type = "deepseek_v2"
+    cfg.num_experts_per_tok = s.topk
+    cfg.n_routed_experts = s.num_experts
+    cfg.routed_scaling_factor = s.scaling
+    cfg.scoring_func = "softmax"
+    cfg.aux_loss_alpha = 0.0
+    cfg.seq_aux = False
+    cfg.topk_method = "greedy"
+    cfg.n_group = 1
+    cfg.topk_group = 1
+    cfg.norm_topk_prob = False
+    cfg.hidden_size = s.hidden
+    cfg.intermediate_size = s.inter
+    cfg.moe_intermediate_size = s.inter
+    cfg.n_shared_experts = s.shared_inter // s.inter
+    cfg.hidden_act = "silu"
+    blk = mod.DeepseekMoEBlock(cfg).to(torch.bfloat16).eval()
+    x, wr, _, w, sh = small_inputs(s, tokens)
+    with torch.no_grad():
+        blk.gate.weight.data = wr.clone()
+        for e in range(s.num_experts):
+            blk.experts[e].gate_proj.weight.copy_(w[e][0])
+            blk.experts[e].up_proj.weight.copy_(w[e][1])
+            blk.experts[e].down_proj.weight.copy_(w[e][2])
+        blk.shared_experts.gate_proj.weight.copy_(sh[0])
+        blk.shared_experts.up_proj.weight.copy_(sh[1])
+        blk.shared_experts.down_proj.weight.copy_(sh[2])
+        blk.expert_executor = _CPUExecutor(blk)
+        blk.layer_id = 0
+        y = blk(x.view(1, tokens, s.hidden)).view(tokens, s.hidden)
+        ti, tw, _ = blk.gate(x.view(1, tokens, s.hidden))
+    np.savez_compressed(os.path.join(HERE, "deepseek_block.npz"),
+                        out=y.float().numpy(), topk_idx=ti.numpy().astype(np.int32), topk_w=tw.float().numpy(),
+                        input_digest=np.array(digest(x, wr, *w[0], *sh)), tokens=np.array(tokens))
+    print("deepseek block:", tuple(y.shape))
+
+
+if __name__ == "__main__":
+    ref = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    codec_cases()
+    qwen_block(ref)
+    deepseek_block(ref)

@@ -1,0 +1,97 @@
+"""Oracle codec pinned against liblz4 (the reference codec library) and the
+committed fixtures."""
+import os
+
+import numpy as np
+import pytest
+
+from oracle import codec
+
+GOLD = os.path.join(os.path.dirname(__file__), "golden", "codec_cases.npz")
+
+
+@pytest.fixture(scope="module")
+def gold():
+    return np.load(GOLD)
+
+
+def _cases(g):
+    for key in g["names"]:
+        key = str(key)
+        tensor = key.split("__")[0]
+        bits = g[tensor + "__bits"]
+        osz = [int(v) for v in g[key + "__osz"]]
+        csz = [int(v) for v in g[key + "__csz"]]
+        raw = g[key + "__blocks"].tobytes()
+        blocks, pos = [], 0
+        for c in csz:
+            blocks.append(raw[pos:pos + c])
+            pos += c
+        yield key, bits, osz, blocks
+
+
+def test_fixture_covers_edge_cases(gold):
+    names = [str(n) for n in gold["names"]]
+    assert any(n.startswith("zeros") for n in names)
+    assert any(n.startswith("tiny_1") for n in names)
+    assert any(n.startswith("random_bits") for n in names)
+    assert any("ragged" in n for n in names)
+
+
+def test_planes_roundtrip(gold):
+    for t in gold["tensors"]:
+        bits = gold[str(t) + "__bits"]
+        exp, sm = codec.split_planes(bits)
+        assert np.array_equal(codec.recombine(exp, sm), bits)
+        assert np.array_equal(codec.recombine_restated(exp, sm), bits)
+
+
+def test_chunk_sizes_follow_reference():
+    exp = np.arange(2883584, dtype=np.uint8)
+    sizes = [c.size for c in codec.chunk_exponents(exp, 3)]
+    assert sizes == [961195, 961195, 961194]
+    assert [c.size for c in codec.chunk_exponents(np.zeros(10, np.uint8), 3)] == [4, 4, 2]
+
+
+def test_restated_decoder_matches_liblz4_on_fixtures(gold):
+    n = 0
+    for key, bits, osz, blocks in _cases(gold):
+        exp, _ = codec.split_planes(bits)
+        parts = []
+        for b, o in zip(blocks, osz):
+            lib = codec.lz4_decompress(b, o)
+            rc, mine = codec.lz4_decompress_restated(b, o)
+            assert rc == o, key
+            assert np.array_equal(lib, mine), key
+            parts.append(mine)
+        assert np.array_equal(np.concatenate(parts), exp), key
+        n += 1
+    assert n == len(gold["names"])
+
+
+def test_fixture_blocks_reproduce_with_this_liblz4(gold):
+    """LZ4HC output can vary across liblz4 versions; parity is on decoded bytes.
+    With the fixture's own version the blocks reproduce byte for byte."""
+    if str(gold["lz4_version"]) != codec.lz4_version():
+        pytest.skip("different liblz4 version")
+    for key, bits, osz, blocks in _cases(gold):
+        cod = key.split("__")[2]
+        chunks = int(key.split("__")[1][1:])
+        again, osz2, _ = codec.encode_tensor(bits, chunks, cod, 9, 5)
+        assert osz2 == osz and again == blocks, key
+
+
+def test_restated_decoder_rejects_malformed():
+    exp = (np.arange(5000) % 7).astype(np.uint8)
+    blk = codec.lz4_compress_hc(exp)
+    rc, _ = codec.lz4_decompress_restated(blk[: len(blk) // 2], exp.size)
+    assert rc < 0 or rc < exp.size
+    bad = bytearray(blk)
+    # first sequence: literals then a zero offset
+    seqs = codec.lz4_sequences(bytes(blk))
+    s0 = seqs[0]
+    off_pos = s0[0] + 1 + s0[2] + (1 if s0[2] >= 15 else 0)
+    bad[off_pos] = 0
+    bad[off_pos + 1] = 0
+    rc, _ = codec.lz4_decompress_restated(bytes(bad), exp.size)
+    assert rc < 0
