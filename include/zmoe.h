@@ -1,0 +1,181 @@
+/*
+ * zmoe.h — C ABI of the B200 (sm_100a) expert hot path of ZipMoE.
+ *
+ * Every entry point takes plain pointers and sizes, works on caller-owned
+ * device memory, is asynchronous on the given stream, and returns a
+ * zmoe_status.  Per-item device status words report data errors (a malformed
+ * LZ4 block, an output overflow) without trapping the GPU.
+ *
+ * Each declaration names the reference interface it replaces (paths are
+ * relative to the reference project root).
+ */
+#ifndef ZMOE_H_
+#define ZMOE_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Binary-compatible with cudaStream_t. */
+typedef struct CUstream_st* zmoe_stream_t;
+
+typedef enum zmoe_status {
+  ZMOE_OK = 0,
+  ZMOE_EINVAL = 1,      /* bad argument (null pointer, unsupported size) */
+  ZMOE_ECUDA = 2,       /* a CUDA runtime call failed */
+  ZMOE_EUNSUPPORTED = 3,/* shape outside what the kernels implement */
+  ZMOE_ENOMEM = 4,
+  ZMOE_ENCCL = 5
+} zmoe_status;
+
+/* Per-chunk decode status written by zmoe_decode_chunks. */
+enum {
+  ZMOE_CHUNK_OK = 0,
+  ZMOE_CHUNK_BAD_OFFSET = 1,     /* zero offset or offset before the chunk start */
+  ZMOE_CHUNK_INPUT_OVERRUN = 2,  /* a length runs past the end of the block */
+  ZMOE_CHUNK_SHORT_OUTPUT = 3,   /* the block ended before out_size bytes */
+  ZMOE_CHUNK_BAD_DESC = 4        /* null pointer or zero-sized block */
+};
+
+/* Version of this ABI. */
+int zmoe_abi_version(void);
+
+/* Human-readable text of the last error recorded on the calling thread. */
+const char* zmoe_last_error(void);
+
+/* --------------------------------------------------------------------------
+ * Plane recombine.
+ * Replaces zipmoe_launch_tensor_recover (csrc/kernels/tensor_recover.hpp:14-20,
+ * kernel csrc/kernels/tensor_recover.cu:12-43):
+ *   out[i] = (sm[i] >> 7) << 15 | exp[i] << 7 | (sm[i] & 0x7F)
+ * n is a 64-bit count (the reference kernel takes a 32-bit int).
+ * ------------------------------------------------------------------------ */
+zmoe_status zmoe_tensor_recover(uint16_t* out, const uint8_t* exp, const uint8_t* sm,
+                                size_t n, zmoe_stream_t stream);
+
+/* --------------------------------------------------------------------------
+ * Fused LZ4-block decode + recombine.
+ * Replaces, per exponent chunk, LZ4_decompress_safe_partial(src, dst, csize,
+ * osize, osize) in LZ4compressor/LZ4HCcompressor::decompress
+ * (csrc/tensor_engine/compressors.cpp:133-149,195-211) as driven by
+ * TensorEngine::io_decompress_mov_submit (csrc/tensor_engine/tensor_engine.cpp:421-474),
+ * followed by the recombine launch of SetModuleMemoryFromDiskGrouped
+ * (csrc/topology/model_topology.cpp:574-580).  The decoded exponent bytes never
+ * leave the SM: each one is merged with its sign+mantissa byte and written as
+ * BF16 straight into the destination slot.
+ * ------------------------------------------------------------------------ */
+typedef struct zmoe_chunk {
+  const uint8_t* src;   /* LZ4 block, device memory */
+  const uint8_t* sm;    /* sign+mantissa bytes of this chunk's elements */
+  uint16_t* dst;        /* BF16 output of this chunk's elements */
+  uint32_t src_size;    /* compressed bytes */
+  uint32_t out_size;    /* exponent bytes = elements (original_sizes[c]) */
+} zmoe_chunk;
+
+/* chunks and status are device arrays of n_chunks entries. */
+zmoe_status zmoe_decode_chunks(const zmoe_chunk* chunks, int n_chunks, int32_t* status,
+                               zmoe_stream_t stream);
+
+/* --------------------------------------------------------------------------
+ * Router: logits, softmax and top-k of one MoE layer.
+ * Replaces Qwen2MoEBlock.__prepare_expert_route (customized/qwen.py:44-54),
+ * MoEGate.forward greedy branch (models/deepseek/modeling_deepseek.py:424-476)
+ * and the transformers<4.47 SwitchTransformersTop1Router used by
+ * customized/switch_transformers.py:72-73.
+ * Logits accumulate in fp32 in a fixed order (lane l of 32 sums h = 256j+8l+i,
+ * xor-butterfly fold); ties in top-k go to the lower expert index.
+ * ------------------------------------------------------------------------ */
+enum { ZMOE_ROUTE_QWEN = 0, ZMOE_ROUTE_DEEPSEEK = 1, ZMOE_ROUTE_SWITCH = 2 };
+
+typedef struct zmoe_router_args {
+  const uint16_t* x;          /* [T, H] BF16 */
+  const uint16_t* w;          /* [E, H] BF16 router weight */
+  const float* bias;          /* [E] fp32 logit bias or NULL */
+  const uint16_t* w_shared_gate; /* [H] BF16 (Qwen shared-expert gate) or NULL */
+  int T, H, E, k;
+  int mode;                   /* ZMOE_ROUTE_* */
+  int norm_topk_prob;         /* Qwen/DeepSeek renormalisation flag */
+  float scaling;              /* DeepSeek routed_scaling_factor */
+  float* logits;              /* [T, E] fp32 out (may be NULL) */
+  int32_t* topk_idx;          /* [T, k] out */
+  float* topk_w;              /* [T, k] out combine weights */
+  float* shared_gate;         /* [T] out sigmoid gate, when w_shared_gate != NULL */
+} zmoe_router_args;
+
+zmoe_status zmoe_router(const zmoe_router_args* a, zmoe_stream_t stream);
+
+/* --------------------------------------------------------------------------
+ * Permute: group the routed (token, slot) pairs by expert, tokens ascending
+ * inside an expert, and gather the activation rows.
+ * Replaces the boolean-mask gather hidden_states_.index({token_indices}) of
+ * ExpertDispatcher::GPUFetchFunc (csrc/dispatcher/expert_dispatcher.cpp:326-330)
+ * and the per-expert counts of ExpertExecutor.dispatch_local
+ * (experts/expert_executor.py:45-49).  For Switch (capacity > 0) a token is
+ * dropped when its expert already has `capacity` earlier tokens in the same
+ * sequence of length seq_len (the cumsum mask of the Top1 router).
+ * ------------------------------------------------------------------------ */
+typedef struct zmoe_permute_args {
+  int32_t* topk_idx;          /* [T, k] in; dropped entries are set to -1 */
+  const uint16_t* x;          /* [T, H] BF16 */
+  int T, H, E, k;
+  int capacity, seq_len;      /* capacity 0 = unlimited */
+  int32_t* counts;            /* [E] out tokens per expert */
+  int32_t* offsets;           /* [E + 1] out exclusive prefix */
+  int32_t* row_of;            /* [T, k] out permuted row or -1 */
+  int32_t* token_of_row;      /* [T * k] out */
+  uint16_t* xp;               /* [T * k, H] out gathered rows */
+} zmoe_permute_args;
+
+zmoe_status zmoe_permute(const zmoe_permute_args* a, zmoe_stream_t stream);
+
+/* --------------------------------------------------------------------------
+ * Grouped expert FFN over the permuted rows.
+ * Replaces DeepSeekMoEDenseActDense::forward (csrc/dispatcher/expert_module.cpp:39-50)
+ * and SwitchTransformersDenseActDense::forward (:67-78) run one expert at a
+ * time by ExpertDispatcher::GPUExecFunc (expert_dispatcher.cpp:354-427).
+ * kind 0: y = bf16(silu(x Wg^T) * (x Wu^T)) Wd^T ; kind 1: y = bf16(relu(x Wi^T)) Wo^T.
+ * w[g*3 + {0,1,2}] are the device pointers of group g's matrices (row-major
+ * [I, H], [I, H], [H, I]; for kind 1 w[g*3+0] = wi [I, H], w[g*3+2] = wo [H, I]).
+ * Rows of group g are offsets[g] .. offsets[g+1] of x; NULL offsets means one
+ * group of rows_total rows.  y is fp32 [rows, H]; h is BF16 scratch [rows, I].
+ * ------------------------------------------------------------------------ */
+typedef struct zmoe_ffn_args {
+  const uint16_t* x;          /* [rows, H] BF16 */
+  const uint16_t* const* w;   /* device array [G * 3] of weight pointers */
+  const int32_t* offsets;     /* [G + 1] device or NULL */
+  int G, rows_total, H, I, kind;
+  uint16_t* h;                /* [rows, I] BF16 scratch */
+  float* y;                   /* [rows, H] fp32 out */
+} zmoe_ffn_args;
+
+zmoe_status zmoe_expert_ffn(const zmoe_ffn_args* a, zmoe_stream_t stream);
+
+/* --------------------------------------------------------------------------
+ * Combine: gate-weighted sum of the expert rows plus the shared expert.
+ * Replaces the Python combine loops customized/qwen.py:89-100,
+ * customized/deepseek.py:103-115 and customized/switch_transformers.py:83-87.
+ * mode QWEN/DEEPSEEK: out[t] = sum_j w[t,j] y[row_of[t,j]] + g[t] * ysh[t]
+ *   (g = shared_gate[t], or 1 when shared_gate is NULL; no ysh term when NULL).
+ * mode SWITCH: out[t] = w[t,0] * (row_of[t,0] >= 0 ? y[row_of[t,0]] : x[t]).
+ * fp32 accumulation, one BF16 rounding.
+ * ------------------------------------------------------------------------ */
+typedef struct zmoe_combine_args {
+  const float* y;             /* [rows, H] */
+  const float* y_shared;      /* [T, H] or NULL */
+  const float* shared_gate;   /* [T] or NULL */
+  const int32_t* row_of;      /* [T, k] */
+  const float* topk_w;        /* [T, k] */
+  const uint16_t* x;          /* [T, H] (Switch pass-through) */
+  int T, H, k, mode;
+  uint16_t* out;              /* [T, H] BF16 */
+} zmoe_combine_args;
+
+zmoe_status zmoe_combine(const zmoe_combine_args* a, zmoe_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* ZMOE_H_ */

@@ -1,0 +1,61 @@
+// extern "C" entry points of libzmoe.so (declared in include/zmoe.h).
+#include <stdarg.h>
+
+#include "common.cuh"
+
+namespace zmoe {
+
+static thread_local char g_err[512] = "";
+
+void set_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+}
+
+zmoe_status launch_tensor_recover(uint16_t*, const uint8_t*, const uint8_t*, size_t, cudaStream_t);
+zmoe_status launch_decode_chunks(const zmoe_chunk*, int, int32_t*, cudaStream_t);
+zmoe_status launch_router(const zmoe_router_args*, cudaStream_t);
+zmoe_status launch_permute(const zmoe_permute_args*, cudaStream_t);
+zmoe_status launch_combine(const zmoe_combine_args*, cudaStream_t);
+zmoe_status launch_expert_ffn_simt(const zmoe_ffn_args*, cudaStream_t);
+
+}  // namespace zmoe
+
+extern "C" {
+
+int zmoe_abi_version(void) { return 1; }
+
+const char* zmoe_last_error(void) { return zmoe::g_err; }
+
+zmoe_status zmoe_tensor_recover(uint16_t* out, const uint8_t* exp, const uint8_t* sm, size_t n,
+                                zmoe_stream_t stream) {
+  ZMOE_CHECK_ARG(n == 0 || (out && exp && sm), "tensor_recover: null pointer");
+  return zmoe::launch_tensor_recover(out, exp, sm, n, reinterpret_cast<cudaStream_t>(stream));
+}
+
+zmoe_status zmoe_decode_chunks(const zmoe_chunk* chunks, int n_chunks, int32_t* status,
+                               zmoe_stream_t stream) {
+  ZMOE_CHECK_ARG(n_chunks >= 0, "decode_chunks: negative count");
+  ZMOE_CHECK_ARG(n_chunks == 0 || (chunks && status), "decode_chunks: null pointer");
+  return zmoe::launch_decode_chunks(chunks, n_chunks, status, reinterpret_cast<cudaStream_t>(stream));
+}
+
+zmoe_status zmoe_router(const zmoe_router_args* a, zmoe_stream_t stream) {
+  return zmoe::launch_router(a, reinterpret_cast<cudaStream_t>(stream));
+}
+
+zmoe_status zmoe_permute(const zmoe_permute_args* a, zmoe_stream_t stream) {
+  return zmoe::launch_permute(a, reinterpret_cast<cudaStream_t>(stream));
+}
+
+zmoe_status zmoe_expert_ffn(const zmoe_ffn_args* a, zmoe_stream_t stream) {
+  return zmoe::launch_expert_ffn_simt(a, reinterpret_cast<cudaStream_t>(stream));
+}
+
+zmoe_status zmoe_combine(const zmoe_combine_args* a, zmoe_stream_t stream) {
+  return zmoe::launch_combine(a, reinterpret_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,85 @@
+"""ctypes binding of libzmoe.so (the C ABI declared in include/zmoe.h).
+
+The library is built in place by ``make`` in the package directory.  There is
+no fallback: if the library is missing, importing this module raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+PKG_DIR = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+LIB_PATH = os.path.join(PKG_DIR, "libzmoe.so")
+
+c_void_p = ctypes.c_void_p
+c_int = ctypes.c_int
+c_u32 = ctypes.c_uint32
+c_size_t = ctypes.c_size_t
+c_float = ctypes.c_float
+
+
+class ZmoeChunk(ctypes.Structure):
+    _fields_ = [("src", c_void_p), ("sm", c_void_p), ("dst", c_void_p),
+                ("src_size", c_u32), ("out_size", c_u32)]
+
+
+class RouterArgs(ctypes.Structure):
+    _fields_ = [("x", c_void_p), ("w", c_void_p), ("bias", c_void_p), ("w_shared_gate", c_void_p),
+                ("T", c_int), ("H", c_int), ("E", c_int), ("k", c_int), ("mode", c_int),
+                ("norm_topk_prob", c_int), ("scaling", c_float),
+                ("logits", c_void_p), ("topk_idx", c_void_p), ("topk_w", c_void_p), ("shared_gate", c_void_p)]
+
+
+class PermuteArgs(ctypes.Structure):
+    _fields_ = [("topk_idx", c_void_p), ("x", c_void_p), ("T", c_int), ("H", c_int), ("E", c_int),
+                ("k", c_int), ("capacity", c_int), ("seq_len", c_int), ("counts", c_void_p),
+                ("offsets", c_void_p), ("row_of", c_void_p), ("token_of_row", c_void_p), ("xp", c_void_p)]
+
+
+class FfnArgs(ctypes.Structure):
+    _fields_ = [("x", c_void_p), ("w", c_void_p), ("offsets", c_void_p), ("G", c_int),
+                ("rows_total", c_int), ("H", c_int), ("I", c_int), ("kind", c_int),
+                ("h", c_void_p), ("y", c_void_p)]
+
+
+class CombineArgs(ctypes.Structure):
+    _fields_ = [("y", c_void_p), ("y_shared", c_void_p), ("shared_gate", c_void_p), ("row_of", c_void_p),
+                ("topk_w", c_void_p), ("x", c_void_p), ("T", c_int), ("H", c_int), ("k", c_int),
+                ("mode", c_int), ("out", c_void_p)]
+
+
+# (name, restype, argtypes) of every exported symbol; tests check the header
+# declares exactly these.
+SIGNATURES = {
+    "zmoe_abi_version": (c_int, []),
+    "zmoe_last_error": (ctypes.c_char_p, []),
+    "zmoe_tensor_recover": (c_int, [c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
+    "zmoe_decode_chunks": (c_int, [c_void_p, c_int, c_void_p, c_void_p]),
+    "zmoe_router": (c_int, [ctypes.POINTER(RouterArgs), c_void_p]),
+    "zmoe_permute": (c_int, [ctypes.POINTER(PermuteArgs), c_void_p]),
+    "zmoe_expert_ffn": (c_int, [ctypes.POINTER(FfnArgs), c_void_p]),
+    "zmoe_combine": (c_int, [ctypes.POINTER(CombineArgs), c_void_p]),
+}
+
+
+class ZmoeError(RuntimeError):
+    pass
+
+
+def _load():
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(f"libzmoe.so not built ({LIB_PATH}); run `make` in {PKG_DIR}")
+    lib = ctypes.CDLL(LIB_PATH)
+    for name, (res, args) in SIGNATURES.items():
+        f = getattr(lib, name)
+        f.restype = res
+        f.argtypes = args
+    return lib
+
+
+lib = _load()
+
+
+def check(status: int, what: str):
+    if status != 0:
+        raise ZmoeError(f"{what}: status {status}: {lib.zmoe_last_error().decode(errors='replace')}")

@@ -1,0 +1,175 @@
+"""Torch-facing wrappers over the C ABI (device tensors in, device tensors out).
+
+Every call runs on torch's current CUDA stream and raises ``ZmoeError`` with
+the library's message on a non-zero status.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import List, Optional, Sequence, Tuple
+
+import torch
+
+from . import _lib
+from ._lib import CombineArgs, FfnArgs, PermuteArgs, RouterArgs, ZmoeChunk, check, lib
+
+ROUTE_QWEN, ROUTE_DEEPSEEK, ROUTE_SWITCH = 0, 1, 2
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _need(t: torch.Tensor, dtype, name: str):
+    if not t.is_cuda or t.dtype != dtype or not t.is_contiguous():
+        raise ValueError(f"{name}: expected a contiguous CUDA {dtype} tensor, got {t.dtype} on {t.device}")
+
+
+# ---------------------------------------------------------------------------
+# codec
+# ---------------------------------------------------------------------------
+def tensor_recover(exp: torch.Tensor, sm: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """BF16 bits from the exponent and sign+mantissa planes (uint8 -> int16 view)."""
+    _need(exp, torch.uint8, "exp")
+    _need(sm, torch.uint8, "sm")
+    if exp.numel() != sm.numel():
+        raise ValueError("plane sizes differ")
+    if out is None:
+        out = torch.empty(exp.numel(), dtype=torch.bfloat16, device=exp.device)
+    check(lib.zmoe_tensor_recover(out.data_ptr(), exp.data_ptr(), sm.data_ptr(), exp.numel(), _stream()),
+          "zmoe_tensor_recover")
+    return out
+
+
+def chunk_table(descs: Sequence[Tuple[int, int, int, int, int]], device) -> torch.Tensor:
+    """Pack (src, sm, dst, src_size, out_size) tuples into a device descriptor array."""
+    arr = (ZmoeChunk * max(len(descs), 1))()
+    for i, (src, sm, dst, csz, osz) in enumerate(descs):
+        arr[i] = ZmoeChunk(src, sm, dst, csz, osz)
+    raw = torch.frombuffer(bytearray(bytes(arr)), dtype=torch.uint8)[: 32 * len(descs)]
+    return raw.to(device)
+
+
+def decode_chunks(table: torch.Tensor, n: int, status: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Launch the fused decoder on a device descriptor table; returns int32 status[n]."""
+    if status is None:
+        status = torch.full((max(n, 1),), -1, dtype=torch.int32, device=table.device)
+    check(lib.zmoe_decode_chunks(table.data_ptr(), n, status.data_ptr(), _stream()), "zmoe_decode_chunks")
+    return status[:n]
+
+
+class CompressedTensor:
+    """One expert matrix in HBM in the reference's storage form: LZ4 exponent
+    chunks (concatenated, 16-byte aligned) and the raw sign+mantissa plane."""
+
+    def __init__(self, blocks: Sequence[bytes], original_sizes: Sequence[int], sm: bytes, device="cuda"):
+        self.original_sizes = [int(o) for o in original_sizes]
+        self.compressed_sizes = [len(b) for b in blocks]
+        self.numel = sum(self.original_sizes)
+        offs, pos = [], 0
+        for b in blocks:
+            offs.append(pos)
+            pos += (len(b) + 15) // 16 * 16
+        buf = bytearray(max(pos, 16))
+        for o, b in zip(offs, blocks):
+            buf[o:o + len(b)] = b
+        self.block_offsets = offs
+        self.blocks = torch.frombuffer(buf, dtype=torch.uint8).to(device)
+        self.sm = torch.frombuffer(bytearray(sm), dtype=torch.uint8).to(device)
+
+    @property
+    def device_bytes(self) -> int:
+        return self.blocks.numel() + self.sm.numel()
+
+    def descs(self, dst: torch.Tensor) -> List[Tuple[int, int, int, int, int]]:
+        out, e0 = [], 0
+        for o, c, n in zip(self.block_offsets, self.compressed_sizes, self.original_sizes):
+            out.append((self.blocks.data_ptr() + o, self.sm.data_ptr() + e0, dst.data_ptr() + 2 * e0, c, n))
+            e0 += n
+        return out
+
+    def decode(self, dst: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+        if dst is None:
+            dst = torch.empty(self.numel, dtype=torch.bfloat16, device=self.blocks.device)
+        d = self.descs(dst)
+        table = chunk_table(d, dst.device)
+        st = decode_chunks(table, len(d))
+        return dst, st
+
+
+# ---------------------------------------------------------------------------
+# layer primitives
+# ---------------------------------------------------------------------------
+def router(x: torch.Tensor, w: torch.Tensor, k: int, mode: int, bias: Optional[torch.Tensor] = None,
+           w_shared_gate: Optional[torch.Tensor] = None, scaling: float = 1.0, norm_topk_prob: bool = False,
+           want_logits: bool = True):
+    _need(x, torch.bfloat16, "x")
+    _need(w, torch.bfloat16, "w")
+    T, H = x.shape
+    E = w.shape[0]
+    dev = x.device
+    logits = torch.empty(T, E, dtype=torch.float32, device=dev) if want_logits else None
+    idx = torch.empty(T, k, dtype=torch.int32, device=dev)
+    tw = torch.empty(T, k, dtype=torch.float32, device=dev)
+    sg = torch.empty(T, dtype=torch.float32, device=dev) if w_shared_gate is not None else None
+    if bias is not None:
+        _need(bias, torch.float32, "bias")
+    a = RouterArgs(x.data_ptr(), w.data_ptr(), _ptr(bias), _ptr(w_shared_gate), T, H, E, k, mode,
+                   int(norm_topk_prob), scaling, _ptr(logits), idx.data_ptr(), tw.data_ptr(), _ptr(sg))
+    check(lib.zmoe_router(ctypes.byref(a), _stream()), "zmoe_router")
+    return logits, idx, tw, sg
+
+
+def permute(topk_idx: torch.Tensor, x: Optional[torch.Tensor], E: int, capacity: int = 0, seq_len: int = 0):
+    """Returns counts, offsets, row_of, token_of_row, xp.  topk_idx is updated
+    in place (-1 for capacity drops)."""
+    _need(topk_idx, torch.int32, "topk_idx")
+    T, k = topk_idx.shape
+    dev = topk_idx.device
+    H = x.shape[1] if x is not None else 0
+    counts = torch.empty(E, dtype=torch.int32, device=dev)
+    offsets = torch.empty(E + 1, dtype=torch.int32, device=dev)
+    row_of = torch.empty(T, k, dtype=torch.int32, device=dev)
+    tor = torch.empty(max(T * k, 1), dtype=torch.int32, device=dev)
+    xp = torch.empty(max(T * k, 1), H, dtype=torch.bfloat16, device=dev) if x is not None else None
+    a = PermuteArgs(topk_idx.data_ptr(), _ptr(x), T, H, E, k, capacity, seq_len, counts.data_ptr(),
+                    offsets.data_ptr(), row_of.data_ptr(), tor.data_ptr(), _ptr(xp))
+    check(lib.zmoe_permute(ctypes.byref(a), _stream()), "zmoe_permute")
+    return counts, offsets, row_of, tor, xp
+
+
+def weight_table(mats: Sequence[Sequence[Optional[torch.Tensor]]], device) -> torch.Tensor:
+    """Device array [G*3] of weight pointers from per-group (w0, w1, w2)."""
+    ptrs = []
+    for g in mats:
+        g = list(g) + [None] * (3 - len(g))
+        ptrs.extend(0 if t is None else t.data_ptr() for t in g)
+    return torch.tensor(ptrs, dtype=torch.int64, device=device)
+
+
+def expert_ffn(x: torch.Tensor, wtab: torch.Tensor, offsets: Optional[torch.Tensor], G: int, I: int, kind: int,
+               rows_total: Optional[int] = None):
+    _need(x, torch.bfloat16, "x")
+    rows = x.shape[0] if rows_total is None else rows_total
+    H = x.shape[1]
+    h = torch.empty(max(rows, 1), I, dtype=torch.bfloat16, device=x.device)
+    y = torch.empty(max(rows, 1), H, dtype=torch.float32, device=x.device)
+    a = FfnArgs(x.data_ptr(), wtab.data_ptr(), _ptr(offsets), G, rows, H, I, kind, h.data_ptr(), y.data_ptr())
+    check(lib.zmoe_expert_ffn(ctypes.byref(a), _stream()), "zmoe_expert_ffn")
+    return y, h
+
+
+def combine(y: torch.Tensor, row_of: torch.Tensor, topk_w: torch.Tensor, mode: int,
+            y_shared: Optional[torch.Tensor] = None, shared_gate: Optional[torch.Tensor] = None,
+            x: Optional[torch.Tensor] = None, H: Optional[int] = None) -> torch.Tensor:
+    T, k = row_of.shape
+    H = y.shape[1] if H is None else H
+    out = torch.empty(T, H, dtype=torch.bfloat16, device=y.device)
+    a = CombineArgs(y.data_ptr(), _ptr(y_shared), _ptr(shared_gate), row_of.data_ptr(), topk_w.data_ptr(),
+                    _ptr(x), T, H, k, mode, out.data_ptr())
+    check(lib.zmoe_combine(ctypes.byref(a), _stream()), "zmoe_combine")
+    return out
