@@ -1,0 +1,320 @@
+#!/usr/bin/env python
+"""Benchmark: Qwen1.5-MoE-A2.7B-shaped MoE layer with exponent-compressed
+experts on B200.
+
+Workload (one step = one layer forward over one 512-token batch): hidden 2048,
+60 routed SwiGLU experts (intermediate 1408), softmax top-4 without
+renormalisation, a shared SwiGLU expert (intermediate 5632) with a sigmoid
+gate.  Router weights N(0, 0.02) plus a per-expert logit bias giving Zipf(1.0)
+expert popularity.  Every routed expert is stored as LZ4HC-9 exponent chunks
+(3 per matrix) + raw sign+mantissa plane in HBM; 16 decoded experts are cached
+(the 16 most popular are decoded before timing); every other activated expert
+is decoded on the GPU inside the step.  Seeded synthetic data (no checkpoint):
+weights N(0, 0.02) BF16, activations N(0, 1) BF16.
+
+Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+Under torchrun (N > 1) every rank runs its own replica of the layer on its
+own 512 tokens (weak scaling; the layer has no exchange step in this mode).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "zipmoe-icml26_b200")
+for _p in (ROOT, PKG):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import torch  # noqa: E402
+
+METRIC = "MoE-layer tokens/s"
+UNIT = "tokens/s"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--tokens", type=int, default=512)
+    ap.add_argument("--cache", type=int, default=16)
+    ap.add_argument("--chunks", type=int, default=3)
+    ap.add_argument("--codec", default="LZ4HC")
+    ap.add_argument("--level", type=int, default=9)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d.get("hbm_gbs", 6650.0), d.get("bf16_tflops", 1590.0), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.p = None
+
+    def __enter__(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                                       "--format=csv,noheader,nounits", "-lms", "200"],
+                                      stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+        return self
+
+    def __exit__(self, *a):
+        if self.p is not None:
+            self.p.terminate()
+            try:
+                self.p.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.p.kill()
+
+    def summary(self):
+        self.f.flush()
+        rows = []
+        for line in open(self.f.name):
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), parts[5:9]))
+            except ValueError:
+                continue
+        os.unlink(self.f.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for _, _, r in rows for i, v in enumerate(r) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": reasons, "samples": len(rows)}
+
+
+def build_workload(args, device_index=0, threads=0):
+    from zmoe import synthetic as syn
+    from zmoe.layer import MoELayer
+    s = syn.QWEN
+    w = syn.expert_weights(s, 1)[0]
+    wr, sg = syn.router_weights(s)
+    sh = syn.shared_weights(s)
+    bias = syn.zipf_bias(s, 0)
+    L = MoELayer(s, max_tokens=args.tokens, cache_slots=args.cache, device=device_index)
+    L.set_router(wr, bias, sg)
+    L.set_shared(*sh)
+    enc = L.load_experts(w, num_file_chunks=args.chunks, codec=args.codec, level=args.level, threads=threads)
+    warm = syn.popularity_order(s, 0)[: args.cache]
+    L.warm_cache(warm)
+    return s, L, enc, (wr, bias, sg, sh, warm)
+
+
+def cpu_reference_layer(s, enc, extra, threads):
+    from oracle.reference_cpu import ReferenceCPULayer
+    wr, bias, sg, sh, warm = extra
+    shapes = [(s.inter, s.hidden), (s.inter, s.hidden), (s.hidden, s.inter)]
+    return ReferenceCPULayer(shapes, enc, wr, bias, sg, sh, s.topk, warm, threads=threads)
+
+
+def run_reference(args):
+    """CPU reference path (oracle port) on the host cores; prints the reference line."""
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return
+    from zmoe import synthetic as syn
+    from zmoe import codec as zc
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    s = syn.QWEN
+    w = syn.expert_weights(s, 1)[0]
+    wr, sg = syn.router_weights(s)
+    sh = syn.shared_weights(s)
+    bias = syn.zipf_bias(s, 0)
+    flat = zc.encode_tensors([t for e in w for t in e], args.chunks, args.codec, args.level, threads)
+    enc = [flat[i * 3:(i + 1) * 3] for i in range(s.num_experts)]
+    warm = syn.popularity_order(s, 0)[: args.cache]
+    L = cpu_reference_layer(s, enc, (wr, bias, sg, sh, warm), threads)
+    x = syn.activations(args.tokens, s.hidden)
+    for _ in range(args.warmup):
+        L.forward(x)
+    t0 = time.perf_counter()
+    st = None
+    for _ in range(args.steps):
+        _, st = L.forward(x)
+    dt = (time.perf_counter() - t0) / max(args.steps, 1)
+    L.close()
+    v = args.tokens / dt
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "qwen1.5-moe-layer", "tokens": args.tokens, "hidden": s.hidden,
+                       "experts": s.num_experts, "topk": s.topk, "cached_experts": args.cache,
+                       "codec": f"{args.codec}-{args.level}", "num_file_chunks": args.chunks},
+            "cpu_baseline": {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
+                             "sample": f"{args.steps} full {args.tokens}-token layer steps: liblz4 decode of "
+                                       f"{st['misses']} missed experts on {threads} threads + torch CPU BF16 layer"},
+            "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args):
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+    threads = max(1, (os.cpu_count() or 1) // max(world, 1))
+    s, L, enc, extra = build_workload(args, local, threads)
+    from zmoe import synthetic as syn
+    x = syn.activations(args.tokens, s.hidden, seed=1 + rank).cuda()
+    out = torch.empty_like(x)
+    stream = torch.cuda.current_stream()
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        L.forward(x, out)
+    L.sync()
+    L.reset_stats()
+    L.set_timing(True)
+    barrier()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        start.record(stream)
+        for _ in range(args.steps):
+            L.forward(x, out)
+        stop.record(stream)
+        torch.cuda.synchronize()
+    L.sync()
+    barrier()
+    ms = start.elapsed_time(stop) / args.steps
+    st = L.stats()
+    L.set_timing(False)
+
+    # end to end through the public API with pinned host buffers
+    xh = x.cpu().pin_memory()
+    oh = torch.empty_like(xh).pin_memory()
+    for _ in range(2):
+        L.forward_host(xh, oh)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        L.forward_host(xh, oh)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+
+    t = torch.tensor([ms, e2e_ms], dtype=torch.float64, device="cuda")
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, e2e_ms = float(t[0]), float(t[1])
+    clocks = clk.summary()
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(args, s, enc, extra)
+    if rank == 0:
+        hbm, tfl, src = peaks()
+        dec_s = st["decode_ns"] * 1e-9
+        launches = max(st["decode_timed_launches"], 1)
+        achieved = (st["decode_timed_bytes"] / launches) / (dec_s / launches) / 1e9 if dec_s > 0 else 0.0
+        traffic = None
+        tp = os.path.join(ROOT, "profiles", "decode_traffic.json")
+        if os.path.exists(tp):
+            traffic = json.load(open(tp)).get("bytes_per_launch")
+        line = {
+            "metric": METRIC, "value": world * args.tokens / (ms / 1e3), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations)",
+            "config": {"workload": "qwen1.5-moe-layer", "tokens_per_gpu": args.tokens, "hidden": s.hidden,
+                       "experts": s.num_experts, "inter": s.inter, "topk": s.topk, "shared_inter": s.shared_inter,
+                       "cached_experts": args.cache, "codec": f"{args.codec}-{args.level}",
+                       "num_file_chunks": args.chunks, "zipf_s": s.zipf_s,
+                       "parallelism": "replicas" if world > 1 else "single",
+                       "l2": "inputs larger than L2 (decoded + compressed experts > 1 GB)"},
+            "e2e": {"value": world * args.tokens / (e2e_ms / 1e3), "unit": UNIT,
+                    "h2d_bytes_per_step": x.numel() * 2, "d2h_bytes_per_step": x.numel() * 2},
+            "roofline": {"bound": "hbm", "kernel": "decode_warp_kernel", "achieved": achieved, "peak": hbm,
+                         "unit": "GB/s", "frac": achieved / hbm, "peak_source": src, "traffic": traffic,
+                         "algorithmic_bytes_per_launch": st["decode_timed_bytes"] / launches,
+                         "kernel_ms_per_launch": dec_s * 1e3 / launches},
+            "decode": {"experts_per_step": st["decoded_experts"] / args.steps,
+                       "gb_per_s": achieved, "share_of_step": dec_s / (ms * 1e-3 * args.steps)},
+            "ffn_ms_per_step": st["ffn_ns"] * 1e-6 / args.steps,
+            "cache": {"hits": st["hits"], "misses": st["misses"], "evictions": st["evictions"]},
+            "gpu_launches": st["launches"],
+            "clocks": clocks,
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    L.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def cpu_baseline(args, s, enc, extra):
+    from zmoe import synthetic as syn
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    enc_py = enc
+    L = cpu_reference_layer(s, enc_py, extra, threads)
+    x = syn.activations(args.tokens, s.hidden, seed=1)
+    L.forward(x)
+    n, t0 = 0, time.perf_counter()
+    st = None
+    while n < 3 and time.perf_counter() - t0 < 20:
+        _, st = L.forward(x)
+        n += 1
+    dt = (time.perf_counter() - t0) / n
+    L.close()
+    return {"value": args.tokens / dt, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{n} full {args.tokens}-token layer steps ({st['misses']} misses decoded by liblz4 on "
+                      f"{threads} threads, torch CPU BF16 experts)"}
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -175,6 +175,89 @@ typedef struct zmoe_combine_args {
 
 zmoe_status zmoe_combine(const zmoe_combine_args* a, zmoe_stream_t stream);
 
+/* --------------------------------------------------------------------------
+ * Offload-side codec (host).
+ * zmoe_split_planes replaces split_and_extract_from_tensor
+ * (runtime/model_offload.py:706-726); zmoe_lz4_compress replaces
+ * LZ4HCcompressor::compress / LZ4compressor::compress
+ * (csrc/tensor_engine/compressors.cpp:105-122, :167-185) and returns the block
+ * size, or a value <= 0 on failure.
+ * ------------------------------------------------------------------------ */
+enum { ZMOE_CODEC_LZ4 = 0, ZMOE_CODEC_LZ4HC = 1 };
+
+zmoe_status zmoe_split_planes(const uint16_t* bits, uint64_t n, uint8_t* exp, uint8_t* sm);
+int zmoe_lz4_compress_bound(int n);
+int zmoe_lz4_compress(const uint8_t* src, int n, uint8_t* dst, int capacity, int codec, int level);
+
+/* --------------------------------------------------------------------------
+ * MoE-layer engine (opaque handle).
+ * Re-targets, for one layer, the reference's runtime around the hot path:
+ * ZipMoEPrefetchHandle's stores and pools (csrc/prefetch/zipmoe_prefetch_handle.cpp:33-108),
+ * ZipMoECacheHandle::ProactiveDecision and its slot policies
+ * (csrc/memory/cache.cpp:226-270, :445-690), TensorEngine::ToWorkers /
+ * ZipMoESchedulerFunc (csrc/tensor_engine/tensor_engine.cpp:515-669) and the
+ * ExpertDispatcher fetch/exec/output loop (csrc/dispatcher/expert_dispatcher.cpp:285-515).
+ * Compressed experts stay resident in HBM in the reference's storage form
+ * (LZ4 exponent chunks + raw sign+mantissa plane); cache_slots decoded experts
+ * stay resident; misses are decoded by zmoe_decode_chunks into cache slots
+ * (NORMAL) or transient slots (EVICT) before the grouped FFN runs.
+ * ------------------------------------------------------------------------ */
+typedef struct zmoe_layer zmoe_layer;
+
+enum { ZMOE_CACHE_ZIPMOE = 0, ZMOE_CACHE_LFU = 1, ZMOE_CACHE_LRU = 2, ZMOE_CACHE_FIFO = 3 };
+
+typedef struct zmoe_layer_config {
+  int hidden, num_experts, inter, topk;
+  int kind;                   /* 0 SwiGLU (Qwen/DeepSeek), 1 ReLU (Switch) */
+  int route_mode;             /* ZMOE_ROUTE_* */
+  int norm_topk_prob;
+  float scaling;              /* DeepSeek routed_scaling_factor */
+  int shared_inter;           /* shared-expert intermediate size, 0 = none */
+  int capacity, seq_len;      /* Switch capacity per sequence of seq_len tokens */
+  int max_tokens;             /* workspace is sized for this many tokens */
+  int cache_slots;            /* decoded experts kept resident */
+  int transient_slots;        /* decode slots for misses; 0 = num_experts - cache_slots */
+  int cache_policy;           /* ZMOE_CACHE_* victim selection */
+  double state_margin;        /* hyperparam_state_margin of the NORMAL threshold */
+} zmoe_layer_config;
+
+typedef struct zmoe_layer_stats {
+  uint64_t forwards, tokens, hits, misses, evictions;
+  uint64_t decoded_experts, decoded_chunks, decoded_bytes, decode_launches;
+  uint64_t launches, decode_errors, store_bytes;
+  /* filled when timing is on: CUDA-event durations on the launch stream */
+  uint64_t decode_ns, decode_timed_bytes, decode_timed_launches, ffn_ns, ffn_timed_launches;
+} zmoe_layer_stats;
+
+zmoe_status zmoe_layer_create(const zmoe_layer_config* cfg, zmoe_layer** out);
+zmoe_status zmoe_layer_destroy(zmoe_layer* layer);
+/* Host pointers; copied to HBM.  bias ([E] fp32) and w_shared_gate ([H] BF16) may be NULL. */
+zmoe_status zmoe_layer_set_router(zmoe_layer* layer, const uint16_t* w_router, const float* bias,
+                                  const uint16_t* w_shared_gate);
+zmoe_status zmoe_layer_set_shared(zmoe_layer* layer, const uint16_t* gate, const uint16_t* up,
+                                  const uint16_t* down);
+/* One expert tensor in the reference's storage form, from host memory: the LZ4
+ * blocks of its exponent chunks and its raw sign+mantissa plane (what
+ * TensorEngine::PipelineCompress writes, tensor_engine.cpp:168-220). */
+zmoe_status zmoe_layer_load_expert(zmoe_layer* layer, int expert, int tensor, const uint8_t* const* blocks,
+                                   const uint32_t* block_sizes, const uint32_t* original_sizes, int n_chunks,
+                                   const uint8_t* sm, uint64_t numel);
+/* Decode the given experts into free cache slots now. */
+zmoe_status zmoe_layer_warm_cache(zmoe_layer* layer, const int* experts, int n, zmoe_stream_t stream);
+/* x, out: device [T, H] BF16.  Synchronises once on the stream to read the
+ * per-expert token counts. */
+zmoe_status zmoe_layer_forward(zmoe_layer* layer, const uint16_t* x, int T, uint16_t* out, zmoe_stream_t stream);
+/* Same with host buffers (pinned for full speed); returns after out_host is written. */
+zmoe_status zmoe_layer_forward_host(zmoe_layer* layer, const uint16_t* x_host, int T, uint16_t* out_host,
+                                    zmoe_stream_t stream);
+/* Wait for the stream and report any decode error of earlier forwards. */
+zmoe_status zmoe_layer_sync(zmoe_layer* layer, zmoe_stream_t stream);
+zmoe_status zmoe_layer_get_stats(const zmoe_layer* layer, zmoe_layer_stats* out);
+zmoe_status zmoe_layer_reset_stats(zmoe_layer* layer);
+/* Record CUDA events around every decode and routed-FFN launch (stats *_ns). */
+zmoe_status zmoe_layer_set_timing(zmoe_layer* layer, int enable);
+zmoe_status zmoe_layer_cached_experts(const zmoe_layer* layer, int32_t* experts, int cap, int* n);
+
 #ifdef __cplusplus
 }
 #endif

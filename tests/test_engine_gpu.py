@@ -1,0 +1,111 @@
+"""The C++ layer engine (compressed store in HBM, decoded cache, miss decode,
+grouped FFN, combine) against the oracle layers."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import moe
+from zmoe import synthetic as syn
+
+pytestmark = pytest.mark.gpu
+TOL_MAX_ABS = 2e-2
+TOL_MEAN_REL = 5e-3
+
+
+def _close(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    d = np.abs(a - b)
+    return d.max(), d.mean() / max(np.abs(b).mean(), 1e-12)
+
+
+def _build(s, cache, transient=0, policy="ZipMoE", T=64, seed=0, bias=None):
+    from zmoe.layer import MoELayer
+    w = syn.expert_weights(s, 1, std=0.05, seed=seed)[0]
+    wr, sg = syn.router_weights(s, std=0.05, seed=seed + 1)
+    sh = syn.shared_weights(s, std=0.05, seed=seed + 2)
+    L = MoELayer(s, max_tokens=T, cache_slots=cache, transient_slots=transient, policy=policy)
+    L.set_router(wr, bias, sg)
+    if sh is not None:
+        L.set_shared(*sh)
+    L.load_experts(w, num_file_chunks=3)
+    return L, w, wr, sg, sh
+
+
+QWEN_SMALL = syn.LayerShape(hidden=256, num_experts=8, inter=64, topk=4, kind=0, shared_inter=128, shared_gate=True)
+DS_SMALL = syn.LayerShape(hidden=256, num_experts=12, inter=96, topk=3, kind=0, shared_inter=192, shared_gate=False)
+SW_SMALL = syn.LayerShape(hidden=256, num_experts=8, inter=128, topk=1, kind=1, capacity=5, seq_len=32)
+
+
+@pytest.mark.parametrize("cache,transient", [(2, 0), (0, 0), (8, 0), (2, 1), (3, 2)])
+def test_engine_qwen_matches_oracle(cache, transient):
+    s = QWEN_SMALL
+    L, w, wr, sg, sh = _build(s, cache, transient)
+    for step, T in enumerate([24, 1, 64, 24]):
+        x = syn.activations(T, s.hidden, seed=100 + step)
+        out = L(x.cuda())
+        L.sync()
+        ref, _ = moe.qwen_layer(x, wr, w, sh, sg, k=s.topk)
+        mx, mr = _close(out.float().cpu().numpy(), ref.float().numpy())
+        assert mx < TOL_MAX_ABS and mr < TOL_MEAN_REL, (step, mx, mr)
+    st = L.stats()
+    assert st["forwards"] == 4 and st["decode_errors"] == 0
+    assert st["hits"] + st["misses"] > 0
+    if cache == 8:
+        assert len(L.cached_experts()) == 8
+    if cache == 0:
+        assert st["hits"] == 0
+
+
+def test_engine_deepseek_and_bias():
+    s = DS_SMALL
+    bias = torch.linspace(0, -2, s.num_experts)
+    L, w, wr, _, sh = _build(s, 4, bias=bias)
+    x = syn.activations(40, s.hidden, seed=7)
+    out = L(x.cuda())
+    L.sync()
+    ref, _ = moe.deepseek_layer(x, wr, w, sh, k=s.topk, bias=bias.numpy())
+    mx, mr = _close(out.float().cpu().numpy(), ref.float().numpy())
+    assert mx < TOL_MAX_ABS and mr < TOL_MEAN_REL, (mx, mr)
+
+
+def test_engine_switch_capacity_passthrough():
+    s = SW_SMALL
+    L, w, wr, _, _ = _build(s, 2)
+    x = syn.activations(64, s.hidden, seed=9)
+    out = L(x.cuda())
+    L.sync()
+    ref, r = moe.switch_layer(x, wr, w, s.capacity, s.seq_len)
+    assert (r.topk_idx < 0).any()
+    mx, mr = _close(out.float().cpu().numpy(), ref.float().numpy())
+    assert mx < TOL_MAX_ABS and mr < TOL_MEAN_REL, (mx, mr)
+
+
+def test_engine_cache_hits_follow_warm_set():
+    s = QWEN_SMALL
+    L, w, wr, sg, sh = _build(s, 8)
+    L.warm_cache(range(8))
+    x = syn.activations(32, s.hidden, seed=3)
+    L(x.cuda())
+    L.sync()
+    st = L.stats()
+    assert st["misses"] == 0 and st["hits"] > 0
+
+
+def test_engine_forward_host_matches_device():
+    s = QWEN_SMALL
+    L, *_ = _build(s, 2)
+    x = syn.activations(16, s.hidden, seed=5)
+    d = L(x.cuda()).cpu()
+    xh = x.pin_memory()
+    oh = torch.empty_like(xh).pin_memory()
+    L.forward_host(xh, oh)
+    assert torch.equal(d, oh)
+
+
+def test_engine_rejects_bad_inputs():
+    from zmoe._lib import ZmoeError
+    s = QWEN_SMALL
+    L, *_ = _build(s, 2, T=8)
+    with pytest.raises(ZmoeError):
+        L(syn.activations(9, s.hidden).cuda())       # more tokens than max_tokens

@@ -19,7 +19,7 @@ zmoe_status launch_decode_chunks(const zmoe_chunk*, int, int32_t*, cudaStream_t)
 zmoe_status launch_router(const zmoe_router_args*, cudaStream_t);
 zmoe_status launch_permute(const zmoe_permute_args*, cudaStream_t);
 zmoe_status launch_combine(const zmoe_combine_args*, cudaStream_t);
-zmoe_status launch_expert_ffn_simt(const zmoe_ffn_args*, cudaStream_t);
+zmoe_status launch_expert_ffn(const zmoe_ffn_args*, cudaStream_t);
 
 }  // namespace zmoe
 
@@ -51,7 +51,7 @@ zmoe_status zmoe_permute(const zmoe_permute_args* a, zmoe_stream_t stream) {
 }
 
 zmoe_status zmoe_expert_ffn(const zmoe_ffn_args* a, zmoe_stream_t stream) {
-  return zmoe::launch_expert_ffn_simt(a, reinterpret_cast<cudaStream_t>(stream));
+  return zmoe::launch_expert_ffn(a, reinterpret_cast<cudaStream_t>(stream));
 }
 
 zmoe_status zmoe_combine(const zmoe_combine_args* a, zmoe_stream_t stream) {

@@ -1,0 +1,680 @@
+// MoE-layer engine: HBM-resident compressed expert store, decoded-expert
+// cache, on-demand decode of misses, and the layer forward
+// router -> permute -> decode misses -> grouped FFN (+ shared expert) -> combine.
+//
+// Re-targets the reference's host runtime for one layer:
+//  * TensorEngine::ToWorkers / ZipMoESchedulerFunc (csrc/tensor_engine/tensor_engine.cpp:515-669)
+//    and its CPU LZ4 workers: misses become one fused decode launch over all
+//    their chunks, reading LZ4 blocks that already sit in HBM;
+//  * ZipMoECacheHandle::ProactiveDecision and the slot policies
+//    (csrc/memory/cache.cpp:226-270, :445-690): NORMAL -> decode into a cache
+//    slot (evicting a victim that this forward does not use), EVICT -> decode
+//    into a transient slot that is reused by the next forward;
+//  * ExpertDispatcher's fetch/exec/output threads (csrc/dispatcher/expert_dispatcher.cpp:285-499):
+//    one stream-ordered launch sequence, with one host synchronisation to read
+//    the per-expert token counts (the reference's expert_count.cpu(),
+//    experts/expert_executor.py:45-49).
+#include <algorithm>
+#include <memory>
+#include <numeric>
+#include <vector>
+
+#include "common.cuh"
+
+namespace zmoe {
+
+zmoe_status launch_decode_chunks(const zmoe_chunk*, int, int32_t*, cudaStream_t);
+zmoe_status launch_router(const zmoe_router_args*, cudaStream_t);
+zmoe_status launch_permute(const zmoe_permute_args*, cudaStream_t);
+zmoe_status launch_combine(const zmoe_combine_args*, cudaStream_t);
+zmoe_status launch_expert_ffn(const zmoe_ffn_args*, cudaStream_t);
+
+namespace {
+
+struct TensorStore {
+  uint8_t* dev = nullptr;          // [LZ4 blocks, each 16-byte aligned][sign+mantissa plane]
+  std::vector<uint32_t> block_off, block_size, orig_size;
+  uint64_t sm_off = 0, numel = 0, bytes = 0;
+};
+
+template <class T>
+T* dmalloc(size_t n, zmoe_status* st) {
+  void* p = nullptr;
+  if (n == 0) n = 1;
+  if (cudaMalloc(&p, n * sizeof(T)) != cudaSuccess) {
+    set_error("cudaMalloc of %zu bytes failed", n * sizeof(T));
+    *st = ZMOE_ENOMEM;
+    return nullptr;
+  }
+  return static_cast<T*>(p);
+}
+
+template <class T>
+T* hmalloc(size_t n, zmoe_status* st) {
+  void* p = nullptr;
+  if (n == 0) n = 1;
+  if (cudaMallocHost(&p, n * sizeof(T)) != cudaSuccess) {
+    set_error("cudaMallocHost of %zu bytes failed", n * sizeof(T));
+    *st = ZMOE_ENOMEM;
+    return nullptr;
+  }
+  return static_cast<T*>(p);
+}
+
+}  // namespace
+
+struct Layer {
+  zmoe_layer_config cfg{};
+  int tensors = 3;                 // per expert: 3 (SwiGLU) or 2 (ReLU)
+  uint64_t numel = 0;              // elements per expert tensor (H * I)
+  std::vector<std::vector<TensorStore>> store;   // [E][tensors]
+
+  // decoded slots: cache slots first, then transient slots
+  uint16_t* slots = nullptr;
+  int n_cache = 0, n_transient = 0;
+  std::vector<int> slot_owner;     // expert or -1
+  std::vector<int> expert_slot;    // slot or -1 (cache slots only)
+  std::vector<uint64_t> slot_count, slot_stamp, slot_admit;
+  std::vector<uint64_t> global_count;
+  uint64_t clock = 0;
+
+  // weights owned by the layer
+  uint16_t* w_router = nullptr;
+  float* bias = nullptr;
+  uint16_t* w_sgate = nullptr;
+  uint16_t* w_shared[3] = {nullptr, nullptr, nullptr};
+
+  // workspace
+  int max_rows = 0;
+  int32_t *idx = nullptr, *counts = nullptr, *offsets = nullptr, *row_of = nullptr, *tor = nullptr;
+  float *tw = nullptr, *sg = nullptr, *y = nullptr, *ysh = nullptr;
+  uint16_t *xp = nullptr, *h = nullptr, *hsh = nullptr;
+  zmoe_chunk* desc_dev = nullptr;
+  int32_t* status_dev = nullptr;
+  const uint16_t** wtab_dev = nullptr;
+  int32_t* counts_host = nullptr;
+  zmoe_chunk* desc_host = nullptr;
+  const uint16_t** wtab_host = nullptr;
+  int32_t* status_host = nullptr;
+  int max_desc = 0, max_waves = 0;
+  int desc_cursor = 0;             // descriptors used by the current forward
+  int pending_status = 0;          // descriptors whose status is still to be checked
+  // host-side pass-through buffers for forward_host
+  uint16_t* x_stage = nullptr;
+  uint16_t* out_stage = nullptr;
+  cudaEvent_t status_ready = nullptr;
+
+  // optional per-kernel timing: events around decode and FFN launches on the
+  // launch stream, folded into stats at the next synchronisation
+  bool timing = false;
+  std::vector<cudaEvent_t> ev_pool;
+  struct Timed { int ev; int kind; uint64_t bytes; };   // events ev (start), ev + 1 (stop)
+  std::vector<Timed> ev_pending;
+  int ev_used = 0;
+  cudaEvent_t next_event();
+  zmoe_status fold_timing();
+
+  zmoe_layer_stats stats{};
+
+  ~Layer();
+  zmoe_status init(const zmoe_layer_config& c);
+  zmoe_status forward(const uint16_t* x, int T, uint16_t* out, cudaStream_t s);
+  zmoe_status check_status();
+  int choose_victim(const std::vector<char>& active);
+  zmoe_status decode_into(const std::vector<std::pair<int, int>>& jobs, cudaStream_t s, int wave);
+  uint16_t* slot_ptr(int slot, int t) const { return slots + ((size_t)slot * tensors + t) * numel; }
+};
+
+Layer::~Layer() {
+  for (auto& e : store)
+    for (auto& t : e) cudaFree(t.dev);
+  cudaFree(slots);
+  cudaFree(w_router); cudaFree(bias); cudaFree(w_sgate);
+  for (auto* p : w_shared) cudaFree(p);
+  cudaFree(idx); cudaFree(counts); cudaFree(offsets); cudaFree(row_of); cudaFree(tor);
+  cudaFree(tw); cudaFree(sg); cudaFree(y); cudaFree(ysh); cudaFree(xp); cudaFree(h); cudaFree(hsh);
+  cudaFree(desc_dev); cudaFree(status_dev); cudaFree(wtab_dev);
+  cudaFreeHost(counts_host); cudaFreeHost(desc_host); cudaFreeHost(wtab_host); cudaFreeHost(status_host);
+  cudaFree(x_stage); cudaFree(out_stage);
+  if (status_ready) cudaEventDestroy(status_ready);
+  for (auto e : ev_pool) cudaEventDestroy(e);
+}
+
+cudaEvent_t Layer::next_event() {
+  if (ev_used == (int)ev_pool.size()) {
+    cudaEvent_t e;
+    if (cudaEventCreate(&e) != cudaSuccess) return nullptr;
+    ev_pool.push_back(e);
+  }
+  return ev_pool[ev_used++];
+}
+
+zmoe_status Layer::fold_timing() {
+  for (const Timed& t : ev_pending) {
+    float ms = 0.f;
+    ZMOE_CUDA_RET(cudaEventSynchronize(ev_pool[t.ev + 1]));
+    ZMOE_CUDA_RET(cudaEventElapsedTime(&ms, ev_pool[t.ev], ev_pool[t.ev + 1]));
+    const uint64_t ns = (uint64_t)((double)ms * 1.0e6);
+    if (t.kind == 0) {
+      stats.decode_ns += ns;
+      stats.decode_timed_bytes += t.bytes;
+      stats.decode_timed_launches++;
+    } else {
+      stats.ffn_ns += ns;
+      stats.ffn_timed_launches++;
+    }
+  }
+  ev_pending.clear();
+  ev_used = 0;
+  return ZMOE_OK;
+}
+
+zmoe_status Layer::init(const zmoe_layer_config& c) {
+  cfg = c;
+  ZMOE_CHECK_ARG(c.hidden > 0 && c.hidden % 256 == 0, "layer: hidden=%d must be a positive multiple of 256", c.hidden);
+  ZMOE_CHECK_ARG(c.inter > 0 && c.inter % 8 == 0, "layer: inter=%d must be a positive multiple of 8", c.inter);
+  ZMOE_CHECK_ARG(c.num_experts >= 1 && c.num_experts <= 256, "layer: num_experts=%d outside [1, 256]", c.num_experts);
+  ZMOE_CHECK_ARG(c.topk >= 1 && c.topk <= 8 && c.topk <= c.num_experts, "layer: bad topk=%d", c.topk);
+  ZMOE_CHECK_ARG(c.kind == 0 || c.kind == 1, "layer: kind must be 0 (SwiGLU) or 1 (ReLU)");
+  ZMOE_CHECK_ARG(c.route_mode >= 0 && c.route_mode <= 2, "layer: bad route_mode");
+  ZMOE_CHECK_ARG(c.max_tokens >= 1, "layer: max_tokens must be >= 1");
+  ZMOE_CHECK_ARG(c.cache_slots >= 0 && c.cache_slots <= c.num_experts, "layer: cache_slots outside [0, E]");
+  ZMOE_CHECK_ARG(c.shared_inter == 0 || c.shared_inter % 8 == 0, "layer: shared_inter must be a multiple of 8");
+  ZMOE_CHECK_ARG(c.route_mode != ZMOE_ROUTE_SWITCH || c.kind == 1, "layer: Switch routing needs ReLU experts");
+  tensors = c.kind == 0 ? 3 : 2;
+  numel = (uint64_t)c.hidden * c.inter;
+  const int E = c.num_experts;
+  store.assign(E, std::vector<TensorStore>(tensors));
+  n_cache = c.cache_slots;
+  n_transient = c.transient_slots > 0 ? std::min(c.transient_slots, E) : E - n_cache;
+  if (n_transient < 1) n_transient = 1;
+  const int n_slots = n_cache + n_transient;
+  slot_owner.assign(n_slots, -1);
+  expert_slot.assign(E, -1);
+  slot_count.assign(n_slots, 0);
+  slot_stamp.assign(n_slots, 0);
+  slot_admit.assign(n_slots, 0);
+  global_count.assign(E, 0);
+  zmoe_status st = ZMOE_OK;
+  slots = dmalloc<uint16_t>((size_t)n_slots * tensors * numel, &st);
+  const int T = c.max_tokens, k = c.topk, H = c.hidden;
+  max_rows = T * k;
+  idx = dmalloc<int32_t>((size_t)T * k, &st);
+  tw = dmalloc<float>((size_t)T * k, &st);
+  sg = dmalloc<float>(T, &st);
+  counts = dmalloc<int32_t>(E, &st);
+  offsets = dmalloc<int32_t>(E + 1, &st);
+  row_of = dmalloc<int32_t>((size_t)T * k, &st);
+  tor = dmalloc<int32_t>((size_t)T * k, &st);
+  xp = dmalloc<uint16_t>((size_t)max_rows * H, &st);
+  h = dmalloc<uint16_t>((size_t)max_rows * c.inter, &st);
+  y = dmalloc<float>((size_t)max_rows * H, &st);
+  if (c.shared_inter > 0) {
+    ysh = dmalloc<float>((size_t)T * H, &st);
+    hsh = dmalloc<uint16_t>((size_t)T * c.shared_inter, &st);
+  }
+  max_waves = (E + n_transient - 1) / n_transient + 1;
+  max_desc = E * tensors * 64;
+  desc_dev = dmalloc<zmoe_chunk>(max_desc, &st);
+  status_dev = dmalloc<int32_t>(max_desc, &st);
+  wtab_dev = dmalloc<const uint16_t*>((size_t)max_waves * E * 3, &st);
+  counts_host = hmalloc<int32_t>(E, &st);
+  desc_host = hmalloc<zmoe_chunk>(max_desc, &st);
+  wtab_host = hmalloc<const uint16_t*>((size_t)max_waves * E * 3, &st);
+  status_host = hmalloc<int32_t>(max_desc, &st);
+  x_stage = dmalloc<uint16_t>((size_t)T * H, &st);
+  out_stage = dmalloc<uint16_t>((size_t)T * H, &st);
+  if (st != ZMOE_OK) return st;
+  ZMOE_CUDA_RET(cudaEventCreateWithFlags(&status_ready, cudaEventDisableTiming));
+  return ZMOE_OK;
+}
+
+int Layer::choose_victim(const std::vector<char>& active) {
+  int victim = -1;
+  uint64_t best = UINT64_MAX;
+  for (int s = 0; s < n_cache; ++s) {
+    const int e = slot_owner[s];
+    if (e < 0) return s;                      // free slot
+    if (active[e]) continue;                  // protected: used by this forward
+    uint64_t key;
+    switch (cfg.cache_policy) {
+      case ZMOE_CACHE_LRU: key = slot_stamp[s]; break;
+      case ZMOE_CACHE_FIFO: key = slot_admit[s]; break;
+      case ZMOE_CACHE_LFU: key = global_count[e]; break;
+      default: key = slot_count[s]; break;     // ZipMoE: tokens served since admission
+    }
+    if (key < best) { best = key; victim = s; }
+  }
+  return victim;
+}
+
+zmoe_status Layer::check_status() {
+  if (pending_status == 0) return ZMOE_OK;
+  ZMOE_CUDA_RET(cudaEventSynchronize(status_ready));
+  const int n = pending_status;
+  pending_status = 0;
+  for (int i = 0; i < n; ++i) {
+    if (status_host[i] != ZMOE_CHUNK_OK) {
+      stats.decode_errors++;
+      set_error("decode of chunk %d failed with status %d", i, status_host[i]);
+      return ZMOE_EINVAL;
+    }
+  }
+  return ZMOE_OK;
+}
+
+// Decode (expert, slot) jobs in one fused launch.
+zmoe_status Layer::decode_into(const std::vector<std::pair<int, int>>& jobs, cudaStream_t s, int wave) {
+  const int base = desc_cursor;
+  int nd = base;
+  for (auto [e, slot] : jobs) {
+    for (int t = 0; t < tensors; ++t) {
+      const TensorStore& ts = store[e][t];
+      uint64_t e0 = 0;
+      uint16_t* dst = slot_ptr(slot, t);
+      for (size_t c = 0; c < ts.block_off.size(); ++c) {
+        if (nd >= max_desc) {
+          set_error("too many chunks in one decode (%d)", nd);
+          return ZMOE_EUNSUPPORTED;
+        }
+        zmoe_chunk& d = desc_host[nd++];
+        d.src = ts.dev + ts.block_off[c];
+        d.sm = ts.dev + ts.sm_off + e0;
+        d.dst = dst + e0;
+        d.src_size = ts.block_size[c];
+        d.out_size = ts.orig_size[c];
+        stats.decoded_bytes += (uint64_t)ts.block_size[c] + 3ull * ts.orig_size[c];
+        e0 += ts.orig_size[c];
+      }
+    }
+    stats.decoded_experts++;
+  }
+  const int cnt = nd - base;
+  if (cnt == 0) return ZMOE_OK;
+  (void)wave;
+  // Descriptors and status words of every wave of one forward live side by
+  // side, so no pinned buffer is rewritten before its copy has run.
+  desc_cursor = nd;
+  ZMOE_CUDA_RET(cudaMemcpyAsync(desc_dev + base, desc_host + base, sizeof(zmoe_chunk) * cnt,
+                                cudaMemcpyHostToDevice, s));
+  uint64_t bytes = 0;
+  for (int i = base; i < nd; ++i) bytes += (uint64_t)desc_host[i].src_size + 3ull * desc_host[i].out_size;
+  int ev = -1;
+  if (timing) {
+    ev = ev_used;
+    cudaEvent_t a = next_event(), b = next_event();
+    if (!a || !b) { set_error("cudaEventCreate failed"); return ZMOE_ECUDA; }
+    ZMOE_CUDA_RET(cudaEventRecord(a, s));
+  }
+  zmoe_status st = launch_decode_chunks(desc_dev + base, cnt, status_dev + base, s);
+  if (st != ZMOE_OK) return st;
+  if (timing) {
+    ZMOE_CUDA_RET(cudaEventRecord(ev_pool[ev + 1], s));
+    ev_pending.push_back({ev, 0, bytes});
+  }
+  stats.launches++;
+  stats.decode_launches++;
+  stats.decoded_chunks += cnt;
+  ZMOE_CUDA_RET(cudaMemcpyAsync(status_host + base, status_dev + base, sizeof(int32_t) * cnt,
+                                cudaMemcpyDeviceToHost, s));
+  ZMOE_CUDA_RET(cudaEventRecord(status_ready, s));
+  pending_status = nd;
+  return ZMOE_OK;
+}
+
+zmoe_status Layer::forward(const uint16_t* x, int T, uint16_t* out, cudaStream_t s) {
+  ZMOE_CHECK_ARG(x && out, "forward: null pointer");
+  ZMOE_CHECK_ARG(T >= 0 && T <= cfg.max_tokens, "forward: T=%d outside [0, max_tokens=%d]", T, cfg.max_tokens);
+  ZMOE_CHECK_ARG(w_router, "forward: router weights not set");
+  const int E = cfg.num_experts, k = cfg.topk, H = cfg.hidden;
+  for (int e = 0; e < E; ++e)
+    for (int t = 0; t < tensors; ++t)
+      ZMOE_CHECK_ARG(store[e][t].dev, "forward: expert %d tensor %d not loaded", e, t);
+  if (T == 0) return ZMOE_OK;
+  zmoe_status st;
+
+  // 1. router
+  zmoe_router_args ra{};
+  ra.x = x; ra.w = w_router; ra.bias = bias; ra.w_shared_gate = w_sgate;
+  ra.T = T; ra.H = H; ra.E = E; ra.k = k; ra.mode = cfg.route_mode;
+  ra.norm_topk_prob = cfg.norm_topk_prob; ra.scaling = cfg.scaling;
+  ra.logits = nullptr; ra.topk_idx = idx; ra.topk_w = tw; ra.shared_gate = w_sgate ? sg : nullptr;
+  if ((st = launch_router(&ra, s)) != ZMOE_OK) return st;
+  stats.launches++;
+
+  // 2. permute + counts to the host
+  zmoe_permute_args pa{};
+  pa.topk_idx = idx; pa.x = x; pa.T = T; pa.H = H; pa.E = E; pa.k = k;
+  pa.capacity = cfg.route_mode == ZMOE_ROUTE_SWITCH ? cfg.capacity : 0;
+  pa.seq_len = cfg.seq_len > 0 ? cfg.seq_len : T;
+  pa.counts = counts; pa.offsets = offsets; pa.row_of = row_of; pa.token_of_row = tor; pa.xp = xp;
+  if ((st = launch_permute(&pa, s)) != ZMOE_OK) return st;
+  stats.launches += 3;
+  ZMOE_CUDA_RET(cudaMemcpyAsync(counts_host, counts, sizeof(int32_t) * E, cudaMemcpyDeviceToHost, s));
+
+  // shared expert first: it needs no decoded weights
+  if (cfg.shared_inter > 0 && w_shared[0]) {
+    zmoe_ffn_args fa{};
+    const uint16_t* tab[3] = {w_shared[0], w_shared[1], w_shared[2]};
+    // the table lives at the end of the wave tables
+    const uint16_t** shtab = wtab_host + (size_t)(max_waves * E - 1) * 3;
+    shtab[0] = tab[0]; shtab[1] = tab[1]; shtab[2] = tab[2];
+    const uint16_t** shtab_dev = wtab_dev + (size_t)(max_waves * E - 1) * 3;
+    ZMOE_CUDA_RET(cudaMemcpyAsync(shtab_dev, shtab, sizeof(void*) * 3, cudaMemcpyHostToDevice, s));
+    fa.x = x; fa.w = shtab_dev; fa.offsets = nullptr; fa.G = 1; fa.rows_total = T; fa.H = H;
+    fa.I = cfg.shared_inter; fa.kind = 0; fa.h = hsh; fa.y = ysh;
+    if ((st = launch_expert_ffn(&fa, s)) != ZMOE_OK) return st;
+    stats.launches += 2;
+  }
+  ZMOE_CUDA_RET(cudaStreamSynchronize(s));
+  if ((st = check_status()) != ZMOE_OK) return st;   // previous forward's decode
+  desc_cursor = 0;
+  if ((st = fold_timing()) != ZMOE_OK) return st;
+
+  // 3. cache decisions (ProactiveDecision)
+  std::vector<char> active(E, 0);
+  std::vector<int> act;
+  for (int e = 0; e < E; ++e)
+    if (counts_host[e] > 0) { active[e] = 1; act.push_back(e); global_count[e] += counts_host[e]; }
+  ++clock;
+  std::vector<int> ranked(act);
+  std::vector<std::pair<int, int>> hits_slots;       // (expert, slot) ready to use
+  std::vector<int> misses;
+  for (int e : act) {
+    const int sl = expert_slot[e];
+    if (sl >= 0) {
+      stats.hits++;
+      slot_count[sl] += counts_host[e];
+      slot_stamp[sl] = clock;
+      hits_slots.push_back({e, sl});
+    } else {
+      stats.misses++;
+      misses.push_back(e);
+    }
+  }
+  // rank of each miss by global count (count_up of cache.cpp:230-238)
+  std::vector<std::pair<int, int>> to_cache, to_transient;
+  const double thr_normal = n_cache + cfg.state_margin * E;
+  for (int e : misses) {
+    int up = 0;
+    for (int q = 0; q < E; ++q) up += global_count[q] > global_count[e];
+    int slot = -1;
+    if (n_cache > 0 && up < thr_normal) {
+      slot = choose_victim(active);
+      if (slot >= 0) {
+        if (slot_owner[slot] >= 0) { expert_slot[slot_owner[slot]] = -1; stats.evictions++; }
+        slot_owner[slot] = e;
+        expert_slot[e] = slot;
+        slot_count[slot] = counts_host[e];
+        slot_stamp[slot] = clock;
+        slot_admit[slot] = clock;
+        to_cache.push_back({e, slot});
+        continue;
+      }
+    }
+    to_transient.push_back({e, -1});
+  }
+
+  // 4. waves: decode misses, run the grouped FFN over experts whose weights are ready
+  size_t tpos = 0;
+  int wave = 0;
+  std::vector<std::pair<int, int>> ready(hits_slots);
+  std::vector<std::pair<int, int>> jobs(to_cache);
+  while (true) {
+    int used = 0;
+    while (tpos < to_transient.size() && used < n_transient) {
+      const int slot = n_cache + used;
+      jobs.push_back({to_transient[tpos].first, slot});
+      ++tpos;
+      ++used;
+    }
+    if ((st = decode_into(jobs, s, wave)) != ZMOE_OK) return st;
+    ready.insert(ready.end(), jobs.begin(), jobs.end());
+    if (!ready.empty()) {
+      if (wave >= max_waves - 1) { set_error("too many decode waves"); return ZMOE_EUNSUPPORTED; }
+      const uint16_t** tab = wtab_host + (size_t)wave * E * 3;
+      std::fill(tab, tab + (size_t)E * 3, nullptr);
+      for (auto [e, slot] : ready) {
+        tab[e * 3 + 0] = slot_ptr(slot, 0);
+        tab[e * 3 + 1] = tensors == 3 ? slot_ptr(slot, 1) : nullptr;
+        tab[e * 3 + 2] = slot_ptr(slot, tensors - 1);
+      }
+      const uint16_t** tdev = wtab_dev + (size_t)wave * E * 3;
+      ZMOE_CUDA_RET(cudaMemcpyAsync(tdev, tab, sizeof(void*) * E * 3, cudaMemcpyHostToDevice, s));
+      zmoe_ffn_args fa{};
+      fa.x = xp; fa.w = tdev; fa.offsets = offsets; fa.G = E; fa.rows_total = T * k; fa.H = H;
+      fa.I = cfg.inter; fa.kind = cfg.kind; fa.h = h; fa.y = y;
+      int ev = -1;
+      if (timing) {
+        ev = ev_used;
+        cudaEvent_t a = next_event(), b = next_event();
+        if (!a || !b) { set_error("cudaEventCreate failed"); return ZMOE_ECUDA; }
+        ZMOE_CUDA_RET(cudaEventRecord(a, s));
+      }
+      if ((st = launch_expert_ffn(&fa, s)) != ZMOE_OK) return st;
+      if (timing) {
+        ZMOE_CUDA_RET(cudaEventRecord(ev_pool[ev + 1], s));
+        ev_pending.push_back({ev, 1, 0});
+      }
+      stats.launches += 2;
+    }
+    ++wave;
+    ready.clear();
+    jobs.clear();
+    if (tpos >= to_transient.size()) break;
+  }
+
+  // 5. combine
+  zmoe_combine_args ca{};
+  ca.y = y; ca.y_shared = (cfg.shared_inter > 0 && w_shared[0]) ? ysh : nullptr;
+  ca.shared_gate = w_sgate ? sg : nullptr; ca.row_of = row_of; ca.topk_w = tw; ca.x = x;
+  ca.T = T; ca.H = H; ca.k = k; ca.mode = cfg.route_mode; ca.out = out;
+  if ((st = launch_combine(&ca, s)) != ZMOE_OK) return st;
+  stats.launches++;
+  stats.forwards++;
+  stats.tokens += T;
+  return ZMOE_OK;
+}
+
+}  // namespace zmoe
+
+using zmoe::Layer;
+
+extern "C" {
+
+zmoe_status zmoe_layer_create(const zmoe_layer_config* cfg, zmoe_layer** out) {
+  ZMOE_CHECK_ARG(cfg && out, "layer_create: null pointer");
+  auto* L = new Layer();
+  zmoe_status st = L->init(*cfg);
+  if (st != ZMOE_OK) {
+    delete L;
+    *out = nullptr;
+    return st;
+  }
+  *out = reinterpret_cast<zmoe_layer*>(L);
+  return ZMOE_OK;
+}
+
+zmoe_status zmoe_layer_destroy(zmoe_layer* layer) {
+  delete reinterpret_cast<Layer*>(layer);
+  return ZMOE_OK;
+}
+
+static zmoe_status upload(void** dst, const void* src, size_t bytes) {
+  ZMOE_CUDA_RET(cudaMalloc(dst, bytes));
+  ZMOE_CUDA_RET(cudaMemcpy(*dst, src, bytes, cudaMemcpyHostToDevice));
+  return ZMOE_OK;
+}
+
+zmoe_status zmoe_layer_set_router(zmoe_layer* layer, const uint16_t* w_router, const float* bias,
+                                  const uint16_t* w_shared_gate) {
+  Layer* L = reinterpret_cast<Layer*>(layer);
+  ZMOE_CHECK_ARG(L && w_router, "set_router: null pointer");
+  const size_t H = L->cfg.hidden, E = L->cfg.num_experts;
+  cudaFree(L->w_router); cudaFree(L->bias); cudaFree(L->w_sgate);
+  L->w_router = nullptr; L->bias = nullptr; L->w_sgate = nullptr;
+  zmoe_status st = upload((void**)&L->w_router, w_router, E * H * 2);
+  if (st == ZMOE_OK && bias) st = upload((void**)&L->bias, bias, E * 4);
+  if (st == ZMOE_OK && w_shared_gate) st = upload((void**)&L->w_sgate, w_shared_gate, H * 2);
+  return st;
+}
+
+zmoe_status zmoe_layer_set_shared(zmoe_layer* layer, const uint16_t* gate, const uint16_t* up,
+                                  const uint16_t* down) {
+  Layer* L = reinterpret_cast<Layer*>(layer);
+  ZMOE_CHECK_ARG(L && gate && up && down, "set_shared: null pointer");
+  ZMOE_CHECK_ARG(L->cfg.shared_inter > 0, "set_shared: layer has no shared expert");
+  const size_t n = (size_t)L->cfg.hidden * L->cfg.shared_inter * 2;
+  const uint16_t* src[3] = {gate, up, down};
+  for (int i = 0; i < 3; ++i) {
+    cudaFree(L->w_shared[i]);
+    L->w_shared[i] = nullptr;
+    zmoe_status st = upload((void**)&L->w_shared[i], src[i], n);
+    if (st != ZMOE_OK) return st;
+  }
+  return ZMOE_OK;
+}
+
+zmoe_status zmoe_layer_load_expert(zmoe_layer* layer, int expert, int tensor, const uint8_t* const* blocks,
+                                   const uint32_t* block_sizes, const uint32_t* original_sizes, int n_chunks,
+                                   const uint8_t* sm, uint64_t numel) {
+  Layer* L = reinterpret_cast<Layer*>(layer);
+  ZMOE_CHECK_ARG(L && blocks && block_sizes && original_sizes && sm, "load_expert: null pointer");
+  ZMOE_CHECK_ARG(expert >= 0 && expert < L->cfg.num_experts, "load_expert: expert %d out of range", expert);
+  ZMOE_CHECK_ARG(tensor >= 0 && tensor < L->tensors, "load_expert: tensor %d out of range", tensor);
+  ZMOE_CHECK_ARG(numel == L->numel, "load_expert: numel %llu != H*I = %llu", (unsigned long long)numel,
+                 (unsigned long long)L->numel);
+  ZMOE_CHECK_ARG(n_chunks >= 1 && n_chunks <= 64, "load_expert: n_chunks=%d outside [1, 64]", n_chunks);
+  uint64_t total = 0;
+  for (int c = 0; c < n_chunks; ++c) {
+    ZMOE_CHECK_ARG(blocks[c] && block_sizes[c] > 0, "load_expert: empty block %d", c);
+    total += original_sizes[c];
+  }
+  ZMOE_CHECK_ARG(total == numel, "load_expert: chunk sizes sum to %llu, expected %llu",
+                 (unsigned long long)total, (unsigned long long)numel);
+  zmoe::TensorStore ts;
+  uint64_t pos = 0;
+  for (int c = 0; c < n_chunks; ++c) {
+    ts.block_off.push_back((uint32_t)pos);
+    ts.block_size.push_back(block_sizes[c]);
+    ts.orig_size.push_back(original_sizes[c]);
+    pos += (block_sizes[c] + 15) / 16 * 16;
+  }
+  ts.sm_off = pos;
+  ts.numel = numel;
+  ts.bytes = pos + numel;
+  std::vector<uint8_t> host(ts.bytes, 0);
+  for (int c = 0; c < n_chunks; ++c) memcpy(host.data() + ts.block_off[c], blocks[c], block_sizes[c]);
+  memcpy(host.data() + ts.sm_off, sm, numel);
+  zmoe_status st = upload((void**)&ts.dev, host.data(), ts.bytes);
+  if (st != ZMOE_OK) return st;
+  auto& slot = L->store[expert][tensor];
+  cudaFree(slot.dev);
+  L->stats.store_bytes += ts.bytes - slot.bytes;
+  slot = std::move(ts);
+  // a re-loaded expert must be decoded again
+  if (L->expert_slot[expert] >= 0) {
+    L->slot_owner[L->expert_slot[expert]] = -1;
+    L->expert_slot[expert] = -1;
+  }
+  return ZMOE_OK;
+}
+
+zmoe_status zmoe_layer_warm_cache(zmoe_layer* layer, const int* experts, int n, zmoe_stream_t stream) {
+  Layer* L = reinterpret_cast<Layer*>(layer);
+  ZMOE_CHECK_ARG(L && (n == 0 || experts), "warm_cache: null pointer");
+  ZMOE_CHECK_ARG(n <= L->n_cache, "warm_cache: %d experts > %d cache slots", n, L->n_cache);
+  std::vector<std::pair<int, int>> jobs;
+  for (int i = 0; i < n; ++i) {
+    const int e = experts[i];
+    ZMOE_CHECK_ARG(e >= 0 && e < L->cfg.num_experts, "warm_cache: expert %d out of range", e);
+    for (int t = 0; t < L->tensors; ++t)
+      ZMOE_CHECK_ARG(L->store[e][t].dev, "warm_cache: expert %d not loaded", e);
+    if (L->expert_slot[e] >= 0) continue;
+    int slot = -1;
+    for (int s2 = 0; s2 < L->n_cache; ++s2)
+      if (L->slot_owner[s2] < 0) { slot = s2; break; }
+    ZMOE_CHECK_ARG(slot >= 0, "warm_cache: no free cache slot");
+    L->slot_owner[slot] = e;
+    L->expert_slot[e] = slot;
+    L->slot_admit[slot] = L->clock;
+    jobs.push_back({e, slot});
+  }
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  ZMOE_CUDA_RET(cudaStreamSynchronize(s));
+  zmoe_status st = L->check_status();
+  if (st != ZMOE_OK) return st;
+  L->desc_cursor = 0;
+  st = L->decode_into(jobs, s, 0);
+  if (st != ZMOE_OK) return st;
+  ZMOE_CUDA_RET(cudaStreamSynchronize(s));
+  return L->check_status();
+}
+
+zmoe_status zmoe_layer_forward(zmoe_layer* layer, const uint16_t* x, int T, uint16_t* out, zmoe_stream_t stream) {
+  Layer* L = reinterpret_cast<Layer*>(layer);
+  ZMOE_CHECK_ARG(L, "forward: null layer");
+  return L->forward(x, T, out, reinterpret_cast<cudaStream_t>(stream));
+}
+
+zmoe_status zmoe_layer_forward_host(zmoe_layer* layer, const uint16_t* x_host, int T, uint16_t* out_host,
+                                    zmoe_stream_t stream) {
+  Layer* L = reinterpret_cast<Layer*>(layer);
+  ZMOE_CHECK_ARG(L && x_host && out_host, "forward_host: null pointer");
+  ZMOE_CHECK_ARG(T >= 0 && T <= L->cfg.max_tokens, "forward_host: T=%d outside [0, max_tokens]", T);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const size_t bytes = (size_t)T * L->cfg.hidden * 2;
+  ZMOE_CUDA_RET(cudaMemcpyAsync(L->x_stage, x_host, bytes, cudaMemcpyHostToDevice, s));
+  zmoe_status st = L->forward(L->x_stage, T, L->out_stage, s);
+  if (st != ZMOE_OK) return st;
+  ZMOE_CUDA_RET(cudaMemcpyAsync(out_host, L->out_stage, bytes, cudaMemcpyDeviceToHost, s));
+  ZMOE_CUDA_RET(cudaStreamSynchronize(s));
+  return ZMOE_OK;
+}
+
+zmoe_status zmoe_layer_sync(zmoe_layer* layer, zmoe_stream_t stream) {
+  Layer* L = reinterpret_cast<Layer*>(layer);
+  ZMOE_CHECK_ARG(L, "sync: null layer");
+  ZMOE_CUDA_RET(cudaStreamSynchronize(reinterpret_cast<cudaStream_t>(stream)));
+  zmoe_status st = L->check_status();
+  if (st != ZMOE_OK) return st;
+  return L->fold_timing();
+}
+
+zmoe_status zmoe_layer_set_timing(zmoe_layer* layer, int enable) {
+  Layer* L = reinterpret_cast<Layer*>(layer);
+  ZMOE_CHECK_ARG(L, "set_timing: null layer");
+  L->timing = enable != 0;
+  return ZMOE_OK;
+}
+
+zmoe_status zmoe_layer_reset_stats(zmoe_layer* layer) {
+  Layer* L = reinterpret_cast<Layer*>(layer);
+  ZMOE_CHECK_ARG(L, "reset_stats: null layer");
+  const uint64_t store = L->stats.store_bytes;
+  L->stats = zmoe_layer_stats{};
+  L->stats.store_bytes = store;
+  return ZMOE_OK;
+}
+
+zmoe_status zmoe_layer_get_stats(const zmoe_layer* layer, zmoe_layer_stats* out) {
+  const Layer* L = reinterpret_cast<const Layer*>(layer);
+  ZMOE_CHECK_ARG(L && out, "get_stats: null pointer");
+  *out = L->stats;
+  return ZMOE_OK;
+}
+
+zmoe_status zmoe_layer_cached_experts(const zmoe_layer* layer, int32_t* experts, int cap, int* n) {
+  const Layer* L = reinterpret_cast<const Layer*>(layer);
+  ZMOE_CHECK_ARG(L && n, "cached_experts: null pointer");
+  int c = 0;
+  for (int s = 0; s < L->n_cache; ++s)
+    if (L->slot_owner[s] >= 0) {
+      if (experts && c < cap) experts[c] = L->slot_owner[s];
+      ++c;
+    }
+  *n = c;
+  return ZMOE_OK;
+}
+
+}  // extern "C"

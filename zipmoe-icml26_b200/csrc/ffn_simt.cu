@@ -27,6 +27,7 @@ ffn_simt_kernel(const uint16_t* __restrict__ A, const uint16_t* const* __restric
   const int col_base = blockIdx.x * kBN;
   const uint16_t* W0 = MODE == 2 ? w[3 * g + 2] : w[3 * g];
   const uint16_t* W1 = MODE == 0 ? w[3 * g + 1] : nullptr;
+  if (W0 == nullptr || (MODE == 0 && W1 == nullptr)) return;   // group not in this launch
   const int tr = threadIdx.x / 16, tc = threadIdx.x % 16;
   float acc[2][4] = {}, accu[2][4] = {};
   for (int k0 = 0; k0 < K; k0 += kBK) {
@@ -81,7 +82,7 @@ ffn_simt_kernel(const uint16_t* __restrict__ A, const uint16_t* const* __restric
 
 }  // namespace
 
-zmoe_status launch_expert_ffn_simt(const zmoe_ffn_args* a, cudaStream_t stream) {
+zmoe_status launch_expert_ffn(const zmoe_ffn_args* a, cudaStream_t stream) {
   ZMOE_CHECK_ARG(a && a->x && a->w && a->h && a->y, "expert_ffn: null pointer");
   ZMOE_CHECK_ARG(a->G >= 1 && a->H > 0 && a->I > 0, "expert_ffn: bad sizes");
   ZMOE_CHECK_ARG(a->kind == 0 || a->kind == 1, "expert_ffn: kind must be 0 (SwiGLU) or 1 (ReLU)");

@@ -48,6 +48,21 @@ class CombineArgs(ctypes.Structure):
                 ("mode", c_int), ("out", c_void_p)]
 
 
+class LayerConfig(ctypes.Structure):
+    _fields_ = [("hidden", c_int), ("num_experts", c_int), ("inter", c_int), ("topk", c_int),
+                ("kind", c_int), ("route_mode", c_int), ("norm_topk_prob", c_int), ("scaling", c_float),
+                ("shared_inter", c_int), ("capacity", c_int), ("seq_len", c_int), ("max_tokens", c_int),
+                ("cache_slots", c_int), ("transient_slots", c_int), ("cache_policy", c_int),
+                ("state_margin", ctypes.c_double)]
+
+
+class LayerStats(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_uint64) for n in (
+        "forwards", "tokens", "hits", "misses", "evictions", "decoded_experts", "decoded_chunks",
+        "decoded_bytes", "decode_launches", "launches", "decode_errors", "store_bytes",
+        "decode_ns", "decode_timed_bytes", "decode_timed_launches", "ffn_ns", "ffn_timed_launches")]
+
+
 # (name, restype, argtypes) of every exported symbol; tests check the header
 # declares exactly these.
 SIGNATURES = {
@@ -59,6 +74,25 @@ SIGNATURES = {
     "zmoe_permute": (c_int, [ctypes.POINTER(PermuteArgs), c_void_p]),
     "zmoe_expert_ffn": (c_int, [ctypes.POINTER(FfnArgs), c_void_p]),
     "zmoe_combine": (c_int, [ctypes.POINTER(CombineArgs), c_void_p]),
+    "zmoe_split_planes": (c_int, [c_void_p, ctypes.c_uint64, c_void_p, c_void_p]),
+    "zmoe_lz4_compress_bound": (c_int, [c_int]),
+    "zmoe_lz4_compress": (c_int, [c_void_p, c_int, c_void_p, c_int, c_int, c_int]),
+    "zmoe_layer_create": (c_int, [ctypes.POINTER(LayerConfig), ctypes.POINTER(c_void_p)]),
+    "zmoe_layer_destroy": (c_int, [c_void_p]),
+    "zmoe_layer_set_router": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p]),
+    "zmoe_layer_set_shared": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p]),
+    "zmoe_layer_load_expert": (c_int, [c_void_p, c_int, c_int, ctypes.POINTER(c_void_p),
+                                       ctypes.POINTER(c_u32), ctypes.POINTER(c_u32), c_int, c_void_p,
+                                       ctypes.c_uint64]),
+    "zmoe_layer_warm_cache": (c_int, [c_void_p, ctypes.POINTER(c_int), c_int, c_void_p]),
+    "zmoe_layer_forward": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p]),
+    "zmoe_layer_forward_host": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p]),
+    "zmoe_layer_sync": (c_int, [c_void_p, c_void_p]),
+    "zmoe_layer_get_stats": (c_int, [c_void_p, ctypes.POINTER(LayerStats)]),
+    "zmoe_layer_reset_stats": (c_int, [c_void_p]),
+    "zmoe_layer_set_timing": (c_int, [c_void_p, c_int]),
+    "zmoe_layer_cached_experts": (c_int, [c_void_p, ctypes.POINTER(ctypes.c_int32), c_int,
+                                          ctypes.POINTER(c_int)]),
 }
 
 
