@@ -25,3 +25,28 @@ def test_encode_matches_oracle_bytes_and_roundtrips():
             blocks, osz, sm = ocodec.encode_tensor(bits, 3, cod, lvl, lvl)
             assert e.blocks == blocks and e.original_sizes == osz and e.sm == sm.tobytes()
             assert np.array_equal(ocodec.decode_tensor(e.blocks, e.original_sizes, np.frombuffer(e.sm, np.uint8)), bits)
+
+
+def test_segment_index_matches_token_walk():
+    from zmoe import ops
+    gen = torch.Generator().manual_seed(4)
+    bits = ocodec.bf16_bits((torch.randn(100, 700, generator=gen) * 0.02).to(torch.bfloat16))
+    blocks, osz, _ = ocodec.encode_tensor(bits, 2)
+    for blk, o in zip(blocks, osz):
+        seqs = ocodec.lz4_sequences(blk)
+        for seg in (64, 2048, 10 ** 6):
+            idx = ops.build_index(blk, o, seg)
+            assert len(idx) == (o + seg - 1) // seg
+            starts = [(s[0], s[1]) for s in seqs]
+            for j, (ip, op) in enumerate(idx.tolist()):
+                want = next(((a, b) for a, b in starts if b >= j * seg), None)
+                assert (ip, op) == want, (seg, j)
+
+
+def test_segment_index_rejects_malformed():
+    from zmoe import ops
+    import pytest
+    exp = (np.arange(5000) % 7).astype(np.uint8)
+    blk = ocodec.lz4_compress_hc(exp)
+    with pytest.raises(ValueError):
+        ops.build_index(blk[: len(blk) // 2], exp.size)

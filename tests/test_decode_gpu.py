@@ -158,3 +158,34 @@ def test_tensor_recover_bit_exact(n, offset):
     out = ops.tensor_recover(e[offset:], s[offset:])
     torch.cuda.synchronize()
     assert np.array_equal(_bits(out), bits)
+
+
+@pytest.mark.parametrize("seg_bytes,indexed", [(64, True), (256, True), (2048, True), (1 << 30, True), (0, False)])
+def test_decode_segment_sizes(seg_bytes, indexed):
+    """Many small segments force cross-segment waits; an unindexed chunk is
+    decoded by one warp; all must give the same bytes."""
+    ops = _ops()
+    gen = torch.Generator().manual_seed(21)
+    w = (torch.randn(512, 2048, generator=gen) * 0.02).to(torch.bfloat16)
+    bits = codec.bf16_bits(w)
+    blocks, osz, sm = codec.encode_tensor(bits, 3)
+    ct = ops.CompressedTensor(blocks, osz, sm.tobytes(), seg_bytes=seg_bytes or 2048, indexed=indexed)
+    out, st = ct.decode()
+    torch.cuda.synchronize()
+    assert (st.cpu().numpy() == 0).all(), st.cpu().numpy()
+    assert np.array_equal(_bits(out), bits)
+
+
+def test_decode_small_offsets_across_segments():
+    """Periodic data gives short offsets that reach into the previous segment."""
+    ops = _ops()
+    rng = np.random.default_rng(8)
+    base = rng.integers(0, 65536, 37, dtype=np.uint16)
+    bits = np.concatenate([np.tile(base, 3000), rng.integers(0, 65536, 5000, dtype=np.uint16),
+                           np.tile(base[:5], 20000)])
+    blocks, osz, sm = codec.encode_tensor(bits, 1)
+    for seg in (64, 512):
+        out, st = ops.CompressedTensor(blocks, osz, sm.tobytes(), seg_bytes=seg).decode()
+        torch.cuda.synchronize()
+        assert (st.cpu().numpy() == 0).all()
+        assert np.array_equal(_bits(out), bits)

@@ -32,10 +32,15 @@ zmoe_status launch_expert_ffn(const zmoe_ffn_args*, cudaStream_t);
 namespace {
 
 struct TensorStore {
-  uint8_t* dev = nullptr;          // [LZ4 blocks, each 16-byte aligned][sign+mantissa plane]
+  // [LZ4 blocks, each 16-byte aligned][sign+mantissa plane][segment indexes]
+  uint8_t* dev = nullptr;
   std::vector<uint32_t> block_off, block_size, orig_size;
+  std::vector<uint64_t> idx_off;   // byte offset of each block's index
+  std::vector<uint32_t> idx_n;     // entries of each block's index
   uint64_t sm_off = 0, numel = 0, bytes = 0;
 };
+
+constexpr uint32_t kSegBytes = 2048;
 
 template <class T>
 T* dmalloc(size_t n, zmoe_status* st) {
@@ -283,6 +288,9 @@ zmoe_status Layer::decode_into(const std::vector<std::pair<int, int>>& jobs, cud
         d.dst = dst + e0;
         d.src_size = ts.block_size[c];
         d.out_size = ts.orig_size[c];
+        d.index = reinterpret_cast<const uint32_t*>(ts.dev + ts.idx_off[c]);
+        d.n_index = ts.idx_n[c];
+        d.seg_bytes = kSegBytes;
         stats.decoded_bytes += (uint64_t)ts.block_size[c] + 3ull * ts.orig_size[c];
         e0 += ts.orig_size[c];
       }
@@ -562,10 +570,25 @@ zmoe_status zmoe_layer_load_expert(zmoe_layer* layer, int expert, int tensor, co
   }
   ts.sm_off = pos;
   ts.numel = numel;
-  ts.bytes = pos + numel;
+  pos = (pos + numel + 15) / 16 * 16;
+  std::vector<std::vector<uint32_t>> idx(n_chunks);
+  for (int c = 0; c < n_chunks; ++c) {
+    const int cap = (int)((original_sizes[c] + zmoe::kSegBytes - 1) / zmoe::kSegBytes) + 1;
+    idx[c].assign(2 * (size_t)cap, 0);
+    const int n = zmoe_lz4_build_index(blocks[c], block_sizes[c], original_sizes[c], zmoe::kSegBytes,
+                                       idx[c].data(), cap);
+    ZMOE_CHECK_ARG(n >= 1, "load_expert: block %d of expert %d tensor %d is not a valid LZ4 block (%d)", c,
+                   expert, tensor, n);
+    idx[c].resize(2 * (size_t)n);
+    ts.idx_off.push_back(pos);
+    ts.idx_n.push_back((uint32_t)n);
+    pos += (idx[c].size() * 4 + 15) / 16 * 16;
+  }
+  ts.bytes = pos;
   std::vector<uint8_t> host(ts.bytes, 0);
   for (int c = 0; c < n_chunks; ++c) memcpy(host.data() + ts.block_off[c], blocks[c], block_sizes[c]);
   memcpy(host.data() + ts.sm_off, sm, numel);
+  for (int c = 0; c < n_chunks; ++c) memcpy(host.data() + ts.idx_off[c], idx[c].data(), idx[c].size() * 4);
   zmoe_status st = upload((void**)&ts.dev, host.data(), ts.bytes);
   if (st != ZMOE_OK) return st;
   auto& slot = L->store[expert][tensor];

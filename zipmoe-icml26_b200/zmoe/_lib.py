@@ -19,8 +19,8 @@ c_float = ctypes.c_float
 
 
 class ZmoeChunk(ctypes.Structure):
-    _fields_ = [("src", c_void_p), ("sm", c_void_p), ("dst", c_void_p),
-                ("src_size", c_u32), ("out_size", c_u32)]
+    _fields_ = [("src", c_void_p), ("sm", c_void_p), ("dst", c_void_p), ("index", c_void_p),
+                ("src_size", c_u32), ("out_size", c_u32), ("n_index", c_u32), ("seg_bytes", c_u32)]
 
 
 class RouterArgs(ctypes.Structure):
@@ -77,6 +77,7 @@ SIGNATURES = {
     "zmoe_split_planes": (c_int, [c_void_p, ctypes.c_uint64, c_void_p, c_void_p]),
     "zmoe_lz4_compress_bound": (c_int, [c_int]),
     "zmoe_lz4_compress": (c_int, [c_void_p, c_int, c_void_p, c_int, c_int, c_int]),
+    "zmoe_lz4_build_index": (c_int, [c_void_p, c_u32, c_u32, c_u32, c_void_p, c_int]),
     "zmoe_layer_create": (c_int, [ctypes.POINTER(LayerConfig), ctypes.POINTER(c_void_p)]),
     "zmoe_layer_destroy": (c_int, [c_void_p]),
     "zmoe_layer_set_router": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p]),

@@ -8,6 +8,7 @@ from __future__ import annotations
 import ctypes
 from typing import List, Optional, Sequence, Tuple
 
+import numpy as np
 import torch
 
 from . import _lib
@@ -45,13 +46,31 @@ def tensor_recover(exp: torch.Tensor, sm: torch.Tensor, out: Optional[torch.Tens
     return out
 
 
-def chunk_table(descs: Sequence[Tuple[int, int, int, int, int]], device) -> torch.Tensor:
-    """Pack (src, sm, dst, src_size, out_size) tuples into a device descriptor array."""
+SEG_BYTES = 2048
+
+
+def chunk_table(descs: Sequence[tuple], device) -> torch.Tensor:
+    """Pack (src, sm, dst, src_size, out_size[, index, n_index, seg_bytes]) tuples
+    into a device descriptor array."""
     arr = (ZmoeChunk * max(len(descs), 1))()
-    for i, (src, sm, dst, csz, osz) in enumerate(descs):
-        arr[i] = ZmoeChunk(src, sm, dst, csz, osz)
-    raw = torch.frombuffer(bytearray(bytes(arr)), dtype=torch.uint8)[: 32 * len(descs)]
+    for i, d in enumerate(descs):
+        src, sm, dst, csz, osz = d[:5]
+        idx, nidx, seg = d[5:8] if len(d) >= 8 else (None, 0, 0)
+        arr[i] = ZmoeChunk(src, sm, dst, idx, csz, osz, nidx, seg)
+    size = ctypes.sizeof(ZmoeChunk)
+    raw = torch.frombuffer(bytearray(bytes(arr)), dtype=torch.uint8)[: size * len(descs)]
     return raw.to(device)
+
+
+def build_index(block: bytes, out_size: int, seg_bytes: int = SEG_BYTES) -> np.ndarray:
+    """Segment index of one LZ4 block (uint32 [n, 2])."""
+    n = max(1, (out_size + seg_bytes - 1) // seg_bytes)
+    ent = np.zeros((n, 2), np.uint32)
+    buf = ctypes.create_string_buffer(bytes(block), max(len(block), 1))
+    rc = lib.zmoe_lz4_build_index(ctypes.addressof(buf), len(block), out_size, seg_bytes, ent.ctypes.data, n)
+    if rc < 0:
+        raise ValueError(f"zmoe_lz4_build_index failed ({rc})")
+    return ent[:rc]
 
 
 def decode_chunks(table: torch.Tensor, n: int, status: Optional[torch.Tensor] = None) -> torch.Tensor:
@@ -66,10 +85,12 @@ class CompressedTensor:
     """One expert matrix in HBM in the reference's storage form: LZ4 exponent
     chunks (concatenated, 16-byte aligned) and the raw sign+mantissa plane."""
 
-    def __init__(self, blocks: Sequence[bytes], original_sizes: Sequence[int], sm: bytes, device="cuda"):
+    def __init__(self, blocks: Sequence[bytes], original_sizes: Sequence[int], sm: bytes, device="cuda",
+                 seg_bytes: int = SEG_BYTES, indexed: bool = True):
         self.original_sizes = [int(o) for o in original_sizes]
         self.compressed_sizes = [len(b) for b in blocks]
         self.numel = sum(self.original_sizes)
+        self.seg_bytes = seg_bytes
         offs, pos = [], 0
         for b in blocks:
             offs.append(pos)
@@ -80,15 +101,25 @@ class CompressedTensor:
         self.block_offsets = offs
         self.blocks = torch.frombuffer(buf, dtype=torch.uint8).to(device)
         self.sm = torch.frombuffer(bytearray(sm), dtype=torch.uint8).to(device)
+        self.indexes = None
+        if indexed:
+            idx = [build_index(b, o, seg_bytes) for b, o in zip(blocks, self.original_sizes)]
+            self.index_rows = [len(i) for i in idx]
+            flat = np.concatenate(idx) if idx else np.zeros((1, 2), np.uint32)
+            self.indexes = torch.from_numpy(flat.astype(np.int32)).to(device)
+            self.index_offsets = np.concatenate([[0], np.cumsum(self.index_rows)]).tolist()
 
     @property
     def device_bytes(self) -> int:
-        return self.blocks.numel() + self.sm.numel()
+        return self.blocks.numel() + self.sm.numel() + (self.indexes.numel() * 4 if self.indexes is not None else 0)
 
-    def descs(self, dst: torch.Tensor) -> List[Tuple[int, int, int, int, int]]:
+    def descs(self, dst: torch.Tensor) -> List[tuple]:
         out, e0 = [], 0
-        for o, c, n in zip(self.block_offsets, self.compressed_sizes, self.original_sizes):
-            out.append((self.blocks.data_ptr() + o, self.sm.data_ptr() + e0, dst.data_ptr() + 2 * e0, c, n))
+        for i, (o, c, n) in enumerate(zip(self.block_offsets, self.compressed_sizes, self.original_sizes)):
+            d = (self.blocks.data_ptr() + o, self.sm.data_ptr() + e0, dst.data_ptr() + 2 * e0, c, n)
+            if self.indexes is not None:
+                d = d + (self.indexes.data_ptr() + 8 * self.index_offsets[i], self.index_rows[i], self.seg_bytes)
+            out.append(d)
             e0 += n
         return out
 
