@@ -130,7 +130,10 @@ def test_decode_reports_malformed_blocks_without_trapping():
     sm_pad = np.concatenate([sm, np.zeros(100, np.uint8)])
     expect = {"zero_off": 1, "far_off": 1, "short": 3}
     for name, (b, o) in cases.items():
-        ct = ops.CompressedTensor([b], [o], sm_pad[:o].tobytes())
+        if name != "short":
+            with pytest.raises(ValueError):       # the host index walk rejects it
+                ops.build_index(b, o)
+        ct = ops.CompressedTensor([b], [o], sm_pad[:o].tobytes(), indexed=False)
         _, st = ct.decode()
         torch.cuda.synchronize()
         code = int(st.cpu()[0])
