@@ -166,6 +166,19 @@ typedef struct zmoe_ffn_args {
 
 zmoe_status zmoe_expert_ffn(const zmoe_ffn_args* a, zmoe_stream_t stream);
 
+/* Same computation for callers that cannot allocate device memory (no
+ * counterpart in the reference).  Runtimes that own all device memory through
+ * their own pool, or that must not call cudaMalloc/cudaFree mid-step (a
+ * cudaFree synchronises the device), cannot provide the h scratch buffer;
+ * here a->h is ignored and the intermediate lives in a file-scope device array
+ * of 16 Mi BF16 elements (32 MiB, held on every GPU that loads the library
+ * until exit).  rows_total * I above that is rejected (ZMOE_EUNSUPPORTED).
+ * Calls no cudaMalloc, cudaFree or allocating routine.  All calls share the
+ * array, which keeps the last call's contents; calls that overlap on the GPU
+ * race and must be serialised.  The first call on a device looks up the
+ * array's address with that device current; make it before any stream capture. */
+zmoe_status zmoe_expert_ffn_noalloc(const zmoe_ffn_args* a, zmoe_stream_t stream);
+
 /* --------------------------------------------------------------------------
  * Combine: gate-weighted sum of the expert rows plus the shared expert.
  * Replaces the Python combine loops customized/qwen.py:89-100,

@@ -73,6 +73,7 @@ SIGNATURES = {
     "zmoe_router": (c_int, [ctypes.POINTER(RouterArgs), c_void_p]),
     "zmoe_permute": (c_int, [ctypes.POINTER(PermuteArgs), c_void_p]),
     "zmoe_expert_ffn": (c_int, [ctypes.POINTER(FfnArgs), c_void_p]),
+    "zmoe_expert_ffn_noalloc": (c_int, [ctypes.POINTER(FfnArgs), c_void_p]),
     "zmoe_combine": (c_int, [ctypes.POINTER(CombineArgs), c_void_p]),
     "zmoe_split_planes": (c_int, [c_void_p, ctypes.c_uint64, c_void_p, c_void_p]),
     "zmoe_lz4_compress_bound": (c_int, [c_int]),
