@@ -363,13 +363,8 @@ zmoe_status Layer::forward(const uint16_t* x, int T, uint16_t* out, cudaStream_t
   // shared expert first: it needs no decoded weights
   if (cfg.shared_inter > 0 && w_shared[0]) {
     zmoe_ffn_args fa{};
-    const uint16_t* tab[3] = {w_shared[0], w_shared[1], w_shared[2]};
-    // the table lives at the end of the wave tables
-    const uint16_t** shtab = wtab_host + (size_t)(max_waves * E - 1) * 3;
-    shtab[0] = tab[0]; shtab[1] = tab[1]; shtab[2] = tab[2];
-    const uint16_t** shtab_dev = wtab_dev + (size_t)(max_waves * E - 1) * 3;
-    ZMOE_CUDA_RET(cudaMemcpyAsync(shtab_dev, shtab, sizeof(void*) * 3, cudaMemcpyHostToDevice, s));
-    fa.x = x; fa.w = shtab_dev; fa.offsets = nullptr; fa.G = 1; fa.rows_total = T; fa.H = H;
+    const uint16_t* tab[3] = {w_shared[0], w_shared[1], w_shared[2]};   // host table
+    fa.x = x; fa.w = tab; fa.offsets = nullptr; fa.G = 1; fa.rows_total = T; fa.H = H;
     fa.I = cfg.shared_inter; fa.kind = 0; fa.h = hsh; fa.y = ysh;
     if ((st = launch_expert_ffn(&fa, s)) != ZMOE_OK) return st;
     stats.launches += 2;
@@ -447,10 +442,8 @@ zmoe_status Layer::forward(const uint16_t* x, int T, uint16_t* out, cudaStream_t
         tab[e * 3 + 1] = tensors == 3 ? slot_ptr(slot, 1) : nullptr;
         tab[e * 3 + 2] = slot_ptr(slot, tensors - 1);
       }
-      const uint16_t** tdev = wtab_dev + (size_t)wave * E * 3;
-      ZMOE_CUDA_RET(cudaMemcpyAsync(tdev, tab, sizeof(void*) * E * 3, cudaMemcpyHostToDevice, s));
       zmoe_ffn_args fa{};
-      fa.x = xp; fa.w = tdev; fa.offsets = offsets; fa.G = E; fa.rows_total = T * k; fa.H = H;
+      fa.x = xp; fa.w = tab; fa.offsets = offsets; fa.G = E; fa.rows_total = T * k; fa.H = H;
       fa.I = cfg.inter; fa.kind = cfg.kind; fa.h = h; fa.y = y;
       int ev = -1;
       if (timing) {

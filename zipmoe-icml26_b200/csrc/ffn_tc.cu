@@ -1,0 +1,477 @@
+// Grouped expert FFN on the 5th-generation tensor cores (tcgen05 + TMEM), fed by TMA.
+//
+// Replaces DeepSeekMoEDenseActDense::forward / SwitchTransformersDenseActDense::forward
+// (csrc/dispatcher/expert_module.cpp:39-50, :67-78), which the reference runs one
+// expert at a time with three libtorch matmuls and a stream synchronisation
+// around each expert (csrc/dispatcher/expert_dispatcher.cpp:354-427).
+//
+// Two persistent launches per layer:
+//   up:   h[t, i] = bf16( silu(sum_k Wg[i,k] x[t,k]) * sum_k Wu[i,k] x[t,k] )   (or relu(Wi x))
+//   down: y[t, j] = sum_i Wd[j,i] h[t,i]                                        (fp32)
+// Both are "swap-AB" GEMMs: the weight rows are the MMA M dimension (128 per
+// tile), the group's tokens are the N dimension (up to 128 per tile), so a
+// group with a handful of tokens still streams its weights at full width.
+//
+// CTA = 6 warps: warp 0 issues TMA (one lane), warp 1 allocates TMEM and issues
+// tcgen05.mma (one lane), warps 2-5 run the epilogue from TMEM (warp w reads
+// TMEM lanes 32*(w%4)..+31).  Operands land in shared memory through 2D tensor
+// maps with 128-byte swizzle (K-major, 64 bf16 per row); a 4-stage (up) or
+// 6-stage (down) mbarrier ring overlaps loads with MMAs.  Accumulators: fp32
+// in TMEM (gate at columns 0..127, up at 128..255).
+//
+// Every mbarrier wait is bounded; on a timeout the CTA records an error code
+// in zmoe's device error word, waits (bounded) for the loads it issued,
+// releases its TMEM and returns.
+#include <cuda.h>
+
+#include <mutex>
+
+#include "common.cuh"
+
+namespace zmoe {
+
+__device__ int32_t g_kernel_error = 0;
+
+namespace tc {
+
+constexpr int BM = 128;               // weight rows per tile (MMA M)
+constexpr int BN = 128;               // tokens per tile (max MMA N)
+constexpr int BK = 64;                // bf16 per 128-byte swizzle row
+constexpr int kTileBytes = BM * BK * 2;   // 16 KiB (A tile; B tile has the same size)
+constexpr int kMaxMaps = 128;
+constexpr int kMaxGroups = 128;
+constexpr int kThreads = 192;
+constexpr long long kWaitCycles = 4000000000LL;   // about 2 s at 1.9 GHz
+
+struct __align__(64) Params {
+  CUtensorMap amap[kMaxMaps];         // weight (A) maps: MODE 0 uses 2 per group
+  CUtensorMap bmap;                   // activation (B) map over [rows_total, K]
+  const int32_t* offsets;             // [G_all + 1] device, or nullptr: one group of rows_total
+  void* out;                          // h (bf16) or y (fp32), row-major [rows_total, n_out]
+  int g_begin, g_count;               // groups of this launch (offset into offsets)
+  int rows_total, K, n_out;           // n_out = weight rows of one matrix (I or H)
+  uint8_t present[kMaxGroups];        // 0: group not in this launch (no weights)
+};
+
+// ---------------------------------------------------------------------------
+// PTX helpers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait; false on timeout (error recorded).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int32_t* cta_err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (*(volatile int32_t*)cta_err) return false;
+    if (clock64() - t0 > kWaitCycles) {
+      atomicCAS(cta_err, 0, 1);
+      atomicCAS(&g_kernel_error, 0, 1);
+      return false;
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                       uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+      ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// K-major operand tile in 128-byte-swizzled layout: rows of 128 bytes, 8-row
+// atoms of 1024 bytes (stride-byte offset), version 1, layout SWIZZLE_128B.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr) {
+  return (uint64_t)((saddr & 0x3FFFFu) >> 4) | (1ull << 16) | ((uint64_t)(1024 >> 4) << 32) | (1ull << 46) |
+         (2ull << 61);
+}
+
+// kind::f16 instruction descriptor: fp32 accumulate, bf16 A and B, both K-major, M = 128.
+__device__ __forceinline__ uint32_t instr_desc(int n) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
+
+__device__ __forceinline__ float silu(float g) { return g / (1.0f + __expf(-g)); }
+
+// ---------------------------------------------------------------------------
+// kernel
+// ---------------------------------------------------------------------------
+template <int MODE>  // 0: SwiGLU up (gate+up maps), 1: ReLU up, 2: down (fp32 out)
+__global__ void __launch_bounds__(kThreads, 1) ffn_tc_kernel(const __grid_constant__ Params p) {
+  constexpr int NA = MODE == 0 ? 2 : 1;
+  constexpr int STAGES = MODE == 0 ? 4 : 6;
+  constexpr int kStageBytes = (NA + 1) * kTileBytes;
+  constexpr uint32_t kTmemCols = MODE == 0 ? 256 : 128;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * kStageBytes);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tmem_full = empty + STAGES;
+  uint64_t* tmem_empty = tmem_full + 1;
+  uint64_t* drain = tmem_empty + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  int32_t* cta_err = reinterpret_cast<int32_t*>(tmem_slot + 1);
+  int32_t* prefix = cta_err + 1;              // [g_count + 1] tile prefix
+  int32_t* ntiles = prefix + kMaxGroups + 1;  // [g_count] n tiles per group
+  int32_t* row0 = ntiles + kMaxGroups;        // [g_count] first row of each group
+  int32_t* rows = row0 + kMaxGroups;          // [g_count] rows of each group
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int MT = (p.n_out + BM - 1) / BM;     // partial tiles read zeros past the matrix edge
+  const int KS = (p.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(tmem_full, 1);
+    mbar_init(tmem_empty, 4);
+    mbar_init(drain, 1);
+    *cta_err = 0;
+    int acc = 0;
+    for (int g = 0; g < p.g_count; ++g) {
+      int r0 = 0, rn = p.rows_total;
+      if (p.offsets) {
+        r0 = p.offsets[p.g_begin + g];
+        rn = p.offsets[p.g_begin + g + 1] - r0;
+      }
+      const int nt = (p.present[g] && rn > 0) ? (rn + BN - 1) / BN : 0;
+      prefix[g] = acc;
+      ntiles[g] = nt;
+      row0[g] = r0;
+      rows[g] = rn;
+      acc += nt * MT;
+    }
+    prefix[p.g_count] = acc;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int total = prefix[p.g_count];
+
+  auto unit_of = [&](int u, int& g, int& mt, int& nt) {
+    int lo = 0, hi = p.g_count - 1;            // last g with prefix[g] <= u
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (prefix[mid] <= u) lo = mid; else hi = mid - 1;
+    }
+    g = lo;
+    const int local = u - prefix[g];
+    mt = local / ntiles[g];
+    nt = local % ntiles[g];
+  };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t armed[8] = {0, 0, 0, 0, 0, 0, 0, 0};   // bit: stage armed in phase
+      bool ok = true;
+      for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
+        int g, mt, nt;
+        unit_of(u, g, mt, nt);
+        const int arow = mt * BM;
+        const int brow = row0[g] + nt * BN;
+        const int m0 = MODE == 0 ? 2 * g : g;
+        for (int ks = 0; ks < KS; ++ks) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, cta_err)) { ok = false; break; }
+          uint8_t* st = smem + stage * kStageBytes;
+          mbar_expect_tx(&full[stage], kStageBytes);
+          armed[stage] = phase + 1;
+          tma_load_2d(st, &p.amap[m0], ks * BK, arow, &full[stage]);
+          if (NA == 2) tma_load_2d(st + kTileBytes, &p.amap[m0 + 1], ks * BK, arow, &full[stage]);
+          tma_load_2d(st + NA * kTileBytes, &p.bmap, ks * BK, brow, &full[stage]);
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+      }
+      if (!ok) {
+        // drain: wait (bounded) for every load this lane issued
+        for (int s = 0; s < STAGES; ++s)
+          if (armed[s]) {
+            const long long t0 = clock64();
+            while (!mbar_try_wait(&full[s], armed[s] - 1) && clock64() - t0 < kWaitCycles) {
+            }
+          }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
+        int g, mt, nt;
+        unit_of(u, g, mt, nt);
+        const int valid = min(BN, rows[g] - nt * BN);
+        const int n = max(16, (valid + 15) & ~15);
+        const uint32_t idesc = instr_desc(n);
+        if (!mbar_wait(tmem_empty, acc_phase ^ 1u, cta_err)) break;
+        tc_fence_after();
+        for (int ks = 0; ks < KS; ++ks) {
+          if (!mbar_wait(&full[stage], phase, cta_err)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * kStageBytes);
+          const uint64_t da0 = smem_desc(sa);
+          const uint64_t da1 = smem_desc(sa + kTileBytes);
+          const uint64_t db = smem_desc(sa + NA * kTileBytes);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint32_t accf = (ks | kk) != 0;
+            tc_mma(tmem, da0 + 2 * kk, db + 2 * kk, idesc, accf);
+            if (NA == 2) tc_mma(tmem + 128, da1 + 2 * kk, db + 2 * kk, idesc, accf);
+          }
+          tc_commit(&empty[stage]);
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+        tc_commit(tmem_full);
+        acc_phase ^= 1u;
+      }
+      if (!ok || *(volatile int32_t*)cta_err) {
+        // error path: wait (bounded) until every MMA issued here has finished
+        tc_commit(drain);
+        const long long t0 = clock64();
+        while (!mbar_try_wait(drain, 0) && clock64() - t0 < kWaitCycles) {
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;                     // TMEM lane quarter of this warp
+    uint32_t acc_phase = 0;
+    for (int u = blockIdx.x; u < total; u += gridDim.x) {
+      int g, mt, nt;
+      unit_of(u, g, mt, nt);
+      const int valid = min(BN, rows[g] - nt * BN);
+      const int n = max(16, (valid + 15) & ~15);
+      if (!mbar_wait(tmem_full, acc_phase, cta_err)) break;
+      tc_fence_after();
+      const int feat = mt * BM + q * 32 + lane;   // output feature of this thread
+      const size_t rbase = (size_t)(row0[g] + nt * BN);
+      const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16);
+      for (int c0 = 0; c0 < n; c0 += 16) {
+        uint32_t a[16], b[16];
+        tmem_ld16(taddr + c0, a);
+        if (MODE == 0) tmem_ld16(taddr + 128 + c0, b);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int t = c0 + j;
+          if (t >= valid || feat >= p.n_out) break;
+          const size_t o = (rbase + t) * (size_t)p.n_out + feat;
+          const float v = __uint_as_float(a[j]);
+          if (MODE == 0) {
+            static_cast<uint16_t*>(p.out)[o] = f32_to_bf16_bits(silu(v) * __uint_as_float(b[j]));
+          } else if (MODE == 1) {
+            static_cast<uint16_t*>(p.out)[o] = f32_to_bf16_bits(fmaxf(v, 0.0f));
+          } else {
+            static_cast<float*>(p.out)[o] = v;
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tmem_empty);
+      acc_phase ^= 1u;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+  }
+}
+
+template <int MODE>
+constexpr int smem_bytes() {
+  constexpr int NA = MODE == 0 ? 2 : 1;
+  constexpr int STAGES = MODE == 0 ? 4 : 6;
+  return 1024 + STAGES * (NA + 1) * kTileBytes + 2 * STAGES * 8 + 24 + 8 + 4 * (4 * kMaxGroups + 2);
+}
+
+// ---------------------------------------------------------------------------
+// host
+// ---------------------------------------------------------------------------
+typedef CUresult (*EncodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled encoder() {
+  static EncodeTiled fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiled>(p);
+  });
+  return fn;
+}
+
+// 2D bf16 map over a row-major [rows, cols] matrix; box = BK columns x box_rows rows.
+zmoe_status make_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+  EncodeTiled enc = encoder();
+  if (!enc) {
+    set_error("cuTensorMapEncodeTiled is not available");
+    return ZMOE_ECUDA;
+  }
+  ZMOE_CHECK_ARG(((uintptr_t)base & 15) == 0, "tensor map base %p is not 16-byte aligned", base);
+  ZMOE_CHECK_ARG((cols * 2) % 16 == 0, "row pitch %llu bytes is not a multiple of 16", (unsigned long long)cols * 2);
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols * 2};
+  cuuint32_t box[2] = {(cuuint32_t)BK, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled failed (%d) for %llux%llu at %p", (int)r, (unsigned long long)rows,
+              (unsigned long long)cols, base);
+    return ZMOE_ECUDA;
+  }
+  return ZMOE_OK;
+}
+
+template <int MODE>
+zmoe_status launch_mode(const zmoe_ffn_args* a, const uint16_t* act, int K, int n_out, void* out,
+                        cudaStream_t stream) {
+  const int per = MODE == 0 ? 2 : 1;
+  const int gmax = kMaxMaps / per < kMaxGroups ? kMaxMaps / per : kMaxGroups;
+  static Params p;                            // 17 KB: too large for the stack frame of a host thread loop
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lock(mu);
+  const int smem = smem_bytes<MODE>();
+  ZMOE_CUDA_RET(cudaFuncSetAttribute(ffn_tc_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  int dev = 0, sms = kNumSMs;
+  ZMOE_CUDA_RET(cudaGetDevice(&dev));
+  ZMOE_CUDA_RET(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  for (int g0 = 0; g0 < a->G; g0 += gmax) {
+    const int gc = a->G - g0 < gmax ? a->G - g0 : gmax;
+    memset(&p, 0, sizeof(p));
+    int any = 0;
+    for (int g = 0; g < gc; ++g) {
+      const uint16_t* const* wg = a->w + 3 * (size_t)(g0 + g);
+      const uint16_t* m0 = MODE == 2 ? wg[2] : wg[0];
+      const uint16_t* m1 = MODE == 0 ? wg[1] : nullptr;
+      if (!m0 || (MODE == 0 && !m1)) continue;
+      zmoe_status st = make_map(&p.amap[per * g], m0, (uint64_t)n_out, (uint64_t)K, BM);
+      if (st == ZMOE_OK && MODE == 0) st = make_map(&p.amap[per * g + 1], m1, (uint64_t)n_out, (uint64_t)K, BM);
+      if (st != ZMOE_OK) return st;
+      p.present[g] = 1;
+      any = 1;
+    }
+    if (!any) continue;
+    zmoe_status st = make_map(&p.bmap, act, (uint64_t)a->rows_total, (uint64_t)K, BN);
+    if (st != ZMOE_OK) return st;
+    p.offsets = a->offsets;
+    p.out = out;
+    p.g_begin = g0;
+    p.g_count = gc;
+    p.rows_total = a->rows_total;
+    p.K = K;
+    p.n_out = n_out;
+    ffn_tc_kernel<MODE><<<sms, kThreads, smem, stream>>>(p);
+    st = launch_status("ffn_tc_kernel");
+    if (st != ZMOE_OK) return st;
+  }
+  return ZMOE_OK;
+}
+
+}  // namespace tc
+
+// a->w is a host array of G*3 device pointers.
+zmoe_status launch_expert_ffn(const zmoe_ffn_args* a, cudaStream_t stream) {
+  ZMOE_CHECK_ARG(a && a->x && a->w && a->h && a->y, "expert_ffn: null pointer");
+  ZMOE_CHECK_ARG(a->G >= 1, "expert_ffn: G must be >= 1");
+  ZMOE_CHECK_ARG(a->kind == 0 || a->kind == 1, "expert_ffn: kind must be 0 (SwiGLU) or 1 (ReLU)");
+  ZMOE_CHECK_ARG(a->H > 0 && a->H % 8 == 0 && a->I > 0 && a->I % 8 == 0,
+                 "expert_ffn: H=%d and I=%d must be positive multiples of 8", a->H, a->I);
+  ZMOE_CHECK_ARG(a->offsets || a->G == 1, "expert_ffn: offsets required for G > 1");
+  if (a->rows_total <= 0) return ZMOE_OK;
+  zmoe_status st = a->kind == 0 ? tc::launch_mode<0>(a, a->x, a->H, a->I, a->h, stream)
+                                : tc::launch_mode<1>(a, a->x, a->H, a->I, a->h, stream);
+  if (st != ZMOE_OK) return st;
+  return tc::launch_mode<2>(a, a->h, a->I, a->H, a->y, stream);
+}
+
+zmoe_status read_kernel_error(int32_t* out, int reset) {
+  ZMOE_CUDA_RET(cudaMemcpyFromSymbol(out, g_kernel_error, sizeof(int32_t)));
+  if (reset) {
+    const int32_t z = 0;
+    ZMOE_CUDA_RET(cudaMemcpyToSymbol(g_kernel_error, &z, sizeof(int32_t)));
+  }
+  return ZMOE_OK;
+}
+
+}  // namespace zmoe

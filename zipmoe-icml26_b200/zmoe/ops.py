@@ -173,13 +173,14 @@ def permute(topk_idx: torch.Tensor, x: Optional[torch.Tensor], E: int, capacity:
     return counts, offsets, row_of, tor, xp
 
 
-def weight_table(mats: Sequence[Sequence[Optional[torch.Tensor]]], device) -> torch.Tensor:
-    """Device array [G*3] of weight pointers from per-group (w0, w1, w2)."""
+def weight_table(mats: Sequence[Sequence[Optional[torch.Tensor]]], device=None) -> torch.Tensor:
+    """Host array [G*3] of device weight pointers from per-group (w0, w1, w2)
+    (the FFN builds one TMA descriptor per matrix on the host)."""
     ptrs = []
     for g in mats:
         g = list(g) + [None] * (3 - len(g))
         ptrs.extend(0 if t is None else t.data_ptr() for t in g)
-    return torch.tensor(ptrs, dtype=torch.int64, device=device)
+    return torch.tensor(ptrs, dtype=torch.int64)
 
 
 def expert_ffn(x: torch.Tensor, wtab: torch.Tensor, offsets: Optional[torch.Tensor], G: int, I: int, kind: int,
