@@ -6,63 +6,117 @@
 // kernel (csrc/kernels/tensor_recover.cu:12-43) reading both planes over
 // zero-copy host memory.
 //
-// One CTA of 16 warps owns one LZ4 block.  A segment index built when the
-// block is loaded (zmoe_lz4_build_index: the first sequence at or after every
-// multiple of seg_bytes of output) lets warp w decode segments w, w+16, ...
-// concurrently.  Inside a segment a warp walks batches of up to 32 sequences:
+// One CTA of 6 warps decodes one LZ4 block.  LZ4HC matches chain back through
+// earlier matches (median offset ~20 KB), so the data dependencies of a block
+// are nearly serial; parsing the token stream is not.  The work is split so
+// that only a cheap gather stays serial:
 //
-//  1. The compressed bytes from the current token are staged in shared memory
-//     with aligned 32-bit loads; each lane computes, for 8 positions, where the
-//     next token would start if one started there.  Pointer doubling over that
-//     table gives lane l the start of sequence l in 5 shared-memory lookups.
-//  2. Each lane decodes its sequence header; a warp scan gives output offsets;
-//     an owner table maps every output byte of the batch to its sequence.
-//  3. A match whose source lies in an earlier segment waits (bounded spin)
-//     until the warp owning that segment has published a frontier past the
-//     source; the warp owning the lowest unfinished segment never waits, so
-//     the CTA always makes progress.
-//  4. Output bytes are spread over the lanes by position (coalesced BF16
-//     stores and sign+mantissa loads).  A literal comes from the staged
-//     window; a match byte k of a copy with offset o reads position
-//     (start - o + k mod o), which resolves overlapping copies directly.
-//     The rare byte whose source is produced in the same batch is written in
-//     a later round once its source is final.
-//  5. Every exponent byte is merged with its sign+mantissa byte and stored as
-//     BF16 in the destination slot; match sources are read back from the slot
-//     through L2 (exponent = bits 7..14).
+//  * 4 parser warps.  A segment index built at load time (zmoe_lz4_build_index:
+//    the first sequence at or after every 1 KiB of output) lets parser p take
+//    segments p, p+4, ...  A parser stages 256 compressed bytes, finds up to 32
+//    token starts at once by pointer doubling over a next-token table, decodes
+//    the headers, and turns a batch of up to 256 output bytes into one 32-bit
+//    descriptor per output byte: a literal value, or the absolute position of
+//    its source byte.  Sources inside the batch itself (short offsets,
+//    overlapping copies) are chased at parse time until they reach a literal
+//    or a byte before the batch, so a descriptor never depends on its batch.
+//    Batches go to a 6-slot queue per parser (one whole segment).
+//  * 1 resolver warp.  It takes the batches in output order and, per byte,
+//    reads either the literal or ring[source & 0xFFFF] from a 64 KiB
+//    shared-memory window of decoded exponents (LZ4 offsets are < 64 KiB),
+//    then writes the batch into the window: one gather + one scatter per
+//    byte, no dependency waits.  A sequence longer than a batch is copied by
+//    the whole warp 32 bytes at a time from its most recent equal byte.
+//  * 1 flusher warp.  It follows the resolver through the window, merges 16
+//    exponent bytes with 16 sign+mantissa bytes (128-bit loads) into BF16 and
+//    stores 32 bytes per lane; the resolver never overwrites a window byte the
+//    flusher has not consumed.
 //
-// Errors (bad offsets, lengths past the block, a block ending short of
-// out_size, a wait that exceeds its bound) set the chunk's status word; the
-// kernel never traps.  Output past out_size is clipped (the
-// targetOutputSize = out_size behaviour of LZ4_decompress_safe_partial).
+// Roles synchronise through counters in shared memory; every wait is bounded
+// and gives up with an error status.  Errors (bad offsets, lengths past the
+// block, a block ending short of out_size) set the chunk's status word; the
+// kernel never traps.  Output past out_size is clipped (the targetOutputSize
+// = out_size behaviour of LZ4_decompress_safe_partial).
 #include "common.cuh"
 
 namespace zmoe {
 namespace {
 
-constexpr int kWarps = 16;
-constexpr uint32_t kWin = 256;          // compressed bytes staged per batch
-constexpr int kLevels = 5;              // jumps of 1, 2, 4, 8, 16 tokens
-constexpr uint32_t kBatchMax = 1024;    // output bytes of one batch (owner table)
-constexpr uint32_t kSpinLimit = 1u << 21;
+constexpr int kParsers = 4;
+constexpr int kWarps = kParsers + 2;          // parsers, resolver, flusher
+constexpr int kResolver = kParsers;           // warp kParsers + 1 is the flusher
+constexpr int kSlots = 6;                     // queue depth per parser (a 1 KiB segment)
+constexpr uint32_t kWin = 256;                // compressed bytes staged per parse step
+constexpr int kLevels = 5;                    // jumps of 1, 2, 4, 8, 16 tokens
+constexpr uint32_t kBatch = 256;              // output bytes of one batch
+constexpr uint32_t kRing = 65536;             // decoded-exponent window
+constexpr uint32_t kRingMask = kRing - 1;
+constexpr uint32_t kLit = 0x80000000u;        // descriptor: literal value in bits 0..7
+constexpr uint32_t kInternal = 0x40000000u;   // descriptor (parse time only): batch-relative source
+constexpr long long kSpinCycles = 2000000000LL;   // ~1 s at 1.9 GHz
 constexpr unsigned kFull = 0xffffffffu;
-constexpr int32_t kTimeout = 5;         // status: a dependency wait ran out
+constexpr int32_t kTimeout = 5;
 
-struct WarpSmem {
-  uint32_t winw[kWin / 4 + 2];          // staged bytes, word aligned at the source
-  uint16_t jump[kLevels][kWin];
-  uint8_t owner[kBatchMax];
-  uint32_t seq_ostart[32], seq_ms[32], seq_lit[32], seq_off[32];
-  uint32_t pend[kBatchMax / 32];
+struct Slot {
+  uint32_t desc[kBatch];
+  uint32_t bs, n, mode, pad;                  // mode 0: descriptors, 1: one long sequence
+  uint32_t l_ll, l_lit, l_ml, l_off;          // long sequence: literal count/source, match length/offset
 };
 
-struct CtaSmem {
-  WarpSmem w[kWarps];
-  uint32_t frontier[kWarps];            // output position final in the warp's current segment
+struct ParserSmem {
+  uint32_t winw[kWin / 4 + 2];
+  uint16_t jump[kLevels][kWin];
+  Slot slot[kSlots];
+};
+
+struct Smem {
+  uint8_t ring[kRing];
+  ParserSmem ps[kParsers];
+  uint32_t q_tail[kParsers];
+  uint32_t q_head[kParsers];
+  uint32_t res_pos;                           // bytes [0, res_pos) resolved into the ring
+  uint32_t flush_pos;                         // bytes [0, flush_pos) consumed by the flusher
   int32_t err;
 };
 
-__device__ __forceinline__ uint32_t vload(const volatile uint32_t* p) { return *p; }
+struct Chunk {
+  const uint8_t* src;
+  const uint8_t* sm;
+  uint16_t* dst;
+  const uint32_t* index;
+  uint32_t src_size, out_size, n_seg;
+  uint32_t rofs;   // ring index of position i is (i + rofs) & kRingMask; makes 16-byte
+                   // groups that the flusher loads aligned both in the ring and in memory
+
+  __device__ __forceinline__ uint32_t ri(uint32_t pos) const { return (pos + rofs) & kRingMask; }
+  __device__ uint32_t seg_out(uint32_t j) const {
+    if (j >= n_seg) return out_size;
+    if (!index) return 0;
+    return min(__ldg(index + 2 * j + 1), out_size);
+  }
+  __device__ uint32_t seg_in(uint32_t j) const { return index ? __ldg(index + 2 * j) : 0; }
+};
+
+__device__ __forceinline__ uint32_t vload(const uint32_t* p) { return *(const volatile uint32_t*)p; }
+__device__ __forceinline__ void vstore(uint32_t* p, uint32_t v) { *(volatile uint32_t*)p = v; }
+__device__ __forceinline__ bool failed(Smem& S) { return *(volatile int32_t*)&S.err != 0; }
+__device__ __forceinline__ void set_err(Smem& S, int32_t code) { atomicCAS(&S.err, 0, code); }
+
+// Spin (bounded) until cond() holds; false on error or timeout.
+template <class F>
+__device__ __forceinline__ bool spin_until(Smem& S, F cond) {
+  if (cond()) return true;
+  const long long t0 = clock64();
+  while (!cond()) {
+    if (failed(S)) return false;
+    if (clock64() - t0 > kSpinCycles) {
+      set_err(S, kTimeout);
+      return false;
+    }
+    __nanosleep(32);
+  }
+  return true;
+}
 
 // Start of the token after a token at window position i, or kWin when the
 // chain cannot continue inside the staged bytes.
@@ -80,7 +134,7 @@ __device__ __forceinline__ uint32_t next_token(const uint8_t* win, uint32_t i, u
     } while (b == 255);
   }
   j += ll;
-  if (j >= rem) return kWin;            // literals reach the block end: last sequence
+  if (j >= rem) return kWin;                  // literals reach the block end: last sequence
   if (j + 2 > avail) return kWin;
   j += 2;
   if ((tok & 15) == 15) {
@@ -93,286 +147,318 @@ __device__ __forceinline__ uint32_t next_token(const uint8_t* win, uint32_t i, u
   return j < kWin ? j : kWin;
 }
 
-__device__ __forceinline__ uint32_t exp_of(const uint16_t* dst, uint32_t pos) {
-  return ((uint32_t)__ldcg(dst + pos) >> 7) & 0xFFu;
-}
-
-struct Chunk {
-  const uint8_t* src;
-  const uint8_t* sm;
-  uint16_t* dst;
-  const uint32_t* index;
-  uint32_t src_size, out_size, n_seg, seg_bytes;
-
-  __device__ uint32_t seg_out(uint32_t j) const {  // output start of segment j
-    return j >= n_seg ? out_size : min(__ldg(index + 2 * j + 1), out_size);
-  }
-  __device__ uint32_t seg_in(uint32_t j) const { return __ldg(index + 2 * j); }
-  // segment holding output position q
-  __device__ uint32_t seg_of(uint32_t q) const {
-    uint32_t j = min(q / seg_bytes, n_seg - 1);
-    while (j > 0 && seg_out(j) > q) --j;
-    return j;
-  }
-};
-
-// Wait until every byte of [a, b) (all before the caller's segment) is final.
-__device__ bool wait_final(CtaSmem& S, const Chunk& c, uint32_t a, uint32_t b) {
-  if (a >= b) return true;
-  uint32_t j = c.seg_of(a);
-  const uint32_t jb = c.seg_of(b - 1);
-  for (; j <= jb; ++j) {
-    const uint32_t need = min(b, c.seg_out(j + 1));
-    const volatile uint32_t* f = &S.frontier[j % kWarps];
-    uint32_t spins = 0;
-    while (vload(f) < need) {
-      if (*(volatile int32_t*)&S.err) return false;
-      if (++spins > kSpinLimit) {
-        atomicCAS(&S.err, 0, kTimeout);
-        return false;
+// ---------------------------------------------------------------------------
+// parser warp
+// ---------------------------------------------------------------------------
+__device__ void parser(Smem& S, const Chunk& c, int p, uint32_t lane) {
+  ParserSmem& P = S.ps[p];
+  const uint8_t* win8 = reinterpret_cast<const uint8_t*>(P.winw);
+  uint32_t tail = 0;
+  for (uint32_t j = p; j < c.n_seg; j += kParsers) {
+    const uint32_t hi = c.seg_out(j + 1);
+    uint32_t op = c.seg_out(j);
+    uint32_t ip = c.seg_in(j);
+    while (op < hi) {
+      if (failed(S)) return;
+      if (ip >= c.src_size) { set_err(S, ZMOE_CHUNK_INPUT_OVERRUN); return; }
+      // ---- stage [ip, ip + kWin) with aligned 32-bit loads ----------------------
+      const uint32_t rem = c.src_size - ip;
+      const uint32_t avail = rem < kWin ? rem : kWin;
+      const uintptr_t beg = reinterpret_cast<uintptr_t>(c.src);
+      const uintptr_t end = beg + c.src_size;
+      const uintptr_t addr = beg + ip;
+      const uint32_t shift = (uint32_t)(addr & 3);
+      for (uint32_t q = lane; q < kWin / 4 + 2; q += 32) {
+        const uintptr_t wa = addr - shift + 4 * q;
+        uint32_t v = 0;
+        if (wa >= beg && wa + 4 <= end) {
+          v = __ldg(reinterpret_cast<const uint32_t*>(wa));
+        } else {
+          for (uint32_t b = 0; b < 4; ++b)
+            if (wa + b >= beg && wa + b < end) v |= (uint32_t)__ldg(reinterpret_cast<const uint8_t*>(wa + b)) << (8 * b);
+        }
+        P.winw[q] = v;
       }
-      __nanosleep(64);
-    }
-  }
-  __threadfence_block();
-  return true;
-}
-
-__device__ __forceinline__ void set_err(CtaSmem& S, int32_t code) { atomicCAS(&S.err, 0, code); }
-
-__device__ __forceinline__ bool cta_failed(CtaSmem& S) { return *(volatile int32_t*)&S.err != 0; }
-
-// Decode one segment [out_lo, out_hi) starting at token position in_lo.
-__device__ void decode_segment(CtaSmem& S, WarpSmem& W, const Chunk& c, uint32_t in_lo, uint32_t out_lo,
-                               uint32_t out_hi, uint32_t lane, int warp) {
-  const uint8_t* win8 = reinterpret_cast<const uint8_t*>(W.winw);
-  uint32_t ip = in_lo, op = out_lo;
-  while (op < out_hi) {
-    if (cta_failed(S)) return;
-    if (ip >= c.src_size) { set_err(S, ZMOE_CHUNK_INPUT_OVERRUN); return; }
-    // ---- stage compressed bytes [ip, ip + kWin) ---------------------------------
-    const uint32_t rem = c.src_size - ip;
-    const uint32_t avail = rem < kWin ? rem : kWin;
-    const uintptr_t addr = reinterpret_cast<uintptr_t>(c.src) + ip;
-    const uint32_t shift = (uint32_t)(addr & 3);
-    const uint32_t* wbase = reinterpret_cast<const uint32_t*>(addr - shift);
-    const uintptr_t beg_addr = reinterpret_cast<uintptr_t>(c.src);
-    const uintptr_t end_addr = beg_addr + c.src_size;
-    for (uint32_t q = lane; q < kWin / 4 + 2; q += 32) {
-      const uintptr_t wa = addr - shift + 4 * q;
-      uint32_t v = 0;
-      if (wa >= beg_addr && wa + 4 <= end_addr) {
-        v = __ldg(wbase + q);
-      } else {
-        for (uint32_t b = 0; b < 4; ++b)
-          if (wa + b >= beg_addr && wa + b < end_addr)
-            v |= (uint32_t)__ldg(reinterpret_cast<const uint8_t*>(wa + b)) << (8 * b);
-      }
-      W.winw[q] = v;
-    }
-    __syncwarp();
-    const uint8_t* win = win8 + shift;
-#pragma unroll
-    for (uint32_t q = 0; q < kWin / 32; ++q) {
-      const uint32_t i = lane * (kWin / 32) + q;
-      W.jump[0][i] = (uint16_t)next_token(win, i, avail, rem);
-    }
-    __syncwarp();
-#pragma unroll
-    for (int k = 0; k + 1 < kLevels; ++k) {
+      __syncwarp();
+      const uint8_t* win = win8 + shift;
 #pragma unroll
       for (uint32_t q = 0; q < kWin / 32; ++q) {
         const uint32_t i = lane * (kWin / 32) + q;
-        const uint32_t v = W.jump[k][i];
-        W.jump[k + 1][i] = v < kWin ? W.jump[k][v] : (uint16_t)kWin;
+        P.jump[0][i] = (uint16_t)next_token(win, i, avail, rem);
       }
       __syncwarp();
-    }
-    uint32_t p = 0;
 #pragma unroll
-    for (int k = 0; k < kLevels; ++k)
-      if ((lane >> k) & 1) p = p < kWin ? W.jump[k][p] : kWin;
-    bool valid = p < avail;
-
-    // ---- sequence header of this lane ----------------------------------------------
-    auto byte_at = [&](uint32_t pos) -> uint32_t {
-      const uint32_t rel = pos - ip;
-      return rel < avail ? (uint32_t)win[rel] : (uint32_t)__ldg(c.src + pos);
-    };
-    uint32_t ll = 0, ml = 0, off = 0, lit_pos = 0, seq_end = 0;
-    int lerr = 0;
-    if (valid) {
-      const uint32_t tok = win[p];
-      uint32_t q = ip + p + 1;
-      ll = tok >> 4;
-      if (ll == 15) {
-        uint32_t b;
-        do {
-          if (q >= c.src_size) { lerr = ZMOE_CHUNK_INPUT_OVERRUN; break; }
-          b = byte_at(q++);
-          ll += b;
-        } while (b == 255 && ll < (1u << 30));
+      for (int k = 0; k + 1 < kLevels; ++k) {
+#pragma unroll
+        for (uint32_t q = 0; q < kWin / 32; ++q) {
+          const uint32_t i = lane * (kWin / 32) + q;
+          const uint32_t v = P.jump[k][i];
+          P.jump[k + 1][i] = v < kWin ? P.jump[k][v] : (uint16_t)kWin;
+        }
+        __syncwarp();
       }
-      lit_pos = q;
-      if (!lerr) {
-        if ((uint64_t)q + ll > c.src_size) {
-          lerr = ZMOE_CHUNK_INPUT_OVERRUN;
-        } else {
-          q += ll;
-          if (q != c.src_size) {
-            if (q + 2 > c.src_size) {
-              lerr = ZMOE_CHUNK_INPUT_OVERRUN;
-            } else {
-              off = byte_at(q) | (byte_at(q + 1) << 8);
-              q += 2;
-              ml = tok & 15;
-              if (ml == 15) {
-                uint32_t b;
-                do {
-                  if (q >= c.src_size) { lerr = ZMOE_CHUNK_INPUT_OVERRUN; break; }
-                  b = byte_at(q++);
-                  ml += b;
-                } while (b == 255 && ml < (1u << 30));
+      uint32_t pp = 0;
+#pragma unroll
+      for (int k = 0; k < kLevels; ++k)
+        if ((lane >> k) & 1) pp = pp < kWin ? P.jump[k][pp] : kWin;
+      bool valid = pp < avail;
+      auto byte_at = [&](uint32_t pos) -> uint32_t {
+        const uint32_t rel = pos - ip;
+        return rel < avail ? (uint32_t)win[rel] : (uint32_t)__ldg(c.src + pos);
+      };
+      // ---- sequence header of this lane --------------------------------------------
+      uint32_t ll = 0, ml = 0, off = 0, lit_pos = 0, seq_end = 0;
+      int lerr = 0;
+      if (valid) {
+        const uint32_t tok = win[pp];
+        uint32_t q = ip + pp + 1;
+        ll = tok >> 4;
+        if (ll == 15) {
+          uint32_t b;
+          do {
+            if (q >= c.src_size) { lerr = ZMOE_CHUNK_INPUT_OVERRUN; break; }
+            b = byte_at(q++);
+            ll += b;
+          } while (b == 255 && ll < (1u << 30));
+        }
+        lit_pos = q;
+        if (!lerr) {
+          if ((uint64_t)q + ll > c.src_size) {
+            lerr = ZMOE_CHUNK_INPUT_OVERRUN;
+          } else {
+            q += ll;
+            if (q != c.src_size) {
+              if (q + 2 > c.src_size) {
+                lerr = ZMOE_CHUNK_INPUT_OVERRUN;
+              } else {
+                off = byte_at(q) | (byte_at(q + 1) << 8);
+                q += 2;
+                ml = tok & 15;
+                if (ml == 15) {
+                  uint32_t b;
+                  do {
+                    if (q >= c.src_size) { lerr = ZMOE_CHUNK_INPUT_OVERRUN; break; }
+                    b = byte_at(q++);
+                    ml += b;
+                  } while (b == 255 && ml < (1u << 30));
+                }
+                ml += 4;
               }
-              ml += 4;
             }
           }
         }
+        seq_end = q;
       }
-      seq_end = q;
-    }
-    // output offsets
-    const uint64_t len = valid ? (uint64_t)ll + ml : 0;
-    uint64_t incl = len;
+      const uint64_t len = valid ? (uint64_t)ll + ml : 0;
+      uint64_t incl = len;
 #pragma unroll
-    for (int d = 1; d < 32; d <<= 1) {
-      const uint64_t v = __shfl_up_sync(kFull, incl, d);
-      if (lane >= (uint32_t)d) incl += v;
-    }
-    const uint64_t ostart = (uint64_t)op + incl - len;
-    valid = valid && ostart < out_hi;                         // sequences of this segment only
-    const uint64_t oend = min(ostart + len, (uint64_t)out_hi); // clip (partial decode target)
-    // a batch holds the leading lanes whose output stays inside kBatchMax
-    const unsigned fit = __ballot_sync(kFull, valid && oend - op <= kBatchMax);
-    const unsigned vmask = __ballot_sync(kFull, valid);
-    int cnt = __popc(vmask);                                   // valid lanes are a prefix
-    int nb = __ffs(~fit) - 1;                                  // leading fitting lanes
-    if (fit == kFull) nb = 32;
-    nb = min(nb, cnt);
-    const bool long_mode = nb == 0;                            // lane 0 alone exceeds kBatchMax
-    const int used = long_mode ? 1 : nb;
-    const bool mine = (int)lane < used;
-    // errors of the lanes that take part
-    const uint64_t ms = ostart + ll;
-    if (mine && !lerr && ml > 0 && ms < oend && (off == 0 || off > ms)) lerr = ZMOE_CHUNK_BAD_OFFSET;
-    const unsigned emask = __ballot_sync(kFull, mine && lerr != 0);
-    if (emask) {
-      set_err(S, __shfl_sync(kFull, lerr, __ffs(emask) - 1));
-      return;
-    }
-    const uint32_t bs = op;
-    const uint32_t be = (uint32_t)__shfl_sync(kFull, oend, used - 1);
-    const uint32_t seg_lo = out_lo;
-
-    // ---- cross-segment sources: wait for their owners ------------------------
-    bool ok = true;
-    if (mine && ml > 0 && ms < oend) {
-      const uint32_t src_lo = (uint32_t)(ms - off);
-      const uint32_t src_hi = (uint32_t)min((uint64_t)src_lo + ml, ms);
-      if (src_lo < seg_lo) ok = wait_final(S, c, src_lo, min(src_hi, seg_lo));
-    }
-    if (__ballot_sync(kFull, !ok)) return;
-
-    if (!long_mode) {
-      // ---- owner table -----------------------------------------------------------
-      if (mine) {
-        const uint32_t a = (uint32_t)(ostart - bs), b = (uint32_t)(oend - bs);
-        for (uint32_t i = a; i < b; ++i) W.owner[i] = (uint8_t)lane;
-        W.seq_ostart[lane] = a;
-        W.seq_ms[lane] = (uint32_t)(ms - bs);
-        W.seq_lit[lane] = lit_pos;
-        W.seq_off[lane] = off;
+      for (int d = 1; d < 32; d <<= 1) {
+        const uint64_t v = __shfl_up_sync(kFull, incl, d);
+        if (lane >= (uint32_t)d) incl += v;
       }
-      __syncwarp();
-      // ---- round 0: every byte whose source is final ----------------------------
-      const uint32_t n = be - bs;
-      const uint32_t ni = (n + 31) / 32;
-      uint32_t pending = 0;
-      for (uint32_t i = 0; i < ni; ++i) {
-        const uint32_t r = lane + 32 * i;
-        if (r >= n) break;
-        const uint32_t sq = W.owner[r];
-        const uint32_t a = W.seq_ostart[sq], m0 = W.seq_ms[sq];
-        uint32_t v;
-        if (r < m0) {
-          v = byte_at(W.seq_lit[sq] + (r - a));
-        } else {
-          const uint32_t o = W.seq_off[sq], k = r - m0;
-          const uint32_t s = bs + m0 - o + (o > k ? k : k % o);
-          if (s >= bs) { pending |= 1u << i; continue; }
-          v = exp_of(c.dst, s);
-        }
-        const uint32_t e = bs + r;
-        c.dst[e] = (uint16_t)recombine(__ldg(c.sm + e), v);
-      }
-      // ---- later rounds: sources produced inside this batch ----------------------
-      if (__ballot_sync(kFull, pending != 0)) {
-        for (uint32_t round = 0; round < n; ++round) {
-          __threadfence_block();
-          __syncwarp();
-          for (uint32_t i = 0; i < ni; ++i) {
-            const unsigned m = __ballot_sync(kFull, (pending >> i) & 1u);
-            if (lane == 0) W.pend[i] = m;
-          }
-          __syncwarp();
-          if (__ballot_sync(kFull, pending != 0) == 0) break;
-          for (uint32_t i = 0; i < ni; ++i) {
-            if (!((pending >> i) & 1u)) continue;
-            const uint32_t r = lane + 32 * i;
-            const uint32_t sq = W.owner[r];
-            const uint32_t m0 = W.seq_ms[sq], o = W.seq_off[sq], k = r - m0;
-            const uint32_t sr = m0 - o + (o > k ? k : k % o);  // batch-relative source
-            if ((W.pend[sr / 32] >> (sr % 32)) & 1u) continue;
-            const uint32_t e = bs + r;
-            c.dst[e] = (uint16_t)recombine(__ldg(c.sm + e), exp_of(c.dst, bs + sr));
-            pending &= ~(1u << i);
+      const uint64_t ostart = (uint64_t)op + incl - len;
+      valid = valid && ostart < hi;
+      const uint64_t oend = min(ostart + len, (uint64_t)hi);
+      const unsigned fit = __ballot_sync(kFull, valid && oend - op <= kBatch);
+      const int cnt = __popc(__ballot_sync(kFull, valid));
+      int nb = fit == kFull ? 32 : __ffs(~fit) - 1;
+      nb = min(nb, cnt);
+      const bool long_mode = nb == 0;
+      const int used = long_mode ? 1 : nb;
+      const bool mine = (int)lane < used;
+      const uint64_t ms = ostart + ll;
+      if (mine && !lerr && ml > 0 && ms < oend && (off == 0 || off > ms)) lerr = ZMOE_CHUNK_BAD_OFFSET;
+      const unsigned emask = __ballot_sync(kFull, mine && lerr != 0);
+      if (emask) { set_err(S, __shfl_sync(kFull, lerr, __ffs(emask) - 1)); return; }
+      const uint32_t be = (uint32_t)__shfl_sync(kFull, oend, used - 1);
+      if (be == op) { set_err(S, ZMOE_CHUNK_SHORT_OUTPUT); return; }   // empty final sequence
+
+      // ---- wait for a free slot --------------------------------------------------
+      if (!spin_until(S, [&] { return tail - vload(&S.q_head[p]) < (uint32_t)kSlots; })) return;
+      Slot& sl = P.slot[tail % kSlots];
+      if (!long_mode) {
+        // one descriptor per output byte of the batch
+        if (mine) {
+          const uint32_t a = (uint32_t)ostart, b = (uint32_t)oend, m0 = (uint32_t)ms;
+          for (uint32_t i = a; i < b; ++i) {
+            uint32_t d;
+            if (i < m0) {
+              d = kLit | byte_at(lit_pos + (i - a));
+            } else {
+              const uint32_t k = i - m0;
+              const uint32_t s = m0 - off + (off > k ? k : k % off);
+              d = s >= op ? (kInternal | (s - op)) : s;
+            }
+            sl.desc[i - op] = d;
           }
         }
-        if (__ballot_sync(kFull, pending != 0)) { set_err(S, kTimeout); return; }
+        __syncwarp();
+        // chase sources produced inside the batch
+        const uint32_t n = be - op;
+        for (uint32_t r = lane; r < n; r += 32) {
+          uint32_t d = sl.desc[r];
+          uint32_t steps = 0;
+          while ((d & kInternal) && steps++ < kBatch) d = *(volatile uint32_t*)&sl.desc[d & ~kInternal];
+          if (d & kInternal) { set_err(S, kTimeout); break; }
+          *(volatile uint32_t*)&sl.desc[r] = d;
+        }
+        if (lane == 0) { sl.mode = 0; }
+      } else if (lane == 0) {
+        sl.mode = 1;
+        sl.l_ll = (uint32_t)min((uint64_t)ll, (uint64_t)(be - op));
+        sl.l_lit = lit_pos;
+        sl.l_ml = be - op - sl.l_ll;
+        sl.l_off = off;
       }
-    } else {
-      // ---- one sequence longer than kBatchMax: the whole warp copies it ---------
-      const uint32_t o0 = (uint32_t)__shfl_sync(kFull, ostart, 0);
-      const uint32_t lit_n = (uint32_t)min((uint64_t)__shfl_sync(kFull, ll, 0), (uint64_t)(be - o0));
-      const uint32_t lp = __shfl_sync(kFull, lit_pos, 0);
-      for (uint32_t i = lane; i < lit_n; i += 32) {
-        const uint32_t e = o0 + i;
-        c.dst[e] = (uint16_t)recombine(__ldg(c.sm + e), byte_at(lp + i));
+      if (lane == 0) {
+        sl.bs = op;
+        sl.n = be - op;
       }
       __threadfence_block();
       __syncwarp();
-      const uint32_t m0 = o0 + lit_n;
-      const uint32_t o = __shfl_sync(kFull, off, 0);
-      for (uint32_t k = lane; m0 + k < be; k += 32) {
-        const uint32_t s = m0 - o + (o > k ? k : k % o);
-        const uint32_t e = m0 + k;
-        c.dst[e] = (uint16_t)recombine(__ldg(c.sm + e), exp_of(c.dst, s));
-      }
+      ++tail;
+      if (lane == 0) vstore(&S.q_tail[p], tail);
+      ip = __shfl_sync(kFull, seq_end, used - 1);
+      op = be;
+      if (op < hi && ip >= c.src_size) { set_err(S, ZMOE_CHUNK_SHORT_OUTPUT); return; }
     }
-    // ---- publish progress, advance -------------------------------------------------
-    __threadfence_block();
-    __syncwarp();
-    if (lane == 0) *(volatile uint32_t*)&S.frontier[warp] = be;
-    ip = __shfl_sync(kFull, seq_end, used - 1);
-    op = be;
-    if (op < out_hi && ip >= c.src_size) { set_err(S, ZMOE_CHUNK_SHORT_OUTPUT); return; }
   }
 }
 
-__global__ void __launch_bounds__(kWarps * 32, 1)
-decode_cta_kernel(const zmoe_chunk* __restrict__ chunks, int n_chunks, int32_t* __restrict__ status) {
+// ---------------------------------------------------------------------------
+// resolver warp
+// ---------------------------------------------------------------------------
+__device__ void resolver(Smem& S, const Chunk& c, uint32_t lane) {
+  uint32_t head[kParsers] = {0, 0, 0, 0};
+  for (uint32_t j = 0; j < c.n_seg; ++j) {
+    const int q = j % kParsers;
+    const uint32_t hi = c.seg_out(j + 1);
+    uint32_t pos = c.seg_out(j);
+    while (pos < hi) {
+      if (!spin_until(S, [&] { return vload(&S.q_tail[q]) != head[q]; })) return;
+      __threadfence_block();
+      Slot& sl = S.ps[q].slot[head[q] % kSlots];
+      const uint32_t bs = sl.bs, n = sl.n, mode = sl.mode;
+      if (bs != pos || n == 0) { set_err(S, kTimeout); return; }
+      if (mode == 0) {
+        if (!spin_until(S, [&] { return vload(&S.flush_pos) + kRing >= bs + n; })) return;
+        uint32_t v[kBatch / 32];
+#pragma unroll
+        for (uint32_t i = 0; i < kBatch / 32; ++i) {
+          const uint32_t r = lane + 32 * i;
+          if (r < n) {
+            const uint32_t d = sl.desc[r];
+            v[i] = (d & kLit) ? (d & 0xFFu) : (uint32_t)S.ring[c.ri(d)];
+          }
+        }
+        __syncwarp();
+#pragma unroll
+        for (uint32_t i = 0; i < kBatch / 32; ++i) {
+          const uint32_t r = lane + 32 * i;
+          if (r < n) S.ring[c.ri(bs + r)] = (uint8_t)v[i];
+        }
+      } else {
+        const uint32_t ll = sl.l_ll, lit = sl.l_lit, ml = sl.l_ml, o = sl.l_off;
+        for (uint32_t k0 = 0; k0 < ll; k0 += 32) {
+          const uint32_t e = bs + k0 + 32;
+          if (!spin_until(S, [&] { return vload(&S.flush_pos) + kRing >= e; })) return;
+          const uint32_t k = k0 + lane;
+          if (k < ll) S.ring[c.ri(bs + k)] = __ldg(c.src + lit + k);
+          __syncwarp();
+        }
+        const uint32_t m0 = bs + ll;
+        for (uint32_t k0 = 0; k0 < ml; k0 += 32) {
+          const uint32_t e = m0 + k0 + 32;
+          if (!spin_until(S, [&] { return vload(&S.flush_pos) + kRing >= e; })) return;
+          const uint32_t k = k0 + lane;
+          uint32_t v = 0;
+          if (k < ml) {
+            const uint32_t m = lane / o + 1;      // most recent equal byte before this step
+            v = S.ring[c.ri(m0 + k - o * m)];
+          }
+          __syncwarp();
+          if (k < ml) S.ring[c.ri(m0 + k)] = (uint8_t)v;
+          __syncwarp();
+        }
+      }
+      __threadfence_block();
+      __syncwarp();
+      ++head[q];
+      if (lane == 0) {
+        vstore(&S.res_pos, bs + n);
+        vstore(&S.q_head[q], head[q]);
+      }
+      pos = bs + n;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// flusher warp
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t pack2(uint32_t e4, uint32_t s4, uint32_t sel) {
+  const uint32_t e2 = __byte_perm(e4, 0, sel);
+  const uint32_t s2 = __byte_perm(s4, 0, sel);
+  return ((s2 & 0x00800080u) << 8) | (e2 << 7) | (s2 & 0x007F007Fu);
+}
+
+__device__ void flusher(Smem& S, const Chunk& c, uint32_t lane) {
+  const uint32_t N = c.out_size;
+  // vector path when the sign+mantissa plane and the output reach 16-byte
+  // boundaries at the same element
+  const uintptr_t sa = reinterpret_cast<uintptr_t>(c.sm), da = reinterpret_cast<uintptr_t>(c.dst);
+  const uint32_t head = (uint32_t)((16 - (sa & 15)) & 15);
+  const bool vec = ((da + 2 * (uintptr_t)head) & 15) == 0;
+  uint32_t e = 0;
+  while (e < N) {
+    uint32_t avail = 0;
+    if (!spin_until(S, [&] { avail = vload(&S.res_pos); return avail > e; })) return;
+    __threadfence_block();
+    uint32_t stop = avail;
+    if (vec) {
+      // scalar up to the first aligned element, then 16 elements per lane
+      const uint32_t h = min(max(head, e), avail);
+      for (uint32_t i = e + lane; i < h; i += 32)
+        c.dst[i] = (uint16_t)recombine(__ldg(c.sm + i), S.ring[c.ri(i)]);
+      uint32_t v0 = h;
+      const uint32_t units = (avail - v0) / 16;
+      for (uint32_t u = lane; u < units; u += 32) {
+        const uint32_t i = v0 + 16 * u;
+        const uint4 ev = *reinterpret_cast<const uint4*>(&S.ring[c.ri(i)]);
+        const uint4 sv = __ldg(reinterpret_cast<const uint4*>(c.sm + i));
+        uint4 lo, hi;
+        lo.x = pack2(ev.x, sv.x, 0x4140); lo.y = pack2(ev.x, sv.x, 0x4342);
+        lo.z = pack2(ev.y, sv.y, 0x4140); lo.w = pack2(ev.y, sv.y, 0x4342);
+        hi.x = pack2(ev.z, sv.z, 0x4140); hi.y = pack2(ev.z, sv.z, 0x4342);
+        hi.z = pack2(ev.w, sv.w, 0x4140); hi.w = pack2(ev.w, sv.w, 0x4342);
+        uint4* o = reinterpret_cast<uint4*>(c.dst + i);
+        o[0] = lo;
+        o[1] = hi;
+      }
+      stop = v0 + 16 * units;
+      if (avail == N) {                         // block done: flush the tail too
+        for (uint32_t i = stop + lane; i < N; i += 32)
+          c.dst[i] = (uint16_t)recombine(__ldg(c.sm + i), S.ring[c.ri(i)]);
+        stop = N;
+      }
+      if (stop <= e) {                          // nothing aligned yet: wait for more
+        if (!spin_until(S, [&] { return vload(&S.res_pos) >= min(N, e + 16 + head); })) return;
+        continue;
+      }
+    } else {
+      for (uint32_t i = e + lane; i < avail; i += 32)
+        c.dst[i] = (uint16_t)recombine(__ldg(c.sm + i), S.ring[c.ri(i)]);
+    }
+    __syncwarp();
+    e = stop;
+    if (lane == 0) vstore(&S.flush_pos, e);
+  }
+}
+
+__global__ void __launch_bounds__(kWarps * 32)
+decode_kernel(const zmoe_chunk* __restrict__ chunks, int n_chunks, int32_t* __restrict__ status) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
-  CtaSmem& S = *reinterpret_cast<CtaSmem*>(smem_raw);
+  Smem& S = *reinterpret_cast<Smem*>(smem_raw);
   const int warp = threadIdx.x >> 5;
   const uint32_t lane = threadIdx.x & 31;
   const zmoe_chunk d = chunks[blockIdx.x];
@@ -380,32 +466,25 @@ decode_cta_kernel(const zmoe_chunk* __restrict__ chunks, int n_chunks, int32_t* 
   c.src = d.src;
   c.sm = d.sm;
   c.dst = d.dst;
-  c.index = d.index;
+  c.index = (d.index && d.n_index > 0) ? d.index : nullptr;
   c.src_size = d.src_size;
   c.out_size = d.out_size;
-  c.seg_bytes = d.seg_bytes ? d.seg_bytes : 0xffffffffu;
-  c.n_seg = d.index ? d.n_index : 1;
-  if (threadIdx.x == 0) {
-    S.err = 0;
-    if (!c.src || !c.sm || !c.dst || c.src_size == 0 || (c.index && c.n_seg == 0) || (c.index && !d.seg_bytes))
-      S.err = ZMOE_CHUNK_BAD_DESC;
+  c.n_seg = c.index ? d.n_index : 1;
+  {
+    const uint32_t head = (uint32_t)((16 - (reinterpret_cast<uintptr_t>(d.sm) & 15)) & 15);
+    c.rofs = (16 - head) & 15;
   }
-  if (threadIdx.x < kWarps) S.frontier[threadIdx.x] = 0;
+  if (threadIdx.x == 0) {
+    S.err = (!c.src || !c.sm || !c.dst || c.src_size == 0) ? ZMOE_CHUNK_BAD_DESC : 0;
+    S.res_pos = 0;
+    S.flush_pos = 0;
+    for (int p = 0; p < kParsers; ++p) { S.q_tail[p] = 0; S.q_head[p] = 0; }
+  }
   __syncthreads();
-  WarpSmem& W = S.w[warp];
   if (!S.err && c.out_size > 0) {
-    for (uint32_t j = warp; j < c.n_seg; j += kWarps) {
-      const uint32_t lo = c.index ? c.seg_out(j) : 0;
-      const uint32_t hi = c.index ? c.seg_out(j + 1) : c.out_size;
-      const uint32_t in = c.index ? c.seg_in(j) : 0;
-      if (lane == 0) *(volatile uint32_t*)&S.frontier[warp] = lo;
-      __syncwarp();
-      if (lo < hi) decode_segment(S, W, c, in, lo, hi, lane, warp);
-      if (cta_failed(S)) break;
-    }
-    __threadfence_block();
-    __syncwarp();
-    if (lane == 0) *(volatile uint32_t*)&S.frontier[warp] = c.out_size;
+    if (warp < kParsers) parser(S, c, warp, lane);
+    else if (warp == kResolver) resolver(S, c, lane);
+    else flusher(S, c, lane);
   }
   __syncthreads();
   if (threadIdx.x == 0) status[blockIdx.x] = S.err;
@@ -415,10 +494,10 @@ decode_cta_kernel(const zmoe_chunk* __restrict__ chunks, int n_chunks, int32_t* 
 
 zmoe_status launch_decode_chunks(const zmoe_chunk* chunks, int n_chunks, int32_t* status, cudaStream_t stream) {
   if (n_chunks <= 0) return ZMOE_OK;
-  const int smem = (int)sizeof(CtaSmem);
-  ZMOE_CUDA_RET(cudaFuncSetAttribute(decode_cta_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-  decode_cta_kernel<<<n_chunks, kWarps * 32, smem, stream>>>(chunks, n_chunks, status);
-  return launch_status("decode_cta_kernel");
+  const int smem = (int)sizeof(Smem);
+  ZMOE_CUDA_RET(cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  decode_kernel<<<n_chunks, kWarps * 32, smem, stream>>>(chunks, n_chunks, status);
+  return launch_status("decode_kernel");
 }
 
 }  // namespace zmoe

@@ -40,7 +40,7 @@ struct TensorStore {
   uint64_t sm_off = 0, numel = 0, bytes = 0;
 };
 
-constexpr uint32_t kSegBytes = 2048;
+constexpr uint32_t kSegBytes = 1024;
 
 template <class T>
 T* dmalloc(size_t n, zmoe_status* st) {

@@ -46,7 +46,7 @@ def tensor_recover(exp: torch.Tensor, sm: torch.Tensor, out: Optional[torch.Tens
     return out
 
 
-SEG_BYTES = 2048
+SEG_BYTES = 1024
 
 
 def chunk_table(descs: Sequence[tuple], device) -> torch.Tensor:
