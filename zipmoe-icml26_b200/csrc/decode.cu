@@ -47,6 +47,7 @@ constexpr int kWarps = kParsers + 2;          // parsers, resolver, flusher
 constexpr int kResolver = kParsers;           // warp kParsers + 1 is the flusher
 constexpr int kSlots = 6;                     // queue depth per parser (a 1 KiB segment)
 constexpr uint32_t kWin = 256;                // compressed bytes staged per parse step
+constexpr uint32_t kInBuf = 1024;             // prefetched compressed bytes per segment buffer
 constexpr int kLevels = 5;                    // jumps of 1, 2, 4, 8, 16 tokens
 constexpr uint32_t kBatch = 256;              // output bytes of one batch
 constexpr uint32_t kRing = 65536;             // decoded-exponent window
@@ -64,6 +65,7 @@ struct Slot {
 };
 
 struct ParserSmem {
+  __align__(16) uint8_t inbuf[2][kInBuf];
   uint32_t winw[kWin / 4 + 2];
   uint16_t jump[kLevels][kWin];
   Slot slot[kSlots];
@@ -150,37 +152,81 @@ __device__ __forceinline__ uint32_t next_token(const uint8_t* win, uint32_t i, u
 // ---------------------------------------------------------------------------
 // parser warp
 // ---------------------------------------------------------------------------
-__device__ void parser(Smem& S, const Chunk& c, int p, uint32_t lane) {
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
+               "l"(src), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+__device__ void parser_body(Smem& S, const Chunk& c, int p, uint32_t lane) {
   ParserSmem& P = S.ps[p];
   const uint8_t* win8 = reinterpret_cast<const uint8_t*>(P.winw);
   uint32_t tail = 0;
-  for (uint32_t j = p; j < c.n_seg; j += kParsers) {
+  // The compressed bytes of this parser's next segment are copied into shared
+  // memory (16-byte cp.async, zero-filled past the block) while it parses the
+  // current one.  Needs a 16-byte aligned block; otherwise bytes come from L1/L2.
+  const bool pf = (reinterpret_cast<uintptr_t>(c.src) & 15) == 0;
+  uint32_t pf_base[2] = {0xffffffffu, 0xffffffffu};
+  auto prefetch = [&](int b, uint32_t j) {
+    if (j >= c.n_seg) {
+      pf_base[b] = 0xffffffffu;
+    } else {
+      const uint32_t base = c.seg_in(j) & ~15u;
+      pf_base[b] = base;
+      for (uint32_t q = lane; q < kInBuf / 16; q += 32) {
+        const uint32_t o = base + 16 * q;
+        const uint32_t nb = o < c.src_size ? min(16u, c.src_size - o) : 0u;
+        cp_async16(&P.inbuf[b][16 * q], nb ? c.src + o : c.src, nb);
+      }
+    }
+    cp_async_commit();
+  };
+  int cur = 0;
+  if (pf) prefetch(0, p);
+  for (uint32_t j = p; j < c.n_seg; j += kParsers, cur ^= 1) {
+    if (pf) {
+      prefetch(cur ^ 1, j + kParsers);
+      cp_async_wait1();
+      __syncwarp();
+    }
+    const uint8_t* buf = P.inbuf[cur];
+    const uint32_t bbase = pf ? pf_base[cur] : 0xffffffffu;
+    const uint32_t bend = pf ? min(bbase + kInBuf, c.src_size) : 0u;
     const uint32_t hi = c.seg_out(j + 1);
     uint32_t op = c.seg_out(j);
     uint32_t ip = c.seg_in(j);
     while (op < hi) {
       if (failed(S)) return;
       if (ip >= c.src_size) { set_err(S, ZMOE_CHUNK_INPUT_OVERRUN); return; }
-      // ---- stage [ip, ip + kWin) with aligned 32-bit loads ----------------------
       const uint32_t rem = c.src_size - ip;
       const uint32_t avail = rem < kWin ? rem : kWin;
-      const uintptr_t beg = reinterpret_cast<uintptr_t>(c.src);
-      const uintptr_t end = beg + c.src_size;
-      const uintptr_t addr = beg + ip;
-      const uint32_t shift = (uint32_t)(addr & 3);
-      for (uint32_t q = lane; q < kWin / 4 + 2; q += 32) {
-        const uintptr_t wa = addr - shift + 4 * q;
-        uint32_t v = 0;
-        if (wa >= beg && wa + 4 <= end) {
-          v = __ldg(reinterpret_cast<const uint32_t*>(wa));
-        } else {
-          for (uint32_t b = 0; b < 4; ++b)
-            if (wa + b >= beg && wa + b < end) v |= (uint32_t)__ldg(reinterpret_cast<const uint8_t*>(wa + b)) << (8 * b);
+      const uint8_t* win;
+      if (pf && ip >= bbase && ip + avail <= bend) {
+        win = buf + (ip - bbase);                  // window already in shared memory
+      } else {
+        // ---- stage [ip, ip + kWin) with aligned 32-bit loads --------------------
+        const uintptr_t beg = reinterpret_cast<uintptr_t>(c.src);
+        const uintptr_t end = beg + c.src_size;
+        const uintptr_t addr = beg + ip;
+        const uint32_t shift = (uint32_t)(addr & 3);
+        for (uint32_t q = lane; q < kWin / 4 + 2; q += 32) {
+          const uintptr_t wa = addr - shift + 4 * q;
+          uint32_t v = 0;
+          if (wa >= beg && wa + 4 <= end) {
+            v = __ldg(reinterpret_cast<const uint32_t*>(wa));
+          } else {
+            for (uint32_t b = 0; b < 4; ++b)
+              if (wa + b >= beg && wa + b < end)
+                v |= (uint32_t)__ldg(reinterpret_cast<const uint8_t*>(wa + b)) << (8 * b);
+          }
+          P.winw[q] = v;
         }
-        P.winw[q] = v;
+        __syncwarp();
+        win = win8 + shift;
       }
-      __syncwarp();
-      const uint8_t* win = win8 + shift;
 #pragma unroll
       for (uint32_t q = 0; q < kWin / 32; ++q) {
         const uint32_t i = lane * (kWin / 32) + q;
@@ -204,7 +250,9 @@ __device__ void parser(Smem& S, const Chunk& c, int p, uint32_t lane) {
       bool valid = pp < avail;
       auto byte_at = [&](uint32_t pos) -> uint32_t {
         const uint32_t rel = pos - ip;
-        return rel < avail ? (uint32_t)win[rel] : (uint32_t)__ldg(c.src + pos);
+        if (rel < avail) return win[rel];
+        if (pos >= bbase && pos < bend) return buf[pos - bbase];
+        return __ldg(c.src + pos);
       };
       // ---- sequence header of this lane --------------------------------------------
       uint32_t ll = 0, ml = 0, off = 0, lit_pos = 0, seq_end = 0;
@@ -325,6 +373,13 @@ __device__ void parser(Smem& S, const Chunk& c, int p, uint32_t lane) {
   }
 }
 
+// Every exit waits for the parser's own asynchronous copies into shared memory.
+__device__ void parser(Smem& S, const Chunk& c, int p, uint32_t lane) {
+  parser_body(S, c, p, lane);
+  cp_async_wait0();
+  __syncwarp();
+}
+
 // ---------------------------------------------------------------------------
 // resolver warp
 // ---------------------------------------------------------------------------
@@ -358,13 +413,21 @@ __device__ void resolver(Smem& S, const Chunk& c, uint32_t lane) {
           if (r < n) S.ring[c.ri(bs + r)] = (uint8_t)v[i];
         }
       } else {
+        // A long sequence can exceed the window: publish progress every 1 KiB so
+        // the flusher keeps draining while the resolver writes.
         const uint32_t ll = sl.l_ll, lit = sl.l_lit, ml = sl.l_ml, o = sl.l_off;
+        auto publish = [&](uint32_t upto) {
+          __threadfence_block();
+          __syncwarp();
+          if (lane == 0) vstore(&S.res_pos, upto);
+        };
         for (uint32_t k0 = 0; k0 < ll; k0 += 32) {
           const uint32_t e = bs + k0 + 32;
           if (!spin_until(S, [&] { return vload(&S.flush_pos) + kRing >= e; })) return;
           const uint32_t k = k0 + lane;
           if (k < ll) S.ring[c.ri(bs + k)] = __ldg(c.src + lit + k);
           __syncwarp();
+          if (((k0 + 32) & 1023) == 0) publish(bs + k0 + 32);
         }
         const uint32_t m0 = bs + ll;
         for (uint32_t k0 = 0; k0 < ml; k0 += 32) {
@@ -379,6 +442,7 @@ __device__ void resolver(Smem& S, const Chunk& c, uint32_t lane) {
           __syncwarp();
           if (k < ml) S.ring[c.ri(m0 + k)] = (uint8_t)v;
           __syncwarp();
+          if (((k0 + 32) & 1023) == 0 && k0 + 32 < ml) publish(m0 + k0 + 32);
         }
       }
       __threadfence_block();
@@ -422,18 +486,29 @@ __device__ void flusher(Smem& S, const Chunk& c, uint32_t lane) {
         c.dst[i] = (uint16_t)recombine(__ldg(c.sm + i), S.ring[c.ri(i)]);
       uint32_t v0 = h;
       const uint32_t units = (avail - v0) / 16;
-      for (uint32_t u = lane; u < units; u += 32) {
-        const uint32_t i = v0 + 16 * u;
-        const uint4 ev = *reinterpret_cast<const uint4*>(&S.ring[c.ri(i)]);
-        const uint4 sv = __ldg(reinterpret_cast<const uint4*>(c.sm + i));
-        uint4 lo, hi;
-        lo.x = pack2(ev.x, sv.x, 0x4140); lo.y = pack2(ev.x, sv.x, 0x4342);
-        lo.z = pack2(ev.y, sv.y, 0x4140); lo.w = pack2(ev.y, sv.y, 0x4342);
-        hi.x = pack2(ev.z, sv.z, 0x4140); hi.y = pack2(ev.z, sv.z, 0x4342);
-        hi.z = pack2(ev.w, sv.w, 0x4140); hi.w = pack2(ev.w, sv.w, 0x4342);
-        uint4* o = reinterpret_cast<uint4*>(c.dst + i);
-        o[0] = lo;
-        o[1] = hi;
+      constexpr int kUnroll = 8;                // sign+mantissa loads in flight per lane
+      for (uint32_t u0 = 0; u0 < units; u0 += 32 * kUnroll) {
+        uint4 sv[kUnroll];
+#pragma unroll
+        for (int q = 0; q < kUnroll; ++q) {
+          const uint32_t u = u0 + lane + 32 * q;
+          if (u < units) sv[q] = __ldg(reinterpret_cast<const uint4*>(c.sm + v0 + 16 * u));
+        }
+#pragma unroll
+        for (int q = 0; q < kUnroll; ++q) {
+          const uint32_t u = u0 + lane + 32 * q;
+          if (u >= units) break;
+          const uint32_t i = v0 + 16 * u;
+          const uint4 ev = *reinterpret_cast<const uint4*>(&S.ring[c.ri(i)]);
+          uint4 lo, hi;
+          lo.x = pack2(ev.x, sv[q].x, 0x4140); lo.y = pack2(ev.x, sv[q].x, 0x4342);
+          lo.z = pack2(ev.y, sv[q].y, 0x4140); lo.w = pack2(ev.y, sv[q].y, 0x4342);
+          hi.x = pack2(ev.z, sv[q].z, 0x4140); hi.y = pack2(ev.z, sv[q].z, 0x4342);
+          hi.z = pack2(ev.w, sv[q].w, 0x4140); hi.w = pack2(ev.w, sv[q].w, 0x4342);
+          uint4* o = reinterpret_cast<uint4*>(c.dst + i);
+          o[0] = lo;
+          o[1] = hi;
+        }
       }
       stop = v0 + 16 * units;
       if (avail == N) {                         // block done: flush the tail too
