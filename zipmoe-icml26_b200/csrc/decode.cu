@@ -13,13 +13,18 @@
 //
 //  * 4 parser warps.  A segment index built at load time (zmoe_lz4_build_index:
 //    the first sequence at or after every 1 KiB of output) lets parser p take
-//    segments p, p+4, ...  A parser stages 256 compressed bytes, finds up to 32
-//    token starts at once by pointer doubling over a next-token table, decodes
-//    the headers, and turns a batch of up to 256 output bytes into one 32-bit
-//    descriptor per output byte: a literal value, or the absolute position of
-//    its source byte.  Sources inside the batch itself (short offsets,
-//    overlapping copies) are chased at parse time until they reach a literal
-//    or a byte before the batch, so a descriptor never depends on its batch.
+//    segments p, p+4, ...  A parser looks at 255 compressed bytes (prefetched
+//    into shared memory with cp.async), builds a next-token table in
+//    registers (8 positions per lane, packed bytes) and finds up to 32 token
+//    starts at once by pointer doubling with warp shuffles; it decodes the
+//    headers and turns a batch of up to 256 output bytes into one 32-bit
+//    descriptor per output byte — a literal value, or the absolute position
+//    of its source byte — with bytes spread over lanes by position (owner
+//    sequence from a bitmap of sequence starts).  Sources inside the batch
+//    itself (short offsets, overlapping copies) are chased at parse time until
+//    they reach a literal or a byte before the batch, so a descriptor never
+//    depends on its batch.  All of this keeps shared-memory traffic low: the
+//    decoder's limit is shared-memory wavefronts, not HBM.
 //    Batches go to a 6-slot queue per parser (one whole segment).
 //  * 1 resolver warp.  It takes the batches in output order and, per byte,
 //    reads either the literal or ring[source & 0xFFFF] from a 64 KiB
@@ -49,6 +54,7 @@ constexpr int kSlots = 6;                     // queue depth per parser (a 1 KiB
 constexpr uint32_t kWin = 256;                // compressed bytes staged per parse step
 constexpr uint32_t kInBuf = 1024;             // prefetched compressed bytes per segment buffer
 constexpr int kLevels = 5;                    // jumps of 1, 2, 4, 8, 16 tokens
+constexpr uint32_t kStop = 255;               // next-token entry: chain stops (window positions 0..254)
 constexpr uint32_t kBatch = 256;              // output bytes of one batch
 constexpr uint32_t kRing = 65536;             // decoded-exponent window
 constexpr uint32_t kRingMask = kRing - 1;
@@ -67,7 +73,6 @@ struct Slot {
 struct ParserSmem {
   __align__(16) uint8_t inbuf[2][kInBuf];
   uint32_t winw[kWin / 4 + 2];
-  uint16_t jump[kLevels][kWin];
   Slot slot[kSlots];
 };
 
@@ -202,9 +207,9 @@ __device__ void parser_body(Smem& S, const Chunk& c, int p, uint32_t lane) {
       if (failed(S)) return;
       if (ip >= c.src_size) { set_err(S, ZMOE_CHUNK_INPUT_OVERRUN); return; }
       const uint32_t rem = c.src_size - ip;
-      const uint32_t avail = rem < kWin ? rem : kWin;
+      const uint32_t avail = rem < kStop ? rem : kStop;
       const uint8_t* win;
-      if (pf && ip >= bbase && ip + avail <= bend) {
+      if (pf && ip >= bbase && ip + avail <= bend && ip - bbase + kWin + 8 <= kInBuf) {
         win = buf + (ip - bbase);                  // window already in shared memory
       } else {
         // ---- stage [ip, ip + kWin) with aligned 32-bit loads --------------------
@@ -227,26 +232,62 @@ __device__ void parser_body(Smem& S, const Chunk& c, int p, uint32_t lane) {
         __syncwarp();
         win = win8 + shift;
       }
+      // ---- token starts: next-token table in registers, pointer doubling ----------
+      // Lane l owns window positions 8l..8l+7; table entries are bytes
+      // (255 = the chain stops), packed 4 per register, fetched with shuffles.
+      uint32_t jt[kLevels][2];
+      {
+        const uintptr_t wa = reinterpret_cast<uintptr_t>(win) + 8 * lane;
+        const uint32_t* aw = reinterpret_cast<const uint32_t*>(wa & ~uintptr_t(3));
+        const uint32_t sh = (uint32_t)(wa & 3) * 8;
+        const uint32_t w0 = aw[0], w1 = aw[1], w2 = aw[2];
+        const uint32_t b03 = __funnelshift_r(w0, w1, sh), b47 = __funnelshift_r(w1, w2, sh);
+        uint32_t r0 = 0, r1 = 0;
 #pragma unroll
-      for (uint32_t q = 0; q < kWin / 32; ++q) {
-        const uint32_t i = lane * (kWin / 32) + q;
-        P.jump[0][i] = (uint16_t)next_token(win, i, avail, rem);
+        for (uint32_t q = 0; q < 8; ++q) {
+          const uint32_t i = 8 * lane + q;
+          const uint32_t t = ((q < 4 ? b03 : b47) >> (8 * (q & 3))) & 0xFFu;
+          uint32_t nx = kStop;
+          if (i < avail) {
+            const uint32_t ll = t >> 4;
+            if (ll == 15 || (t & 15) == 15) {
+              nx = next_token(win, i, avail, rem);           // length extensions: slow path
+            } else {
+              const uint32_t j = i + 1 + ll;
+              if (j < rem && j + 2 <= avail) nx = j + 2;
+            }
+            if (nx > kStop) nx = kStop;
+          }
+          if (q < 4) r0 |= nx << (8 * q); else r1 |= nx << (8 * (q - 4));
+        }
+        jt[0][0] = r0;
+        jt[0][1] = r1;
       }
-      __syncwarp();
 #pragma unroll
       for (int k = 0; k + 1 < kLevels; ++k) {
+        uint32_t r0 = 0, r1 = 0;
 #pragma unroll
-        for (uint32_t q = 0; q < kWin / 32; ++q) {
-          const uint32_t i = lane * (kWin / 32) + q;
-          const uint32_t v = P.jump[k][i];
-          P.jump[k + 1][i] = v < kWin ? P.jump[k][v] : (uint16_t)kWin;
+        for (uint32_t q = 0; q < 8; ++q) {
+          const uint32_t v = ((q < 4 ? jt[k][0] : jt[k][1]) >> (8 * (q & 3))) & 0xFFu;
+          const int src = (int)(v >> 3);
+          const uint32_t a = __shfl_sync(kFull, jt[k][0], src), b = __shfl_sync(kFull, jt[k][1], src);
+          const uint32_t e = v & 7;
+          uint32_t nv = ((e < 4 ? a : b) >> (8 * (e & 3))) & 0xFFu;
+          if (v == kStop) nv = kStop;
+          if (q < 4) r0 |= nv << (8 * q); else r1 |= nv << (8 * (q - 4));
         }
-        __syncwarp();
+        jt[k + 1][0] = r0;
+        jt[k + 1][1] = r1;
       }
       uint32_t pp = 0;
 #pragma unroll
-      for (int k = 0; k < kLevels; ++k)
-        if ((lane >> k) & 1) pp = pp < kWin ? P.jump[k][pp] : kWin;
+      for (int k = 0; k < kLevels; ++k) {
+        const int src = (int)(pp >> 3);
+        const uint32_t a = __shfl_sync(kFull, jt[k][0], src), b = __shfl_sync(kFull, jt[k][1], src);
+        const uint32_t e = pp & 7;
+        const uint32_t nv = ((e < 4 ? a : b) >> (8 * (e & 3))) & 0xFFu;
+        if (((lane >> k) & 1) && pp != kStop) pp = nv;
+      }
       bool valid = pp < avail;
       auto byte_at = [&](uint32_t pos) -> uint32_t {
         const uint32_t rel = pos - ip;
@@ -325,30 +366,59 @@ __device__ void parser_body(Smem& S, const Chunk& c, int p, uint32_t lane) {
       if (!spin_until(S, [&] { return tail - vload(&S.q_head[p]) < (uint32_t)kSlots; })) return;
       Slot& sl = P.slot[tail % kSlots];
       if (!long_mode) {
-        // one descriptor per output byte of the batch
-        if (mine) {
-          const uint32_t a = (uint32_t)ostart, b = (uint32_t)oend, m0 = (uint32_t)ms;
-          for (uint32_t i = a; i < b; ++i) {
+        // One descriptor per output byte, spread over the lanes by position.
+        // The owner sequence of byte r is found from a bitmap of sequence
+        // starts (warp OR-reductions), its fields by shuffles.
+        const uint32_t n = be - op;
+        const uint32_t srel = mine ? (uint32_t)(ostart - op) : 0xffffffffu;
+        const uint32_t mrel = (uint32_t)(ms - op);
+        uint32_t startw[kBatch / 32], before[kBatch / 32];
+        uint32_t acc = 0;
+#pragma unroll
+        for (uint32_t w = 0; w < kBatch / 32; ++w) {
+          const uint32_t bit = (srel >> 5) == w ? (1u << (srel & 31)) : 0u;
+          startw[w] = __reduce_or_sync(kFull, bit);
+          before[w] = acc;
+          acc += __popc(startw[w]);
+        }
+        const uint32_t lane_mask = (2u << lane) - 1u;   // bits 0..lane
+        bool internal = false;
+#pragma unroll
+        for (uint32_t w = 0; w < kBatch / 32; ++w) {
+          if (w * 32 >= n) break;                         // uniform
+          const uint32_t r = lane + 32 * w;
+          int own = (int)(before[w] + __popc(startw[w] & lane_mask)) - 1;
+          own = max(0, min(own, used - 1));
+          const uint32_t o_s = __shfl_sync(kFull, srel, own);
+          const uint32_t o_m = __shfl_sync(kFull, mrel, own);
+          const uint32_t o_lit = __shfl_sync(kFull, lit_pos, own);
+          const uint32_t o_off = __shfl_sync(kFull, off, own);
+          if (r < n) {
             uint32_t d;
-            if (i < m0) {
-              d = kLit | byte_at(lit_pos + (i - a));
+            if (r < o_m) {
+              d = kLit | byte_at(o_lit + (r - o_s));
             } else {
-              const uint32_t k = i - m0;
-              const uint32_t s = m0 - off + (off > k ? k : k % off);
-              d = s >= op ? (kInternal | (s - op)) : s;
+              const uint32_t k = r - o_m;
+              uint32_t kk = k;
+              if (o_off <= k) kk = k % o_off;
+              const uint32_t s = op + o_m - o_off + kk;   // o_off <= ms: checked above
+              if (s >= op) { d = kInternal | (s - op); internal = true; }
+              else d = s;
             }
-            sl.desc[i - op] = d;
+            sl.desc[r] = d;
           }
         }
-        __syncwarp();
-        // chase sources produced inside the batch
-        const uint32_t n = be - op;
-        for (uint32_t r = lane; r < n; r += 32) {
-          uint32_t d = sl.desc[r];
-          uint32_t steps = 0;
-          while ((d & kInternal) && steps++ < kBatch) d = *(volatile uint32_t*)&sl.desc[d & ~kInternal];
-          if (d & kInternal) { set_err(S, kTimeout); break; }
-          *(volatile uint32_t*)&sl.desc[r] = d;
+        // sources produced inside the batch: chase them to a literal or an
+        // earlier batch (rare; skipped when no lane has one)
+        if (__any_sync(kFull, internal)) {
+          __syncwarp();
+          for (uint32_t r = lane; r < n; r += 32) {
+            uint32_t d = *(volatile uint32_t*)&sl.desc[r];
+            uint32_t steps = 0;
+            while ((d & kInternal) && steps++ < kBatch) d = *(volatile uint32_t*)&sl.desc[d & ~kInternal];
+            if (d & kInternal) { set_err(S, kTimeout); break; }
+            *(volatile uint32_t*)&sl.desc[r] = d;
+          }
         }
         if (lane == 0) { sl.mode = 0; }
       } else if (lane == 0) {
