@@ -67,28 +67,35 @@ zmoe_status zmoe_tensor_recover(uint16_t* out, const uint8_t* exp, const uint8_t
  * leave the SM: each one is merged with its sign+mantissa byte and written as
  * BF16 straight into the destination slot.
  * ------------------------------------------------------------------------ */
+#define ZMOE_SLICE_BYTES 256      /* output bytes per slice-index entry */
+#define ZMOE_MAP_ENTRIES 32768    /* uint32 scratch entries per indexed chunk (128 KiB) */
+
 typedef struct zmoe_chunk {
   const uint8_t* src;   /* LZ4 block, device memory */
   const uint8_t* sm;    /* sign+mantissa bytes of this chunk's elements */
   uint16_t* dst;        /* BF16 output of this chunk's elements */
-  const uint32_t* index;/* device [n_index][2] segment index from zmoe_lz4_build_index, or NULL */
+  const uint32_t* index;/* device [n_index][2] slice index from zmoe_lz4_build_index, or NULL */
+  uint32_t* map;        /* device scratch, ZMOE_MAP_ENTRIES uint32, 16-byte aligned (with index) */
   uint32_t src_size;    /* compressed bytes */
   uint32_t out_size;    /* exponent bytes = elements (original_sizes[c]) */
   uint32_t n_index;     /* entries in index */
-  uint32_t seg_bytes;   /* output bytes per index step */
+  uint32_t seg_bytes;   /* output bytes per index entry: ZMOE_SLICE_BYTES */
 } zmoe_chunk;
 
 /* chunks and status are device arrays of n_chunks entries.  One CTA decodes
- * one chunk; with an index its 16 warps work on different segments of it. */
+ * one chunk: with an index, 4 warps map sources (one 256-byte slice per lane)
+ * while one warp resolves bytes from a shared-memory window and one writes
+ * BF16; without an index one warp decodes the chunk serially. */
 zmoe_status zmoe_decode_chunks(const zmoe_chunk* chunks, int n_chunks, int32_t* status,
                                zmoe_stream_t stream);
 
-/* Host: segment index of one LZ4 block (no counterpart in the reference; the
+/* Host: slice index of one LZ4 block (no counterpart in the reference; the
  * reference decodes each block serially on one CPU thread).  Entry j =
- * (input position, output position) of the first sequence starting at or after
- * output byte j * seg_bytes; ceil(out_size / seg_bytes) entries are written to
- * entries[2 * j .. 2 * j + 1].  Returns the entry count, or a negative value
- * for a malformed block (-3 overrun, -4 bad offset) or too small a capacity (-2). */
+ * (input position of the token, output position where it starts) of the
+ * sequence that contains output byte j * seg_bytes; ceil(out_size / seg_bytes)
+ * entries are written to entries[2 * j .. 2 * j + 1].  Returns the entry
+ * count, or a negative value for a malformed block (-3 overrun, -4 bad offset,
+ * -5 fewer than out_size bytes) or too small a capacity (-2). */
 int zmoe_lz4_build_index(const uint8_t* src, uint32_t src_size, uint32_t out_size, uint32_t seg_bytes,
                          uint32_t* entries, int capacity);
 

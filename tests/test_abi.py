@@ -26,7 +26,7 @@ def test_library_exports_header_symbols():
 
 def test_struct_layouts_match_header():
     from zmoe import _lib
-    assert ctypes.sizeof(_lib.ZmoeChunk) == 48
+    assert ctypes.sizeof(_lib.ZmoeChunk) == 56
     # 4 pointers, 6 ints, 1 float (+4 padding), 4 pointers
     assert ctypes.sizeof(_lib.RouterArgs) == 96
     src = '#include "zmoe.h"\n#include <stdio.h>\nint main(){printf("%zu %zu %zu %zu %zu", sizeof(zmoe_chunk), sizeof(zmoe_router_args), sizeof(zmoe_permute_args), sizeof(zmoe_ffn_args), sizeof(zmoe_combine_args));}'

@@ -27,19 +27,21 @@ def test_encode_matches_oracle_bytes_and_roundtrips():
             assert np.array_equal(ocodec.decode_tensor(e.blocks, e.original_sizes, np.frombuffer(e.sm, np.uint8)), bits)
 
 
-def test_segment_index_matches_token_walk():
+def test_slice_index_matches_token_walk():
+    """Entry j names the sequence that contains output byte j * slice."""
     from zmoe import ops
     gen = torch.Generator().manual_seed(4)
     bits = ocodec.bf16_bits((torch.randn(100, 700, generator=gen) * 0.02).to(torch.bfloat16))
+    bits = np.concatenate([bits, np.full(5000, 0x3C00, np.uint16)])     # a long run too
     blocks, osz, _ = ocodec.encode_tensor(bits, 2)
     for blk, o in zip(blocks, osz):
         seqs = ocodec.lz4_sequences(blk)
-        for seg in (64, 2048, 10 ** 6):
+        for seg in (256, 4096):
             idx = ops.build_index(blk, o, seg)
             assert len(idx) == (o + seg - 1) // seg
-            starts = [(s[0], s[1]) for s in seqs]
             for j, (ip, op) in enumerate(idx.tolist()):
-                want = next(((a, b) for a, b in starts if b >= j * seg), None)
+                b = j * seg
+                want = next((s[0], s[1]) for s in seqs if s[1] <= b < s[1] + s[2] + s[4])
                 assert (ip, op) == want, (seg, j)
 
 

@@ -83,7 +83,8 @@ def test_decode_many_chunks_one_launch_unaligned_destinations():
         descs.extend(ct.descs(v))
         views.append(v)
         pos += b.size
-    table = ops.chunk_table(descs, "cuda")
+    scratch = ops.map_scratch(len(descs), "cuda")
+    table = ops.chunk_table(descs, "cuda", scratch)
     st = ops.decode_chunks(table, len(descs))
     torch.cuda.synchronize()
     assert (st.cpu().numpy() == 0).all()
@@ -99,9 +100,9 @@ def test_decode_long_runs_and_overlapping_matches():
     parts = [rng.integers(0, 65536, 3000, dtype=np.uint16), np.full(70000, 0x3C00, np.uint16),
              rng.integers(0, 65536, 77, dtype=np.uint16), np.tile(np.arange(3, dtype=np.uint16) + 0x3F00, 9000)]
     bits = np.concatenate(parts)
-    for chunks in (1, 2, 7):
+    for chunks, indexed in ((1, True), (2, True), (7, True), (2, False)):
         blocks, osz, sm = codec.encode_tensor(bits, chunks)
-        out, st = ops.CompressedTensor(blocks, osz, sm.tobytes()).decode()
+        out, st = ops.CompressedTensor(blocks, osz, sm.tobytes(), indexed=indexed).decode()
         torch.cuda.synchronize()
         assert (st.cpu().numpy() == 0).all()
         assert np.array_equal(_bits(out), bits)
@@ -163,16 +164,16 @@ def test_tensor_recover_bit_exact(n, offset):
     assert np.array_equal(_bits(out), bits)
 
 
-@pytest.mark.parametrize("seg_bytes,indexed", [(64, True), (256, True), (2048, True), (1 << 30, True), (0, False)])
-def test_decode_segment_sizes(seg_bytes, indexed):
-    """Many small segments force cross-segment waits; an unindexed chunk is
-    decoded by one warp; all must give the same bytes."""
+@pytest.mark.parametrize("indexed", [True, False])
+def test_decode_indexed_and_unindexed(indexed):
+    """With the slice index 4 warps map sources in parallel; without it one
+    warp decodes serially; both must give the same bytes."""
     ops = _ops()
     gen = torch.Generator().manual_seed(21)
     w = (torch.randn(512, 2048, generator=gen) * 0.02).to(torch.bfloat16)
     bits = codec.bf16_bits(w)
     blocks, osz, sm = codec.encode_tensor(bits, 3)
-    ct = ops.CompressedTensor(blocks, osz, sm.tobytes(), seg_bytes=seg_bytes or 2048, indexed=indexed)
+    ct = ops.CompressedTensor(blocks, osz, sm.tobytes(), indexed=indexed)
     out, st = ct.decode()
     torch.cuda.synchronize()
     assert (st.cpu().numpy() == 0).all(), st.cpu().numpy()
@@ -187,8 +188,8 @@ def test_decode_small_offsets_across_segments():
     bits = np.concatenate([np.tile(base, 3000), rng.integers(0, 65536, 5000, dtype=np.uint16),
                            np.tile(base[:5], 20000)])
     blocks, osz, sm = codec.encode_tensor(bits, 1)
-    for seg in (64, 512):
-        out, st = ops.CompressedTensor(blocks, osz, sm.tobytes(), seg_bytes=seg).decode()
+    for indexed in (True, False):
+        out, st = ops.CompressedTensor(blocks, osz, sm.tobytes(), indexed=indexed).decode()
         torch.cuda.synchronize()
         assert (st.cpu().numpy() == 0).all()
         assert np.array_equal(_bits(out), bits)

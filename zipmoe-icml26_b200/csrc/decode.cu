@@ -6,36 +6,30 @@
 // kernel (csrc/kernels/tensor_recover.cu:12-43) reading both planes over
 // zero-copy host memory.
 //
-// One CTA of 6 warps decodes one LZ4 block.  LZ4HC matches chain back through
-// earlier matches (median offset ~20 KB), so the data dependencies of a block
-// are nearly serial; parsing the token stream is not.  The work is split so
-// that only a cheap gather stays serial:
+// LZ4HC matches chain back through earlier matches (median offset ~20 KB), so
+// the bytes of a block depend on each other almost serially; the token stream
+// does not.  One CTA of 6 warps decodes one block in two overlapped stages:
 //
-//  * 4 parser warps.  A segment index built at load time (zmoe_lz4_build_index:
-//    the first sequence at or after every 1 KiB of output) lets parser p take
-//    segments p, p+4, ...  A parser looks at 255 compressed bytes (prefetched
-//    into shared memory with cp.async), builds a next-token table in
-//    registers (8 positions per lane, packed bytes) and finds up to 32 token
-//    starts at once by pointer doubling with warp shuffles; it decodes the
-//    headers and turns a batch of up to 256 output bytes into one 32-bit
-//    descriptor per output byte — a literal value, or the absolute position
-//    of its source byte — with bytes spread over lanes by position (owner
-//    sequence from a bitmap of sequence starts).  Sources inside the batch
-//    itself (short offsets, overlapping copies) are chased at parse time until
-//    they reach a literal or a byte before the batch, so a descriptor never
-//    depends on its batch.  All of this keeps shared-memory traffic low: the
-//    decoder's limit is shared-memory wavefronts, not HBM.
-//    Batches go to a 6-slot queue per parser (one whole segment).
-//  * 1 resolver warp.  It takes the batches in output order and, per byte,
-//    reads either the literal or ring[source & 0xFFFF] from a 64 KiB
-//    shared-memory window of decoded exponents (LZ4 offsets are < 64 KiB),
-//    then writes the batch into the window: one gather + one scatter per
-//    byte, no dependency waits.  A sequence longer than a batch is copied by
-//    the whole warp 32 bytes at a time from its most recent equal byte.
-//  * 1 flusher warp.  It follows the resolver through the window, merges 16
-//    exponent bytes with 16 sign+mantissa bytes (128-bit loads) into BF16 and
-//    stores 32 bytes per lane; the resolver never overwrites a window byte the
-//    flusher has not consumed.
+//  * Source map (4 parser warps).  A slice index built when the block is
+//    loaded (zmoe_lz4_build_index) names, for every 256 output bytes, the
+//    sequence that contains that byte.  Each lane parses one 256-byte slice on
+//    its own (a parser warp covers an 8 KiB window) and writes one 32-bit
+//    entry per output byte into a map ring in L2-resident scratch: a literal
+//    value, or the position of a byte with the same value.  For a match byte
+//    the position is the most recent equal byte before the 2 KiB step that
+//    holds it (for a run of period o, the latest earlier copy), so it is
+//    always inside the 64 KiB window; a source inside the step itself is
+//    chased through the map at parse time.  No entry depends on its own step.
+//  * Resolve (1 resolver warp + 1 flusher warp).  Per 2 KiB step the resolver
+//    reads 2048 map entries (coalesced 128-bit loads) and gathers each byte
+//    from a 64 KiB shared-memory window of decoded exponents, then writes the
+//    step into the window.  The flusher follows, merging 16 exponent bytes
+//    with 16 sign+mantissa bytes (128-bit loads) into BF16 (two 128-bit
+//    stores per lane); the resolver never overwrites a byte the flusher has
+//    not consumed.
+//
+// A chunk without an index (zmoe_chunk.index == NULL) is decoded by warp 0
+// alone in one pass straight into the output (no scratch needed).
 //
 // Roles synchronise through counters in shared memory; every wait is bounded
 // and gives up with an error status.  Errors (bad offsets, lengths past the
@@ -50,38 +44,28 @@ namespace {
 constexpr int kParsers = 4;
 constexpr int kWarps = kParsers + 2;          // parsers, resolver, flusher
 constexpr int kResolver = kParsers;           // warp kParsers + 1 is the flusher
-constexpr int kSlots = 6;                     // queue depth per parser (a 1 KiB segment)
-constexpr uint32_t kWin = 256;                // compressed bytes staged per parse step
-constexpr uint32_t kInBuf = 1024;             // prefetched compressed bytes per segment buffer
-constexpr int kLevels = 5;                    // jumps of 1, 2, 4, 8, 16 tokens
-constexpr uint32_t kStop = 255;               // next-token entry: chain stops (window positions 0..254)
-constexpr uint32_t kBatch = 256;              // output bytes of one batch
+constexpr uint32_t kSlice = 256;              // output bytes parsed by one lane
+constexpr uint32_t kWindow = 32 * kSlice;     // output bytes mapped by one parser pass
+constexpr uint32_t kStep = 2048;              // output bytes resolved per resolver step
 constexpr uint32_t kRing = 65536;             // decoded-exponent window
 constexpr uint32_t kRingMask = kRing - 1;
-constexpr uint32_t kLit = 0x80000000u;        // descriptor: literal value in bits 0..7
-constexpr uint32_t kInternal = 0x40000000u;   // descriptor (parse time only): batch-relative source
+constexpr uint32_t kMapEntries = ZMOE_MAP_ENTRIES;   // source-map ring per chunk (scratch)
+constexpr uint32_t kMapMask = kMapEntries - 1;
+static_assert(kSlice == ZMOE_SLICE_BYTES, "slice index granularity");
+constexpr uint32_t kMapWindows = kMapEntries / kWindow;
+constexpr uint32_t kLit = 0x80000000u;        // map entry: literal value in bits 0..7
+constexpr uint32_t kInner = 0x40000000u;      // map entry (parse time only): source inside its step
 constexpr long long kSpinCycles = 2000000000LL;   // ~1 s at 1.9 GHz
 constexpr unsigned kFull = 0xffffffffu;
 constexpr int32_t kTimeout = 5;
 
-struct Slot {
-  uint32_t desc[kBatch];
-  uint32_t bs, n, mode, pad;                  // mode 0: descriptors, 1: one long sequence
-  uint32_t l_ll, l_lit, l_ml, l_off;          // long sequence: literal count/source, match length/offset
-};
-
-struct ParserSmem {
-  __align__(16) uint8_t inbuf[2][kInBuf];
-  uint32_t winw[kWin / 4 + 2];
-  Slot slot[kSlots];
-};
+static_assert((kMapEntries & (kMapEntries - 1)) == 0 && kMapWindows >= 2, "map ring");
 
 struct Smem {
   uint8_t ring[kRing];
-  ParserSmem ps[kParsers];
-  uint32_t q_tail[kParsers];
-  uint32_t q_head[kParsers];
+  uint32_t win_ready[kMapWindows];            // window w mapped: win_ready[w % n] == w + 1
   uint32_t res_pos;                           // bytes [0, res_pos) resolved into the ring
+  uint32_t res_win;                           // windows fully resolved (map slots reusable)
   uint32_t flush_pos;                         // bytes [0, flush_pos) consumed by the flusher
   int32_t err;
 };
@@ -91,17 +75,11 @@ struct Chunk {
   const uint8_t* sm;
   uint16_t* dst;
   const uint32_t* index;
-  uint32_t src_size, out_size, n_seg;
+  uint32_t* map;
+  uint32_t src_size, out_size, n_index;
   uint32_t rofs;   // ring index of position i is (i + rofs) & kRingMask; makes 16-byte
                    // groups that the flusher loads aligned both in the ring and in memory
-
   __device__ __forceinline__ uint32_t ri(uint32_t pos) const { return (pos + rofs) & kRingMask; }
-  __device__ uint32_t seg_out(uint32_t j) const {
-    if (j >= n_seg) return out_size;
-    if (!index) return 0;
-    return min(__ldg(index + 2 * j + 1), out_size);
-  }
-  __device__ uint32_t seg_in(uint32_t j) const { return index ? __ldg(index + 2 * j) : 0; }
 };
 
 __device__ __forceinline__ uint32_t vload(const uint32_t* p) { return *(const volatile uint32_t*)p; }
@@ -120,410 +98,189 @@ __device__ __forceinline__ bool spin_until(Smem& S, F cond) {
       set_err(S, kTimeout);
       return false;
     }
-    __nanosleep(32);
+    __nanosleep(64);
   }
   return true;
 }
 
-// Start of the token after a token at window position i, or kWin when the
-// chain cannot continue inside the staged bytes.
-__device__ __forceinline__ uint32_t next_token(const uint8_t* win, uint32_t i, uint32_t avail, uint32_t rem) {
-  if (i >= avail) return kWin;
-  const uint32_t tok = win[i];
-  uint32_t j = i + 1;
+// One LZ4 sequence header at ip: literal count and position, match offset and
+// length, position of the next token.  Returns 0 or a ZMOE_CHUNK_* error.
+struct Seq {
+  uint32_t ll, lit, off, ml, next;
+  bool last;
+};
+
+__device__ __forceinline__ int read_seq(const uint8_t* __restrict__ src, uint32_t size, uint32_t ip, Seq& s) {
+  if (ip >= size) return ZMOE_CHUNK_INPUT_OVERRUN;
+  const uint32_t tok = __ldg(src + ip);
+  uint32_t q = ip + 1;
   uint32_t ll = tok >> 4;
   if (ll == 15) {
     uint32_t b;
     do {
-      if (j >= avail) return kWin;
-      b = win[j++];
+      if (q >= size) return ZMOE_CHUNK_INPUT_OVERRUN;
+      b = __ldg(src + q++);
       ll += b;
-    } while (b == 255);
+    } while (b == 255 && ll < (1u << 30));
   }
-  j += ll;
-  if (j >= rem) return kWin;                  // literals reach the block end: last sequence
-  if (j + 2 > avail) return kWin;
-  j += 2;
-  if ((tok & 15) == 15) {
-    uint32_t b;
-    do {
-      if (j >= avail) return kWin;
-      b = win[j++];
-    } while (b == 255);
+  if ((uint64_t)q + ll > size) return ZMOE_CHUNK_INPUT_OVERRUN;
+  s.ll = ll;
+  s.lit = q;
+  q += ll;
+  s.off = 0;
+  s.ml = 0;
+  s.last = q == size;
+  if (!s.last) {
+    if (q + 2 > size) return ZMOE_CHUNK_INPUT_OVERRUN;
+    s.off = __ldg(src + q) | ((uint32_t)__ldg(src + q + 1) << 8);
+    q += 2;
+    uint32_t ml = tok & 15;
+    if (ml == 15) {
+      uint32_t b;
+      do {
+        if (q >= size) return ZMOE_CHUNK_INPUT_OVERRUN;
+        b = __ldg(src + q++);
+        ml += b;
+      } while (b == 255 && ml < (1u << 30));
+    }
+    s.ml = ml + 4;
   }
-  return j < kWin ? j : kWin;
+  s.next = q;
+  return 0;
 }
 
 // ---------------------------------------------------------------------------
-// parser warp
+// parser warps: source map
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void cp_async16(void* dst, const void* src, uint32_t bytes) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
-               "l"(src), "r"(bytes)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
-
-__device__ void parser_body(Smem& S, const Chunk& c, int p, uint32_t lane) {
-  ParserSmem& P = S.ps[p];
-  const uint8_t* win8 = reinterpret_cast<const uint8_t*>(P.winw);
-  uint32_t tail = 0;
-  // The compressed bytes of this parser's next segment are copied into shared
-  // memory (16-byte cp.async, zero-filled past the block) while it parses the
-  // current one.  Needs a 16-byte aligned block; otherwise bytes come from L1/L2.
-  const bool pf = (reinterpret_cast<uintptr_t>(c.src) & 15) == 0;
-  uint32_t pf_base[2] = {0xffffffffu, 0xffffffffu};
-  auto prefetch = [&](int b, uint32_t j) {
-    if (j >= c.n_seg) {
-      pf_base[b] = 0xffffffffu;
-    } else {
-      const uint32_t base = c.seg_in(j) & ~15u;
-      pf_base[b] = base;
-      for (uint32_t q = lane; q < kInBuf / 16; q += 32) {
-        const uint32_t o = base + 16 * q;
-        const uint32_t nb = o < c.src_size ? min(16u, c.src_size - o) : 0u;
-        cp_async16(&P.inbuf[b][16 * q], nb ? c.src + o : c.src, nb);
-      }
-    }
-    cp_async_commit();
-  };
-  int cur = 0;
-  if (pf) prefetch(0, p);
-  for (uint32_t j = p; j < c.n_seg; j += kParsers, cur ^= 1) {
-    if (pf) {
-      prefetch(cur ^ 1, j + kParsers);
-      cp_async_wait1();
-      __syncwarp();
-    }
-    const uint8_t* buf = P.inbuf[cur];
-    const uint32_t bbase = pf ? pf_base[cur] : 0xffffffffu;
-    const uint32_t bend = pf ? min(bbase + kInBuf, c.src_size) : 0u;
-    const uint32_t hi = c.seg_out(j + 1);
-    uint32_t op = c.seg_out(j);
-    uint32_t ip = c.seg_in(j);
-    while (op < hi) {
-      if (failed(S)) return;
-      if (ip >= c.src_size) { set_err(S, ZMOE_CHUNK_INPUT_OVERRUN); return; }
-      const uint32_t rem = c.src_size - ip;
-      const uint32_t avail = rem < kStop ? rem : kStop;
-      const uint8_t* win;
-      if (pf && ip >= bbase && ip + avail <= bend && ip - bbase + kWin + 8 <= kInBuf) {
-        win = buf + (ip - bbase);                  // window already in shared memory
+__device__ void parser(Smem& S, const Chunk& c, int p, uint32_t lane) {
+  const uint32_t n_win = (c.out_size + kWindow - 1) / kWindow;
+  for (uint32_t w = p; w < n_win; w += kParsers) {
+    // the map slots of window w are free once window w - kMapWindows is resolved
+    if (w >= kMapWindows && !spin_until(S, [&] { return vload(&S.res_win) > w - kMapWindows; })) return;
+    const uint32_t g = w * 32 + lane;                 // slice of this lane
+    const uint32_t b0 = g * kSlice;
+    const uint32_t b1 = min(b0 + kSlice, c.out_size);
+    int err = 0;
+    bool inner = false;
+    if (b0 < c.out_size) {
+      if (g >= c.n_index) {
+        err = ZMOE_CHUNK_BAD_DESC;
       } else {
-        // ---- stage [ip, ip + kWin) with aligned 32-bit loads --------------------
-        const uintptr_t beg = reinterpret_cast<uintptr_t>(c.src);
-        const uintptr_t end = beg + c.src_size;
-        const uintptr_t addr = beg + ip;
-        const uint32_t shift = (uint32_t)(addr & 3);
-        for (uint32_t q = lane; q < kWin / 4 + 2; q += 32) {
-          const uintptr_t wa = addr - shift + 4 * q;
-          uint32_t v = 0;
-          if (wa >= beg && wa + 4 <= end) {
-            v = __ldg(reinterpret_cast<const uint32_t*>(wa));
-          } else {
-            for (uint32_t b = 0; b < 4; ++b)
-              if (wa + b >= beg && wa + b < end)
-                v |= (uint32_t)__ldg(reinterpret_cast<const uint8_t*>(wa + b)) << (8 * b);
+        uint32_t ip = __ldg(c.index + 2 * g);
+        uint32_t so = __ldg(c.index + 2 * g + 1);     // output start of the sequence at ip
+        uint32_t e = b0;
+        uint4 buf;                                    // 4 entries per 128-bit store
+        uint32_t* bv = reinterpret_cast<uint32_t*>(&buf);
+        if (so > b0) err = ZMOE_CHUNK_BAD_DESC;
+        while (!err && e < b1) {
+          Seq s;
+          err = read_seq(c.src, c.src_size, ip, s);
+          if (err) break;
+          const uint32_t ms = so + s.ll;              // first match byte
+          const uint32_t me = ms + s.ml;
+          if (s.ml > 0 && (s.off == 0 || s.off > ms)) { err = ZMOE_CHUNK_BAD_OFFSET; break; }
+          // literals
+          for (; e < b1 && e < ms; ++e) {
+            bv[e & 3] = kLit | __ldg(c.src + s.lit + (e - so));
+            if ((e & 3) == 3) reinterpret_cast<uint4*>(c.map)[(e & kMapMask) >> 2] = buf;
           }
-          P.winw[q] = v;
-        }
-        __syncwarp();
-        win = win8 + shift;
-      }
-      // ---- token starts: next-token table in registers, pointer doubling ----------
-      // Lane l owns window positions 8l..8l+7; table entries are bytes
-      // (255 = the chain stops), packed 4 per register, fetched with shuffles.
-      uint32_t jt[kLevels][2];
-      {
-        const uintptr_t wa = reinterpret_cast<uintptr_t>(win) + 8 * lane;
-        const uint32_t* aw = reinterpret_cast<const uint32_t*>(wa & ~uintptr_t(3));
-        const uint32_t sh = (uint32_t)(wa & 3) * 8;
-        const uint32_t w0 = aw[0], w1 = aw[1], w2 = aw[2];
-        const uint32_t b03 = __funnelshift_r(w0, w1, sh), b47 = __funnelshift_r(w1, w2, sh);
-        uint32_t r0 = 0, r1 = 0;
-#pragma unroll
-        for (uint32_t q = 0; q < 8; ++q) {
-          const uint32_t i = 8 * lane + q;
-          const uint32_t t = ((q < 4 ? b03 : b47) >> (8 * (q & 3))) & 0xFFu;
-          uint32_t nx = kStop;
-          if (i < avail) {
-            const uint32_t ll = t >> 4;
-            if (ll == 15 || (t & 15) == 15) {
-              nx = next_token(win, i, avail, rem);           // length extensions: slow path
+          // match bytes: the latest byte before the step that repeats e
+          for (; e < b1 && e < me; ++e) {
+            const uint32_t step0 = e & ~(kStep - 1);
+            const uint32_t o = s.off;
+            const uint32_t k = e - ms;
+            const uint32_t base = ms - o + (k < o ? k : k % o);   // first copy, in [ms - o, ms)
+            uint32_t v;
+            if (base < step0) {
+              v = base + o * ((step0 - 1 - base) / o);            // latest copy below the step
             } else {
-              const uint32_t j = i + 1 + ll;
-              if (j < rem && j + 2 <= avail) nx = j + 2;
+              v = kInner | base;                                  // inside the step: chase later
+              inner = true;
             }
-            if (nx > kStop) nx = kStop;
+            bv[e & 3] = v;
+            if ((e & 3) == 3) reinterpret_cast<uint4*>(c.map)[(e & kMapMask) >> 2] = buf;
           }
-          if (q < 4) r0 |= nx << (8 * q); else r1 |= nx << (8 * (q - 4));
-        }
-        jt[0][0] = r0;
-        jt[0][1] = r1;
-      }
-#pragma unroll
-      for (int k = 0; k + 1 < kLevels; ++k) {
-        uint32_t r0 = 0, r1 = 0;
-#pragma unroll
-        for (uint32_t q = 0; q < 8; ++q) {
-          const uint32_t v = ((q < 4 ? jt[k][0] : jt[k][1]) >> (8 * (q & 3))) & 0xFFu;
-          const int src = (int)(v >> 3);
-          const uint32_t a = __shfl_sync(kFull, jt[k][0], src), b = __shfl_sync(kFull, jt[k][1], src);
-          const uint32_t e = v & 7;
-          uint32_t nv = ((e < 4 ? a : b) >> (8 * (e & 3))) & 0xFFu;
-          if (v == kStop) nv = kStop;
-          if (q < 4) r0 |= nv << (8 * q); else r1 |= nv << (8 * (q - 4));
-        }
-        jt[k + 1][0] = r0;
-        jt[k + 1][1] = r1;
-      }
-      uint32_t pp = 0;
-#pragma unroll
-      for (int k = 0; k < kLevels; ++k) {
-        const int src = (int)(pp >> 3);
-        const uint32_t a = __shfl_sync(kFull, jt[k][0], src), b = __shfl_sync(kFull, jt[k][1], src);
-        const uint32_t e = pp & 7;
-        const uint32_t nv = ((e < 4 ? a : b) >> (8 * (e & 3))) & 0xFFu;
-        if (((lane >> k) & 1) && pp != kStop) pp = nv;
-      }
-      bool valid = pp < avail;
-      auto byte_at = [&](uint32_t pos) -> uint32_t {
-        const uint32_t rel = pos - ip;
-        if (rel < avail) return win[rel];
-        if (pos >= bbase && pos < bend) return buf[pos - bbase];
-        return __ldg(c.src + pos);
-      };
-      // ---- sequence header of this lane --------------------------------------------
-      uint32_t ll = 0, ml = 0, off = 0, lit_pos = 0, seq_end = 0;
-      int lerr = 0;
-      if (valid) {
-        const uint32_t tok = win[pp];
-        uint32_t q = ip + pp + 1;
-        ll = tok >> 4;
-        if (ll == 15) {
-          uint32_t b;
-          do {
-            if (q >= c.src_size) { lerr = ZMOE_CHUNK_INPUT_OVERRUN; break; }
-            b = byte_at(q++);
-            ll += b;
-          } while (b == 255 && ll < (1u << 30));
-        }
-        lit_pos = q;
-        if (!lerr) {
-          if ((uint64_t)q + ll > c.src_size) {
-            lerr = ZMOE_CHUNK_INPUT_OVERRUN;
-          } else {
-            q += ll;
-            if (q != c.src_size) {
-              if (q + 2 > c.src_size) {
-                lerr = ZMOE_CHUNK_INPUT_OVERRUN;
-              } else {
-                off = byte_at(q) | (byte_at(q + 1) << 8);
-                q += 2;
-                ml = tok & 15;
-                if (ml == 15) {
-                  uint32_t b;
-                  do {
-                    if (q >= c.src_size) { lerr = ZMOE_CHUNK_INPUT_OVERRUN; break; }
-                    b = byte_at(q++);
-                    ml += b;
-                  } while (b == 255 && ml < (1u << 30));
-                }
-                ml += 4;
-              }
-            }
+          if (e < b1) {
+            if (s.last) { err = ZMOE_CHUNK_SHORT_OUTPUT; break; }
+            ip = s.next;
+            so = me;
           }
         }
-        seq_end = q;
-      }
-      const uint64_t len = valid ? (uint64_t)ll + ml : 0;
-      uint64_t incl = len;
-#pragma unroll
-      for (int d = 1; d < 32; d <<= 1) {
-        const uint64_t v = __shfl_up_sync(kFull, incl, d);
-        if (lane >= (uint32_t)d) incl += v;
-      }
-      const uint64_t ostart = (uint64_t)op + incl - len;
-      valid = valid && ostart < hi;
-      const uint64_t oend = min(ostart + len, (uint64_t)hi);
-      const unsigned fit = __ballot_sync(kFull, valid && oend - op <= kBatch);
-      const int cnt = __popc(__ballot_sync(kFull, valid));
-      int nb = fit == kFull ? 32 : __ffs(~fit) - 1;
-      nb = min(nb, cnt);
-      const bool long_mode = nb == 0;
-      const int used = long_mode ? 1 : nb;
-      const bool mine = (int)lane < used;
-      const uint64_t ms = ostart + ll;
-      if (mine && !lerr && ml > 0 && ms < oend && (off == 0 || off > ms)) lerr = ZMOE_CHUNK_BAD_OFFSET;
-      const unsigned emask = __ballot_sync(kFull, mine && lerr != 0);
-      if (emask) { set_err(S, __shfl_sync(kFull, lerr, __ffs(emask) - 1)); return; }
-      const uint32_t be = (uint32_t)__shfl_sync(kFull, oend, used - 1);
-      if (be == op) { set_err(S, ZMOE_CHUNK_SHORT_OUTPUT); return; }   // empty final sequence
-
-      // ---- wait for a free slot --------------------------------------------------
-      if (!spin_until(S, [&] { return tail - vload(&S.q_head[p]) < (uint32_t)kSlots; })) return;
-      Slot& sl = P.slot[tail % kSlots];
-      if (!long_mode) {
-        // One descriptor per output byte, spread over the lanes by position.
-        // The owner sequence of byte r is found from a bitmap of sequence
-        // starts (warp OR-reductions), its fields by shuffles.
-        const uint32_t n = be - op;
-        const uint32_t srel = mine ? (uint32_t)(ostart - op) : 0xffffffffu;
-        const uint32_t mrel = (uint32_t)(ms - op);
-        uint32_t startw[kBatch / 32], before[kBatch / 32];
-        uint32_t acc = 0;
-#pragma unroll
-        for (uint32_t w = 0; w < kBatch / 32; ++w) {
-          const uint32_t bit = (srel >> 5) == w ? (1u << (srel & 31)) : 0u;
-          startw[w] = __reduce_or_sync(kFull, bit);
-          before[w] = acc;
-          acc += __popc(startw[w]);
+        if (!err && (e & 3)) {                        // partial group at the chunk end
+          for (uint32_t i = e & ~3u; i < e; ++i) c.map[i & kMapMask] = bv[i & 3];
         }
-        const uint32_t lane_mask = (2u << lane) - 1u;   // bits 0..lane
-        bool internal = false;
-#pragma unroll
-        for (uint32_t w = 0; w < kBatch / 32; ++w) {
-          if (w * 32 >= n) break;                         // uniform
-          const uint32_t r = lane + 32 * w;
-          int own = (int)(before[w] + __popc(startw[w] & lane_mask)) - 1;
-          own = max(0, min(own, used - 1));
-          const uint32_t o_s = __shfl_sync(kFull, srel, own);
-          const uint32_t o_m = __shfl_sync(kFull, mrel, own);
-          const uint32_t o_lit = __shfl_sync(kFull, lit_pos, own);
-          const uint32_t o_off = __shfl_sync(kFull, off, own);
-          if (r < n) {
-            uint32_t d;
-            if (r < o_m) {
-              d = kLit | byte_at(o_lit + (r - o_s));
-            } else {
-              const uint32_t k = r - o_m;
-              uint32_t kk = k;
-              if (o_off <= k) kk = k % o_off;
-              const uint32_t s = op + o_m - o_off + kk;   // o_off <= ms: checked above
-              if (s >= op) { d = kInternal | (s - op); internal = true; }
-              else d = s;
-            }
-            sl.desc[r] = d;
-          }
-        }
-        // sources produced inside the batch: chase them to a literal or an
-        // earlier batch (rare; skipped when no lane has one)
-        if (__any_sync(kFull, internal)) {
-          __syncwarp();
-          for (uint32_t r = lane; r < n; r += 32) {
-            uint32_t d = *(volatile uint32_t*)&sl.desc[r];
-            uint32_t steps = 0;
-            while ((d & kInternal) && steps++ < kBatch) d = *(volatile uint32_t*)&sl.desc[d & ~kInternal];
-            if (d & kInternal) { set_err(S, kTimeout); break; }
-            *(volatile uint32_t*)&sl.desc[r] = d;
-          }
-        }
-        if (lane == 0) { sl.mode = 0; }
-      } else if (lane == 0) {
-        sl.mode = 1;
-        sl.l_ll = (uint32_t)min((uint64_t)ll, (uint64_t)(be - op));
-        sl.l_lit = lit_pos;
-        sl.l_ml = be - op - sl.l_ll;
-        sl.l_off = off;
       }
-      if (lane == 0) {
-        sl.bs = op;
-        sl.n = be - op;
-      }
+    }
+    const unsigned emask = __ballot_sync(kFull, err != 0);
+    if (emask) {
+      set_err(S, __shfl_sync(kFull, err, __ffs(emask) - 1));
+      return;
+    }
+    // chase sources inside the same 2 KiB step (entries of any lane of this warp)
+    if (__any_sync(kFull, inner)) {
       __threadfence_block();
       __syncwarp();
-      ++tail;
-      if (lane == 0) vstore(&S.q_tail[p], tail);
-      ip = __shfl_sync(kFull, seq_end, used - 1);
-      op = be;
-      if (op < hi && ip >= c.src_size) { set_err(S, ZMOE_CHUNK_SHORT_OUTPUT); return; }
+      if (inner) {
+        for (uint32_t i = b0; i < b1; ++i) {
+          uint32_t v = __ldcg(c.map + (i & kMapMask));
+          if (!(v & kInner)) continue;
+          uint32_t steps = 0;
+          while ((v & kInner) && steps++ < kStep) v = __ldcg(c.map + ((v & ~kInner) & kMapMask));
+          if (v & kInner) { set_err(S, kTimeout); break; }
+          c.map[i & kMapMask] = v;
+        }
+      }
     }
+    __threadfence_block();
+    __syncwarp();
+    if (lane == 0) vstore(&S.win_ready[w % kMapWindows], w + 1);
   }
-}
-
-// Every exit waits for the parser's own asynchronous copies into shared memory.
-__device__ void parser(Smem& S, const Chunk& c, int p, uint32_t lane) {
-  parser_body(S, c, p, lane);
-  cp_async_wait0();
-  __syncwarp();
 }
 
 // ---------------------------------------------------------------------------
 // resolver warp
 // ---------------------------------------------------------------------------
 __device__ void resolver(Smem& S, const Chunk& c, uint32_t lane) {
-  uint32_t head[kParsers] = {0, 0, 0, 0};
-  for (uint32_t j = 0; j < c.n_seg; ++j) {
-    const int q = j % kParsers;
-    const uint32_t hi = c.seg_out(j + 1);
-    uint32_t pos = c.seg_out(j);
-    while (pos < hi) {
-      if (!spin_until(S, [&] { return vload(&S.q_tail[q]) != head[q]; })) return;
-      __threadfence_block();
-      Slot& sl = S.ps[q].slot[head[q] % kSlots];
-      const uint32_t bs = sl.bs, n = sl.n, mode = sl.mode;
-      if (bs != pos || n == 0) { set_err(S, kTimeout); return; }
-      if (mode == 0) {
-        if (!spin_until(S, [&] { return vload(&S.flush_pos) + kRing >= bs + n; })) return;
-        uint32_t v[kBatch / 32];
+  const uint32_t n_win = (c.out_size + kWindow - 1) / kWindow;
+  for (uint32_t w = 0; w < n_win; ++w) {
+    if (!spin_until(S, [&] { return vload(&S.win_ready[w % kMapWindows]) == w + 1; })) return;
+    __threadfence_block();
+    const uint32_t we = min((w + 1) * kWindow, c.out_size);
+    for (uint32_t s0 = w * kWindow; s0 < we; s0 += kStep) {
+      const uint32_t s1 = min(s0 + kStep, we);
+      if (!spin_until(S, [&] { return vload(&S.flush_pos) + kRing >= s1; })) return;
+      // gather the whole step, then write it (a write may reuse the slot of
+      // a source read in this step)
+      uint32_t val[kStep / 128];
 #pragma unroll
-        for (uint32_t i = 0; i < kBatch / 32; ++i) {
-          const uint32_t r = lane + 32 * i;
-          if (r < n) {
-            const uint32_t d = sl.desc[r];
-            v[i] = (d & kLit) ? (d & 0xFFu) : (uint32_t)S.ring[c.ri(d)];
+      for (uint32_t i = 0; i < kStep / 128; ++i) {
+        const uint32_t e = s0 + 128 * i + 4 * lane;
+        uint32_t packed = 0;
+        if (e < s1) {
+          const uint4 m = __ldcg(reinterpret_cast<const uint4*>(c.map) + ((e & kMapMask) >> 2));
+          const uint32_t mv[4] = {m.x, m.y, m.z, m.w};
+#pragma unroll
+          for (uint32_t b = 0; b < 4; ++b) {
+            const uint32_t d = mv[b];
+            const uint32_t x = (d & kLit) ? (d & 0xFFu) : (uint32_t)S.ring[c.ri(d)];
+            packed |= x << (8 * b);
           }
         }
-        __syncwarp();
+        val[i] = packed;
+      }
+      __syncwarp();
 #pragma unroll
-        for (uint32_t i = 0; i < kBatch / 32; ++i) {
-          const uint32_t r = lane + 32 * i;
-          if (r < n) S.ring[c.ri(bs + r)] = (uint8_t)v[i];
-        }
-      } else {
-        // A long sequence can exceed the window: publish progress every 1 KiB so
-        // the flusher keeps draining while the resolver writes.
-        const uint32_t ll = sl.l_ll, lit = sl.l_lit, ml = sl.l_ml, o = sl.l_off;
-        auto publish = [&](uint32_t upto) {
-          __threadfence_block();
-          __syncwarp();
-          if (lane == 0) vstore(&S.res_pos, upto);
-        };
-        for (uint32_t k0 = 0; k0 < ll; k0 += 32) {
-          const uint32_t e = bs + k0 + 32;
-          if (!spin_until(S, [&] { return vload(&S.flush_pos) + kRing >= e; })) return;
-          const uint32_t k = k0 + lane;
-          if (k < ll) S.ring[c.ri(bs + k)] = __ldg(c.src + lit + k);
-          __syncwarp();
-          if (((k0 + 32) & 1023) == 0) publish(bs + k0 + 32);
-        }
-        const uint32_t m0 = bs + ll;
-        for (uint32_t k0 = 0; k0 < ml; k0 += 32) {
-          const uint32_t e = m0 + k0 + 32;
-          if (!spin_until(S, [&] { return vload(&S.flush_pos) + kRing >= e; })) return;
-          const uint32_t k = k0 + lane;
-          uint32_t v = 0;
-          if (k < ml) {
-            const uint32_t m = lane / o + 1;      // most recent equal byte before this step
-            v = S.ring[c.ri(m0 + k - o * m)];
-          }
-          __syncwarp();
-          if (k < ml) S.ring[c.ri(m0 + k)] = (uint8_t)v;
-          __syncwarp();
-          if (((k0 + 32) & 1023) == 0 && k0 + 32 < ml) publish(m0 + k0 + 32);
-        }
+      for (uint32_t i = 0; i < kStep / 128; ++i) {
+        const uint32_t e = s0 + 128 * i + 4 * lane;
+#pragma unroll
+        for (uint32_t b = 0; b < 4; ++b)
+          if (e + b < s1) S.ring[c.ri(e + b)] = (uint8_t)(val[i] >> (8 * b));
       }
       __threadfence_block();
       __syncwarp();
-      ++head[q];
-      if (lane == 0) {
-        vstore(&S.res_pos, bs + n);
-        vstore(&S.q_head[q], head[q]);
-      }
-      pos = bs + n;
+      if (lane == 0) vstore(&S.res_pos, s1);
     }
+    if (lane == 0) vstore(&S.res_win, w + 1);
   }
 }
 
@@ -554,7 +311,7 @@ __device__ void flusher(Smem& S, const Chunk& c, uint32_t lane) {
       const uint32_t h = min(max(head, e), avail);
       for (uint32_t i = e + lane; i < h; i += 32)
         c.dst[i] = (uint16_t)recombine(__ldg(c.sm + i), S.ring[c.ri(i)]);
-      uint32_t v0 = h;
+      const uint32_t v0 = h;
       const uint32_t units = (avail - v0) / 16;
       constexpr int kUnroll = 8;                // sign+mantissa loads in flight per lane
       for (uint32_t u0 = 0; u0 < units; u0 += 32 * kUnroll) {
@@ -600,6 +357,58 @@ __device__ void flusher(Smem& S, const Chunk& c, uint32_t lane) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// chunks without an index: one warp, straight into the output
+// ---------------------------------------------------------------------------
+// Lane 0 walks the tokens; the warp copies each sequence cooperatively.  A
+// match byte k of a copy with offset o repeats the byte at (start - o + k mod o),
+// so a copy needs no serial loop.  Sources are read back from the BF16 output
+// (exponent = bits 7..14) through L2.
+__device__ int decode_unindexed(const Chunk& c, uint32_t lane) {
+  uint32_t ip = 0, op = 0;
+  int err = 0;
+  while (op < c.out_size) {
+    Seq s;
+    if (lane == 0) err = read_seq(c.src, c.src_size, ip, s);
+    err = __shfl_sync(kFull, err, 0);
+    if (err) return err;
+    s.ll = __shfl_sync(kFull, s.ll, 0);
+    s.lit = __shfl_sync(kFull, s.lit, 0);
+    s.off = __shfl_sync(kFull, s.off, 0);
+    s.ml = __shfl_sync(kFull, s.ml, 0);
+    s.next = __shfl_sync(kFull, s.next, 0);
+    s.last = __shfl_sync(kFull, (int)s.last, 0) != 0;
+    const uint32_t lit_n = min(s.ll, c.out_size - op);
+    for (uint32_t i = lane; i < lit_n; i += 32)
+      c.dst[op + i] = (uint16_t)recombine(__ldg(c.sm + op + i), __ldg(c.src + s.lit + i));
+    op += lit_n;
+    if (op >= c.out_size) break;
+    if (s.last) return ZMOE_CHUNK_SHORT_OUTPUT;
+    if (s.off == 0 || s.off > op) return ZMOE_CHUNK_BAD_OFFSET;
+    __threadfence_block();
+    __syncwarp();
+    const uint32_t mlen = min(s.ml, c.out_size - op);
+    for (uint32_t k0 = 0; k0 < mlen; k0 += 32) {
+      const uint32_t k = k0 + lane;
+      // source: most recent copy before this 32-byte step (written already)
+      uint32_t v = 0;
+      if (k < mlen) {
+        const uint32_t base = op - s.off + (k < s.off ? k : k % s.off);
+        const uint32_t step0 = op + k0;
+        const uint32_t src = base < step0 ? base + s.off * ((step0 - 1 - base) / s.off) : base;
+        v = ((uint32_t)__ldcg(c.dst + src) >> 7) & 0xFFu;
+      }
+      __syncwarp();
+      if (k < mlen) c.dst[op + k] = (uint16_t)recombine(__ldg(c.sm + op + k), v);
+      __threadfence_block();
+      __syncwarp();
+    }
+    op += mlen;
+    ip = s.next;
+  }
+  return 0;
+}
+
 __global__ void __launch_bounds__(kWarps * 32)
 decode_kernel(const zmoe_chunk* __restrict__ chunks, int n_chunks, int32_t* __restrict__ status) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
@@ -612,24 +421,37 @@ decode_kernel(const zmoe_chunk* __restrict__ chunks, int n_chunks, int32_t* __re
   c.sm = d.sm;
   c.dst = d.dst;
   c.index = (d.index && d.n_index > 0) ? d.index : nullptr;
+  c.map = d.map;
   c.src_size = d.src_size;
   c.out_size = d.out_size;
-  c.n_seg = c.index ? d.n_index : 1;
+  c.n_index = d.n_index;
   {
     const uint32_t head = (uint32_t)((16 - (reinterpret_cast<uintptr_t>(d.sm) & 15)) & 15);
     c.rofs = (16 - head) & 15;
   }
   if (threadIdx.x == 0) {
-    S.err = (!c.src || !c.sm || !c.dst || c.src_size == 0) ? ZMOE_CHUNK_BAD_DESC : 0;
+    bool bad = !c.src || !c.sm || !c.dst || c.src_size == 0;
+    if (c.index && (!c.map || (reinterpret_cast<uintptr_t>(c.map) & 15) || d.seg_bytes != kSlice)) bad = true;
+    S.err = bad ? ZMOE_CHUNK_BAD_DESC : 0;
     S.res_pos = 0;
+    S.res_win = 0;
     S.flush_pos = 0;
-    for (int p = 0; p < kParsers; ++p) { S.q_tail[p] = 0; S.q_head[p] = 0; }
+    for (uint32_t w = 0; w < kMapWindows; ++w) S.win_ready[w] = 0;
   }
   __syncthreads();
   if (!S.err && c.out_size > 0) {
-    if (warp < kParsers) parser(S, c, warp, lane);
-    else if (warp == kResolver) resolver(S, c, lane);
-    else flusher(S, c, lane);
+    if (!c.index) {
+      if (warp == 0) {
+        const int e = decode_unindexed(c, lane);
+        if (e && lane == 0) set_err(S, e);
+      }
+    } else if (warp < kParsers) {
+      parser(S, c, warp, lane);
+    } else if (warp == kResolver) {
+      resolver(S, c, lane);
+    } else {
+      flusher(S, c, lane);
+    }
   }
   __syncthreads();
   if (threadIdx.x == 0) status[blockIdx.x] = S.err;

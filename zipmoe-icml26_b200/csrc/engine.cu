@@ -40,7 +40,7 @@ struct TensorStore {
   uint64_t sm_off = 0, numel = 0, bytes = 0;
 };
 
-constexpr uint32_t kSegBytes = 1024;
+constexpr uint32_t kSegBytes = ZMOE_SLICE_BYTES;
 
 template <class T>
 T* dmalloc(size_t n, zmoe_status* st) {
@@ -103,6 +103,8 @@ struct Layer {
   int32_t* status_host = nullptr;
   int max_desc = 0, max_waves = 0;
   int desc_cursor = 0;             // descriptors used by the current forward
+  uint32_t* map_scratch = nullptr; // decoder source-map scratch, ZMOE_MAP_ENTRIES per chunk
+  int map_cap = 0;                 // chunks the scratch can hold
   int pending_status = 0;          // descriptors whose status is still to be checked
   // host-side pass-through buffers for forward_host
   uint16_t* x_stage = nullptr;
@@ -140,7 +142,7 @@ Layer::~Layer() {
   cudaFree(tw); cudaFree(sg); cudaFree(y); cudaFree(ysh); cudaFree(xp); cudaFree(h); cudaFree(hsh);
   cudaFree(desc_dev); cudaFree(status_dev); cudaFree(wtab_dev);
   cudaFreeHost(counts_host); cudaFreeHost(desc_host); cudaFreeHost(wtab_host); cudaFreeHost(status_host);
-  cudaFree(x_stage); cudaFree(out_stage);
+  cudaFree(x_stage); cudaFree(out_stage); cudaFree(map_scratch);
   if (status_ready) cudaEventDestroy(status_ready);
   for (auto e : ev_pool) cudaEventDestroy(e);
 }
@@ -291,6 +293,7 @@ zmoe_status Layer::decode_into(const std::vector<std::pair<int, int>>& jobs, cud
         d.index = reinterpret_cast<const uint32_t*>(ts.dev + ts.idx_off[c]);
         d.n_index = ts.idx_n[c];
         d.seg_bytes = kSegBytes;
+        d.map = nullptr;                     // assigned below, one scratch area per chunk
         stats.decoded_bytes += (uint64_t)ts.block_size[c] + 3ull * ts.orig_size[c];
         e0 += ts.orig_size[c];
       }
@@ -298,6 +301,17 @@ zmoe_status Layer::decode_into(const std::vector<std::pair<int, int>>& jobs, cud
     stats.decoded_experts++;
   }
   const int cnt = nd - base;
+  if (cnt > map_cap) {
+    // grows to the largest decode seen (a synchronising allocation, only
+    // before the working set is known)
+    ZMOE_CUDA_RET(cudaStreamSynchronize(s));
+    cudaFree(map_scratch);
+    map_scratch = nullptr;
+    map_cap = 0;
+    ZMOE_CUDA_RET(cudaMalloc(&map_scratch, (size_t)cnt * ZMOE_MAP_ENTRIES * sizeof(uint32_t)));
+    map_cap = cnt;
+  }
+  for (int i = 0; i < cnt; ++i) desc_host[base + i].map = map_scratch + (size_t)i * ZMOE_MAP_ENTRIES;
   if (cnt == 0) return ZMOE_OK;
   (void)wave;
   // Descriptors and status words of every wave of one forward live side by

@@ -19,8 +19,12 @@ c_float = ctypes.c_float
 
 
 class ZmoeChunk(ctypes.Structure):
-    _fields_ = [("src", c_void_p), ("sm", c_void_p), ("dst", c_void_p), ("index", c_void_p),
+    _fields_ = [("src", c_void_p), ("sm", c_void_p), ("dst", c_void_p), ("index", c_void_p), ("map", c_void_p),
                 ("src_size", c_u32), ("out_size", c_u32), ("n_index", c_u32), ("seg_bytes", c_u32)]
+
+
+SLICE_BYTES = 256        # ZMOE_SLICE_BYTES
+MAP_ENTRIES = 32768      # ZMOE_MAP_ENTRIES
 
 
 class RouterArgs(ctypes.Structure):

@@ -46,17 +46,23 @@ def tensor_recover(exp: torch.Tensor, sm: torch.Tensor, out: Optional[torch.Tens
     return out
 
 
-SEG_BYTES = 1024
+SEG_BYTES = _lib.SLICE_BYTES
 
 
-def chunk_table(descs: Sequence[tuple], device) -> torch.Tensor:
+def map_scratch(n_chunks: int, device) -> torch.Tensor:
+    """Decoder scratch: one source-map ring (ZMOE_MAP_ENTRIES uint32) per indexed chunk."""
+    return torch.empty(max(n_chunks, 1) * _lib.MAP_ENTRIES, dtype=torch.int32, device=device)
+
+
+def chunk_table(descs: Sequence[tuple], device, scratch: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Pack (src, sm, dst, src_size, out_size[, index, n_index, seg_bytes]) tuples
-    into a device descriptor array."""
+    into a device descriptor array; indexed chunks get consecutive scratch areas."""
     arr = (ZmoeChunk * max(len(descs), 1))()
     for i, d in enumerate(descs):
         src, sm, dst, csz, osz = d[:5]
         idx, nidx, seg = d[5:8] if len(d) >= 8 else (None, 0, 0)
-        arr[i] = ZmoeChunk(src, sm, dst, idx, csz, osz, nidx, seg)
+        mp = scratch.data_ptr() + 4 * i * _lib.MAP_ENTRIES if (idx and scratch is not None) else None
+        arr[i] = ZmoeChunk(src, sm, dst, idx, mp, csz, osz, nidx, seg)
     size = ctypes.sizeof(ZmoeChunk)
     raw = torch.frombuffer(bytearray(bytes(arr)), dtype=torch.uint8)[: size * len(descs)]
     return raw.to(device)
@@ -127,8 +133,10 @@ class CompressedTensor:
         if dst is None:
             dst = torch.empty(self.numel, dtype=torch.bfloat16, device=self.blocks.device)
         d = self.descs(dst)
-        table = chunk_table(d, dst.device)
+        scratch = map_scratch(len(d), dst.device) if self.indexes is not None else None
+        table = chunk_table(d, dst.device, scratch)
         st = decode_chunks(table, len(d))
+        self._scratch = scratch                      # alive until the caller synchronises
         return dst, st
 
 
