@@ -19,11 +19,13 @@
 //    the position is the most recent equal byte before the 2 KiB step that
 //    holds it (for a run of period o, the latest earlier copy), so it is
 //    always inside the 64 KiB window; a source inside the step itself is
-//    chased through the map at parse time.  No entry depends on its own step.
-//  * Resolve (1 resolver warp + 1 flusher warp).  Per 2 KiB step the resolver
-//    reads 2048 map entries (coalesced 128-bit loads) and gathers each byte
-//    from a 64 KiB shared-memory window of decoded exponents, then writes the
-//    step into the window.  The flusher follows, merging 16 exponent bytes
+//    recorded in a shared-memory list and chased through the map once the
+//    window is mapped.  No entry depends on its own step.
+//  * Resolve (1 resolver warp + 1 flusher warp).  The map entries of the next
+//    2 KiB step are copied into shared memory (cp.async) while the resolver
+//    gathers the current step's bytes from a 64 KiB shared-memory window of
+//    decoded exponents and writes them back into the window.  The flusher
+//    follows, merging 16 exponent bytes
 //    with 16 sign+mantissa bytes (128-bit loads) into BF16 (two 128-bit
 //    stores per lane); the resolver never overwrites a byte the flusher has
 //    not consumed.
@@ -61,8 +63,13 @@ constexpr int32_t kTimeout = 5;
 
 static_assert((kMapEntries & (kMapEntries - 1)) == 0 && kMapWindows >= 2, "map ring");
 
+constexpr uint32_t kChaseCap = 256;           // in-step sources recorded per parser window
+
 struct Smem {
   uint8_t ring[kRing];
+  __align__(16) uint32_t mbuf[2][kStep];      // resolver: map entries of the current/next step
+  uint32_t chase[kParsers][kChaseCap];        // positions whose source lies inside their step
+  uint32_t n_chase[kParsers];
   uint32_t win_ready[kMapWindows];            // window w mapped: win_ready[w % n] == w + 1
   uint32_t res_pos;                           // bytes [0, res_pos) resolved into the ring
   uint32_t res_win;                           // windows fully resolved (map slots reusable)
@@ -161,7 +168,7 @@ __device__ void parser(Smem& S, const Chunk& c, int p, uint32_t lane) {
     const uint32_t b0 = g * kSlice;
     const uint32_t b1 = min(b0 + kSlice, c.out_size);
     int err = 0;
-    bool inner = false;
+    bool overflow = false;
     if (b0 < c.out_size) {
       if (g >= c.n_index) {
         err = ZMOE_CHUNK_BAD_DESC;
@@ -169,8 +176,19 @@ __device__ void parser(Smem& S, const Chunk& c, int p, uint32_t lane) {
         uint32_t ip = __ldg(c.index + 2 * g);
         uint32_t so = __ldg(c.index + 2 * g + 1);     // output start of the sequence at ip
         uint32_t e = b0;
-        uint4 buf;                                    // 4 entries per 128-bit store
-        uint32_t* bv = reinterpret_cast<uint32_t*>(&buf);
+        uint32_t r0 = 0, r1 = 0, r2 = 0;              // entries waiting for a 128-bit store
+        auto put = [&](uint32_t pos, uint32_t v) {
+          switch (pos & 3) {
+            case 0: r0 = v; break;
+            case 1: r1 = v; break;
+            case 2: r2 = v; break;
+            default: reinterpret_cast<uint4*>(c.map)[(pos & kMapMask) >> 2] = make_uint4(r0, r1, r2, v);
+          }
+        };
+        auto note_inner = [&](uint32_t pos) {         // chase this position after the window
+          const uint32_t slot = atomicAdd(&S.n_chase[p], 1u);
+          if (slot < kChaseCap) S.chase[p][slot] = pos; else overflow = true;
+        };
         if (so > b0) err = ZMOE_CHUNK_BAD_DESC;
         while (!err && e < b1) {
           Seq s;
@@ -178,27 +196,26 @@ __device__ void parser(Smem& S, const Chunk& c, int p, uint32_t lane) {
           if (err) break;
           const uint32_t ms = so + s.ll;              // first match byte
           const uint32_t me = ms + s.ml;
-          if (s.ml > 0 && (s.off == 0 || s.off > ms)) { err = ZMOE_CHUNK_BAD_OFFSET; break; }
+          const uint32_t o = s.off;
+          if (s.ml > 0 && (o == 0 || o > ms)) { err = ZMOE_CHUNK_BAD_OFFSET; break; }
           // literals
-          for (; e < b1 && e < ms; ++e) {
-            bv[e & 3] = kLit | __ldg(c.src + s.lit + (e - so));
-            if ((e & 3) == 3) reinterpret_cast<uint4*>(c.map)[(e & kMapMask) >> 2] = buf;
-          }
-          // match bytes: the latest byte before the step that repeats e
+          for (; e < b1 && e < ms; ++e) put(e, kLit | __ldg(c.src + s.lit + (e - so)));
+          // match bytes: a byte with the same value before the 2 KiB step of e
           for (; e < b1 && e < me; ++e) {
             const uint32_t step0 = e & ~(kStep - 1);
-            const uint32_t o = s.off;
             const uint32_t k = e - ms;
-            const uint32_t base = ms - o + (k < o ? k : k % o);   // first copy, in [ms - o, ms)
             uint32_t v;
-            if (base < step0) {
-              v = base + o * ((step0 - 1 - base) / o);            // latest copy below the step
-            } else {
-              v = kInner | base;                                  // inside the step: chase later
-              inner = true;
+            if (k < o) {                              // plain copy: the source itself
+              v = e - o;
+            } else {                                  // overlapping copy of period o
+              const uint32_t base = ms - o + k % o;  // first copy, in [ms - o, ms)
+              v = base < step0 ? base + o * ((step0 - 1 - base) / o) : base;   // latest below the step
             }
-            bv[e & 3] = v;
-            if ((e & 3) == 3) reinterpret_cast<uint4*>(c.map)[(e & kMapMask) >> 2] = buf;
+            if (v >= step0) {                         // inside the step: chase after the window
+              note_inner(e);
+              v |= kInner;
+            }
+            put(e, v);
           }
           if (e < b1) {
             if (s.last) { err = ZMOE_CHUNK_SHORT_OUTPUT; break; }
@@ -207,7 +224,10 @@ __device__ void parser(Smem& S, const Chunk& c, int p, uint32_t lane) {
           }
         }
         if (!err && (e & 3)) {                        // partial group at the chunk end
-          for (uint32_t i = e & ~3u; i < e; ++i) c.map[i & kMapMask] = bv[i & 3];
+          const uint32_t i0 = e & ~3u;
+          c.map[i0 & kMapMask] = r0;
+          if (e - i0 > 1) c.map[(i0 + 1) & kMapMask] = r1;
+          if (e - i0 > 2) c.map[(i0 + 2) & kMapMask] = r2;
         }
       }
     }
@@ -216,21 +236,27 @@ __device__ void parser(Smem& S, const Chunk& c, int p, uint32_t lane) {
       set_err(S, __shfl_sync(kFull, err, __ffs(emask) - 1));
       return;
     }
-    // chase sources inside the same 2 KiB step (entries of any lane of this warp)
-    if (__any_sync(kFull, inner)) {
-      __threadfence_block();
-      __syncwarp();
-      if (inner) {
-        for (uint32_t i = b0; i < b1; ++i) {
-          uint32_t v = __ldcg(c.map + (i & kMapMask));
-          if (!(v & kInner)) continue;
-          uint32_t steps = 0;
-          while ((v & kInner) && steps++ < kStep) v = __ldcg(c.map + ((v & ~kInner) & kMapMask));
-          if (v & kInner) { set_err(S, kTimeout); break; }
-          c.map[i & kMapMask] = v;
-        }
-      }
+    // chase sources inside the same 2 KiB step through the map (written by any
+    // lane of this warp) until a literal or a byte before the step
+    __threadfence_block();
+    __syncwarp();
+    const uint32_t n_list = min(vload(&S.n_chase[p]), kChaseCap);
+    const bool full_scan = __any_sync(kFull, overflow);
+    auto chase_one = [&](uint32_t i) {
+      uint32_t v = __ldcg(c.map + (i & kMapMask));
+      if (!(v & kInner)) return;
+      uint32_t steps = 0;
+      while ((v & kInner) && steps++ < kStep) v = __ldcg(c.map + ((v & ~kInner) & kMapMask));
+      if (v & kInner) { set_err(S, kTimeout); return; }
+      c.map[i & kMapMask] = v;
+    };
+    if (!full_scan) {
+      for (uint32_t q = lane; q < n_list; q += 32) chase_one(S.chase[p][q]);
+    } else {
+      for (uint32_t i = b0; i < b1; ++i) chase_one(i);
     }
+    __syncwarp();
+    if (lane == 0) vstore(&S.n_chase[p], 0);
     __threadfence_block();
     __syncwarp();
     if (lane == 0) vstore(&S.win_ready[w % kMapWindows], w + 1);
@@ -240,48 +266,93 @@ __device__ void parser(Smem& S, const Chunk& c, int p, uint32_t lane) {
 // ---------------------------------------------------------------------------
 // resolver warp
 // ---------------------------------------------------------------------------
-__device__ void resolver(Smem& S, const Chunk& c, uint32_t lane) {
-  const uint32_t n_win = (c.out_size + kWindow - 1) / kWindow;
-  for (uint32_t w = 0; w < n_win; ++w) {
-    if (!spin_until(S, [&] { return vload(&S.win_ready[w % kMapWindows]) == w + 1; })) return;
-    __threadfence_block();
-    const uint32_t we = min((w + 1) * kWindow, c.out_size);
-    for (uint32_t s0 = w * kWindow; s0 < we; s0 += kStep) {
-      const uint32_t s1 = min(s0 + kStep, we);
-      if (!spin_until(S, [&] { return vload(&S.flush_pos) + kRing >= s1; })) return;
-      // gather the whole step, then write it (a write may reuse the slot of
-      // a source read in this step)
-      uint32_t val[kStep / 128];
-#pragma unroll
-      for (uint32_t i = 0; i < kStep / 128; ++i) {
-        const uint32_t e = s0 + 128 * i + 4 * lane;
-        uint32_t packed = 0;
-        if (e < s1) {
-          const uint4 m = __ldcg(reinterpret_cast<const uint4*>(c.map) + ((e & kMapMask) >> 2));
-          const uint32_t mv[4] = {m.x, m.y, m.z, m.w};
-#pragma unroll
-          for (uint32_t b = 0; b < 4; ++b) {
-            const uint32_t d = mv[b];
-            const uint32_t x = (d & kLit) ? (d & 0xFFu) : (uint32_t)S.ring[c.ri(d)];
-            packed |= x << (8 * b);
-          }
-        }
-        val[i] = packed;
-      }
-      __syncwarp();
-#pragma unroll
-      for (uint32_t i = 0; i < kStep / 128; ++i) {
-        const uint32_t e = s0 + 128 * i + 4 * lane;
-#pragma unroll
-        for (uint32_t b = 0; b < 4; ++b)
-          if (e + b < s1) S.ring[c.ri(e + b)] = (uint8_t)(val[i] >> (8 * b));
-      }
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+// Copy the map entries of step t (2048 x 4 bytes, contiguous in the ring) to mbuf[t & 1].
+__device__ __forceinline__ void fetch_step(Smem& S, const Chunk& c, uint32_t t, uint32_t lane) {
+  const uint32_t* src = c.map + ((t * kStep) & kMapMask);
+  uint32_t* dst = S.mbuf[t & 1];
+  for (uint32_t q = lane; q < kStep / 4; q += 32) cp_async16(dst + 4 * q, src + 4 * q);
+  cp_async_commit();
+}
+
+__device__ void resolver_body(Smem& S, const Chunk& c, uint32_t lane) {
+  const uint32_t n_steps = (c.out_size + kStep - 1) / kStep;
+  constexpr uint32_t kStepsPerWin = kWindow / kStep;
+  auto ready = [&](uint32_t t) {
+    const uint32_t w = t / kStepsPerWin;
+    return vload(&S.win_ready[w % kMapWindows]) == w + 1;
+  };
+  // map entries of step t + 1 are copied while step t resolves
+  if (!spin_until(S, [&] { return ready(0); })) return;
+  __threadfence_block();
+  fetch_step(S, c, 0, lane);
+  bool have_next = true;                              // a copy for step t is in flight
+  for (uint32_t t = 0; t < n_steps; ++t) {
+    const uint32_t s0 = t * kStep, s1 = min(s0 + kStep, c.out_size);
+    if (!have_next) {
+      if (!spin_until(S, [&] { return ready(t); })) return;
       __threadfence_block();
-      __syncwarp();
-      if (lane == 0) vstore(&S.res_pos, s1);
+      fetch_step(S, c, t, lane);
     }
-    if (lane == 0) vstore(&S.res_win, w + 1);
+    have_next = false;
+    if (t + 1 < n_steps && ready(t + 1)) {
+      __threadfence_block();
+      fetch_step(S, c, t + 1, lane);
+      have_next = true;
+      cp_async_wait1();
+    } else {
+      cp_async_wait0();
+    }
+    __syncwarp();
+    if (!spin_until(S, [&] { return vload(&S.flush_pos) + kRing >= s1; })) return;
+    // gather the whole step, then write it (a write may reuse the window slot
+    // of a source read in this step)
+    const uint32_t* mb = S.mbuf[t & 1];
+    uint32_t val[kStep / 128];
+#pragma unroll
+    for (uint32_t i = 0; i < kStep / 128; ++i) {
+      const uint32_t r = 128 * i + 4 * lane;
+      const uint4 m = *reinterpret_cast<const uint4*>(mb + r);
+      const uint32_t mv[4] = {m.x, m.y, m.z, m.w};
+      uint32_t packed = 0;
+#pragma unroll
+      for (uint32_t b = 0; b < 4; ++b) {
+        const uint32_t d = mv[b];
+        uint32_t x = d & 0xFFu;
+        if (!(d & kLit) && s0 + r + b < s1) x = S.ring[c.ri(d)];
+        packed |= x << (8 * b);
+      }
+      val[i] = packed;
+    }
+    __syncwarp();
+#pragma unroll
+    for (uint32_t i = 0; i < kStep / 128; ++i) {
+      const uint32_t e = s0 + 128 * i + 4 * lane;
+#pragma unroll
+      for (uint32_t b = 0; b < 4; ++b)
+        if (e + b < s1) S.ring[c.ri(e + b)] = (uint8_t)(val[i] >> (8 * b));
+    }
+    __threadfence_block();
+    __syncwarp();
+    if (lane == 0) {
+      vstore(&S.res_pos, s1);
+      if (s1 == c.out_size || (s1 % kWindow) == 0) vstore(&S.res_win, (s1 + kWindow - 1) / kWindow);
+    }
   }
+}
+
+// Every exit waits for the resolver's own asynchronous copies into shared memory.
+__device__ void resolver(Smem& S, const Chunk& c, uint32_t lane) {
+  resolver_body(S, c, lane);
+  cp_async_wait0();
+  __syncwarp();
 }
 
 // ---------------------------------------------------------------------------
@@ -437,6 +508,7 @@ decode_kernel(const zmoe_chunk* __restrict__ chunks, int n_chunks, int32_t* __re
     S.res_win = 0;
     S.flush_pos = 0;
     for (uint32_t w = 0; w < kMapWindows; ++w) S.win_ready[w] = 0;
+    for (int p = 0; p < kParsers; ++p) S.n_chase[p] = 0;
   }
   __syncthreads();
   if (!S.err && c.out_size > 0) {
