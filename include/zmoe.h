@@ -68,7 +68,7 @@ zmoe_status zmoe_tensor_recover(uint16_t* out, const uint8_t* exp, const uint8_t
  * BF16 straight into the destination slot.
  * ------------------------------------------------------------------------ */
 #define ZMOE_SLICE_BYTES 256      /* output bytes per slice-index entry */
-#define ZMOE_MAP_ENTRIES 32768    /* uint32 scratch entries per indexed chunk (128 KiB) */
+#define ZMOE_MAP_ENTRIES 65536    /* uint32 scratch entries per indexed chunk (256 KiB) */
 
 typedef struct zmoe_chunk {
   const uint8_t* src;   /* LZ4 block, device memory */

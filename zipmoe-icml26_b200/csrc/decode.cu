@@ -6,74 +6,71 @@
 // kernel (csrc/kernels/tensor_recover.cu:12-43) reading both planes over
 // zero-copy host memory.
 //
-// LZ4HC matches chain back through earlier matches (median offset ~20 KB), so
-// the bytes of a block depend on each other almost serially; the token stream
-// does not.  One CTA of 6 warps decodes one block in two overlapped stages:
+// Exponent planes compress into many short sequences (about one per 7 output
+// bytes, 92% of the bytes in matches, match chains tens deep), so the bytes of
+// a block depend on each other almost serially while the token stream does
+// not.  One CTA of 256 threads decodes one block, 64 KiB of output (a region)
+// at a time, in four barrier-separated phases:
 //
-//  * Source map (4 parser warps).  A slice index built when the block is
-//    loaded (zmoe_lz4_build_index) names, for every 256 output bytes, the
-//    sequence that contains that byte.  Each lane parses one 256-byte slice on
-//    its own (a parser warp covers an 8 KiB window) and writes one 32-bit
-//    entry per output byte into a map ring in L2-resident scratch: a literal
-//    value, or the position of a byte with the same value.  For a match byte
-//    the position is the most recent equal byte before the 2 KiB step that
-//    holds it (for a run of period o, the latest earlier copy), so it is
-//    always inside the 64 KiB window; a source inside the step itself is
-//    recorded in a shared-memory list and chased through the map once the
-//    window is mapped.  No entry depends on its own step.
-//  * Resolve (1 resolver warp + 1 flusher warp).  The map entries of the next
-//    2 KiB step are copied into shared memory (cp.async) while the resolver
-//    gathers the current step's bytes from a 64 KiB shared-memory window of
-//    decoded exponents and writes them back into the window.  The flusher
-//    follows, merging 16 exponent bytes
-//    with 16 sign+mantissa bytes (128-bit loads) into BF16 (two 128-bit
-//    stores per lane); the resolver never overwrites a byte the flusher has
-//    not consumed.
+//  1. Stage: the region's compressed bytes are copied into shared memory
+//     (cp.async, issued while the previous region is being flushed).
+//  2. Map: a slice index built when the block is loaded (zmoe_lz4_build_index)
+//     names, for every 256 output bytes, the sequence that contains the first
+//     of them.  Each thread parses one slice on its own and writes one 32-bit
+//     entry per output byte into a per-chunk map in L2-resident scratch: a
+//     literal value, or the position of an earlier byte with the same value.
+//     For a match byte that position is the latest equal byte before the
+//     2 KiB step holding it when one exists (a run of period o repeats every
+//     o bytes), so it is always resolved already; otherwise it is the first
+//     copy of the run, inside the step, and is marked for a chase.
+//  3. Resolve: step by step (2 KiB, 8 bytes per thread), the entries are
+//     copied into shared memory (cp.async, one step ahead) and every byte is
+//     gathered from a 64 KiB shared-memory window of decoded exponents; marked
+//     entries first follow the step's own entries back to a literal or to a
+//     byte before the step.  The whole step is gathered before it is written.
+//  4. Flush: 16 exponent bytes and 16 sign+mantissa bytes (128-bit loads)
+//     become 16 BF16 values (two 128-bit stores) per thread and group.
 //
 // A chunk without an index (zmoe_chunk.index == NULL) is decoded by warp 0
 // alone in one pass straight into the output (no scratch needed).
 //
-// Roles synchronise through counters in shared memory; every wait is bounded
-// and gives up with an error status.  Errors (bad offsets, lengths past the
-// block, a block ending short of out_size) set the chunk's status word; the
-// kernel never traps.  Output past out_size is clipped (the targetOutputSize
-// = out_size behaviour of LZ4_decompress_safe_partial).
+// There are no inter-warp flags and no waits other than barriers and the
+// completion of the CTA's own asynchronous copies.  Errors (bad offsets,
+// lengths past the block, a block ending short of out_size, an index that
+// does not match the block) set the chunk's status word; the kernel never
+// traps.  Output past out_size is clipped (the targetOutputSize = out_size
+// behaviour of LZ4_decompress_safe_partial).
 #include "common.cuh"
 
 namespace zmoe {
 namespace {
 
-constexpr int kParsers = 4;
-constexpr int kWarps = kParsers + 2;          // parsers, resolver, flusher
-constexpr int kResolver = kParsers;           // warp kParsers + 1 is the flusher
-constexpr uint32_t kSlice = 256;              // output bytes parsed by one lane
-constexpr uint32_t kWindow = 32 * kSlice;     // output bytes mapped by one parser pass
-constexpr uint32_t kStep = 2048;              // output bytes resolved per resolver step
-constexpr uint32_t kRing = 65536;             // decoded-exponent window
+constexpr int kThreads = 256;
+constexpr uint32_t kSlice = 256;                    // output bytes parsed by one thread
+constexpr uint32_t kRegion = kThreads * kSlice;     // output bytes per region (64 KiB)
+constexpr uint32_t kStep = 2048;                    // output bytes resolved per step
+constexpr uint32_t kPerThread = kStep / kThreads;   // bytes resolved per thread and step
+constexpr uint32_t kRing = 65536;                   // decoded-exponent window
 constexpr uint32_t kRingMask = kRing - 1;
-constexpr uint32_t kMapEntries = ZMOE_MAP_ENTRIES;   // source-map ring per chunk (scratch)
-constexpr uint32_t kMapMask = kMapEntries - 1;
-static_assert(kSlice == ZMOE_SLICE_BYTES, "slice index granularity");
-constexpr uint32_t kMapWindows = kMapEntries / kWindow;
-constexpr uint32_t kLit = 0x80000000u;        // map entry: literal value in bits 0..7
-constexpr uint32_t kInner = 0x40000000u;      // map entry (parse time only): source inside its step
-constexpr long long kSpinCycles = 2000000000LL;   // ~1 s at 1.9 GHz
+constexpr uint32_t kStage = 48 * 1024;              // staged compressed bytes per region
+constexpr uint32_t kLit = 0x80000000u;              // map entry: literal value in bits 0..7
+constexpr uint32_t kInner = 0x40000000u;            // map entry: source inside its own step
+constexpr uint32_t kPosMask = kInner - 1;
 constexpr unsigned kFull = 0xffffffffu;
-constexpr int32_t kTimeout = 5;
 
-static_assert((kMapEntries & (kMapEntries - 1)) == 0 && kMapWindows >= 2, "map ring");
-
-constexpr uint32_t kChaseCap = 256;           // in-step sources recorded per parser window
+static_assert(kSlice == ZMOE_SLICE_BYTES, "slice index granularity");
+static_assert(kRegion == ZMOE_MAP_ENTRIES, "one map entry per byte of a region");
+static_assert(kRegion <= kRing, "a region's sources stay inside the window");
+static_assert(kStep % kSlice == 0 && kRegion % kStep == 0, "slices nest in steps nest in regions");
+static_assert(kPerThread == 8, "two 128-bit map loads per thread and step");
+static_assert(2 * kStep * 4 <= kStage, "map double buffer fits the staging area");
 
 struct Smem {
   uint8_t ring[kRing];
-  __align__(16) uint32_t mbuf[2][kStep];      // resolver: map entries of the current/next step
-  uint32_t chase[kParsers][kChaseCap];        // positions whose source lies inside their step
-  uint32_t n_chase[kParsers];
-  uint32_t win_ready[kMapWindows];            // window w mapped: win_ready[w % n] == w + 1
-  uint32_t res_pos;                           // bytes [0, res_pos) resolved into the ring
-  uint32_t res_win;                           // windows fully resolved (map slots reusable)
-  uint32_t flush_pos;                         // bytes [0, flush_pos) consumed by the flusher
+  union {
+    uint8_t stage[kStage];                          // phase 2: compressed bytes of the region
+    uint32_t mbuf[2][kStep];                        // phase 3: map entries of this/next step
+  } u;
   int32_t err;
 };
 
@@ -85,30 +82,19 @@ struct Chunk {
   uint32_t* map;
   uint32_t src_size, out_size, n_index;
   uint32_t rofs;   // ring index of position i is (i + rofs) & kRingMask; makes 16-byte
-                   // groups that the flusher loads aligned both in the ring and in memory
+                   // groups that the flush loads aligned both in the ring and in memory
   __device__ __forceinline__ uint32_t ri(uint32_t pos) const { return (pos + rofs) & kRingMask; }
 };
 
-__device__ __forceinline__ uint32_t vload(const uint32_t* p) { return *(const volatile uint32_t*)p; }
-__device__ __forceinline__ void vstore(uint32_t* p, uint32_t v) { *(volatile uint32_t*)p = v; }
-__device__ __forceinline__ bool failed(Smem& S) { return *(volatile int32_t*)&S.err != 0; }
 __device__ __forceinline__ void set_err(Smem& S, int32_t code) { atomicCAS(&S.err, 0, code); }
 
-// Spin (bounded) until cond() holds; false on error or timeout.
-template <class F>
-__device__ __forceinline__ bool spin_until(Smem& S, F cond) {
-  if (cond()) return true;
-  const long long t0 = clock64();
-  while (!cond()) {
-    if (failed(S)) return false;
-    if (clock64() - t0 > kSpinCycles) {
-      set_err(S, kTimeout);
-      return false;
-    }
-    __nanosleep(64);
-  }
-  return true;
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+               : "memory");
 }
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
 // One LZ4 sequence header at ip: literal count and position, match offset and
 // length, position of the next token.  Returns 0 or a ZMOE_CHUNK_* error.
@@ -117,16 +103,17 @@ struct Seq {
   bool last;
 };
 
-__device__ __forceinline__ int read_seq(const uint8_t* __restrict__ src, uint32_t size, uint32_t ip, Seq& s) {
+template <class ByteAt>
+__device__ __forceinline__ int read_seq(ByteAt byte_at, uint32_t size, uint32_t ip, Seq& s) {
   if (ip >= size) return ZMOE_CHUNK_INPUT_OVERRUN;
-  const uint32_t tok = __ldg(src + ip);
+  const uint32_t tok = byte_at(ip);
   uint32_t q = ip + 1;
   uint32_t ll = tok >> 4;
   if (ll == 15) {
     uint32_t b;
     do {
       if (q >= size) return ZMOE_CHUNK_INPUT_OVERRUN;
-      b = __ldg(src + q++);
+      b = byte_at(q++);
       ll += b;
     } while (b == 255 && ll < (1u << 30));
   }
@@ -139,14 +126,14 @@ __device__ __forceinline__ int read_seq(const uint8_t* __restrict__ src, uint32_
   s.last = q == size;
   if (!s.last) {
     if (q + 2 > size) return ZMOE_CHUNK_INPUT_OVERRUN;
-    s.off = __ldg(src + q) | ((uint32_t)__ldg(src + q + 1) << 8);
+    s.off = byte_at(q) | (byte_at(q + 1) << 8);
     q += 2;
     uint32_t ml = tok & 15;
     if (ml == 15) {
       uint32_t b;
       do {
         if (q >= size) return ZMOE_CHUNK_INPUT_OVERRUN;
-        b = __ldg(src + q++);
+        b = byte_at(q++);
         ml += b;
       } while (b == 255 && ml < (1u << 30));
     }
@@ -157,206 +144,156 @@ __device__ __forceinline__ int read_seq(const uint8_t* __restrict__ src, uint32_
 }
 
 // ---------------------------------------------------------------------------
-// parser warps: source map
+// phase 1: stage the compressed bytes of region r
 // ---------------------------------------------------------------------------
-__device__ void parser(Smem& S, const Chunk& c, int p, uint32_t lane) {
-  const uint32_t n_win = (c.out_size + kWindow - 1) / kWindow;
-  for (uint32_t w = p; w < n_win; w += kParsers) {
-    // the map slots of window w are free once window w - kMapWindows is resolved
-    if (w >= kMapWindows && !spin_until(S, [&] { return vload(&S.res_win) > w - kMapWindows; })) return;
-    const uint32_t g = w * 32 + lane;                 // slice of this lane
-    const uint32_t b0 = g * kSlice;
-    const uint32_t b1 = min(b0 + kSlice, c.out_size);
-    int err = 0;
-    bool overflow = false;
-    if (b0 < c.out_size) {
-      if (g >= c.n_index) {
-        err = ZMOE_CHUNK_BAD_DESC;
-      } else {
-        uint32_t ip = __ldg(c.index + 2 * g);
-        uint32_t so = __ldg(c.index + 2 * g + 1);     // output start of the sequence at ip
-        uint32_t e = b0;
-        uint32_t r0 = 0, r1 = 0, r2 = 0;              // entries waiting for a 128-bit store
-        auto put = [&](uint32_t pos, uint32_t v) {
-          switch (pos & 3) {
-            case 0: r0 = v; break;
-            case 1: r1 = v; break;
-            case 2: r2 = v; break;
-            default: reinterpret_cast<uint4*>(c.map)[(pos & kMapMask) >> 2] = make_uint4(r0, r1, r2, v);
-          }
-        };
-        auto note_inner = [&](uint32_t pos) {         // chase this position after the window
-          const uint32_t slot = atomicAdd(&S.n_chase[p], 1u);
-          if (slot < kChaseCap) S.chase[p][slot] = pos; else overflow = true;
-        };
-        if (so > b0) err = ZMOE_CHUNK_BAD_DESC;
-        while (!err && e < b1) {
-          Seq s;
-          err = read_seq(c.src, c.src_size, ip, s);
-          if (err) break;
-          const uint32_t ms = so + s.ll;              // first match byte
-          const uint32_t me = ms + s.ml;
-          const uint32_t o = s.off;
-          if (s.ml > 0 && (o == 0 || o > ms)) { err = ZMOE_CHUNK_BAD_OFFSET; break; }
-          // literals
-          for (; e < b1 && e < ms; ++e) put(e, kLit | __ldg(c.src + s.lit + (e - so)));
-          // match bytes: a byte with the same value before the 2 KiB step of e
-          for (; e < b1 && e < me; ++e) {
-            const uint32_t step0 = e & ~(kStep - 1);
-            const uint32_t k = e - ms;
-            uint32_t v;
-            if (k < o) {                              // plain copy: the source itself
-              v = e - o;
-            } else {                                  // overlapping copy of period o
-              const uint32_t base = ms - o + k % o;  // first copy, in [ms - o, ms)
-              v = base < step0 ? base + o * ((step0 - 1 - base) / o) : base;   // latest below the step
-            }
-            if (v >= step0) {                         // inside the step: chase after the window
-              note_inner(e);
-              v |= kInner;
-            }
-            put(e, v);
-          }
-          if (e < b1) {
-            if (s.last) { err = ZMOE_CHUNK_SHORT_OUTPUT; break; }
-            ip = s.next;
-            so = me;
-          }
-        }
-        if (!err && (e & 3)) {                        // partial group at the chunk end
-          const uint32_t i0 = e & ~3u;
-          c.map[i0 & kMapMask] = r0;
-          if (e - i0 > 1) c.map[(i0 + 1) & kMapMask] = r1;
-          if (e - i0 > 2) c.map[(i0 + 2) & kMapMask] = r2;
-        }
-      }
-    }
-    const unsigned emask = __ballot_sync(kFull, err != 0);
-    if (emask) {
-      set_err(S, __shfl_sync(kFull, err, __ffs(emask) - 1));
-      return;
-    }
-    // chase sources inside the same 2 KiB step through the map (written by any
-    // lane of this warp) until a literal or a byte before the step
-    __threadfence_block();
-    __syncwarp();
-    const uint32_t n_list = min(vload(&S.n_chase[p]), kChaseCap);
-    const bool full_scan = __any_sync(kFull, overflow);
-    auto chase_one = [&](uint32_t i) {
-      uint32_t v = __ldcg(c.map + (i & kMapMask));
-      if (!(v & kInner)) return;
-      uint32_t steps = 0;
-      while ((v & kInner) && steps++ < kStep) v = __ldcg(c.map + ((v & ~kInner) & kMapMask));
-      if (v & kInner) { set_err(S, kTimeout); return; }
-      c.map[i & kMapMask] = v;
-    };
-    if (!full_scan) {
-      for (uint32_t q = lane; q < n_list; q += 32) chase_one(S.chase[p][q]);
-    } else {
-      for (uint32_t i = b0; i < b1; ++i) chase_one(i);
-    }
-    __syncwarp();
-    if (lane == 0) vstore(&S.n_chase[p], 0);
-    __threadfence_block();
-    __syncwarp();
-    if (lane == 0) vstore(&S.win_ready[w % kMapWindows], w + 1);
-  }
+// The region's sequences start in [index[g0].in, index[g0 + 256].in]; the last
+// one's header and literals may run past that, so a margin is staged too and
+// anything beyond the staged range is read from global memory.
+struct StageRange {
+  uint32_t lo, len;   // compressed bytes [lo, lo + len) are in S.u.stage
+};
+
+__device__ __forceinline__ StageRange stage_range(const Chunk& c, uint32_t r) {
+  StageRange st{0, 0};
+  const uint32_t g0 = r * kThreads;
+  if (g0 >= c.n_index) return st;
+  const uint32_t in_lo = __ldg(c.index + 2 * g0);
+  const uint32_t in_hi = g0 + kThreads < c.n_index ? __ldg(c.index + 2 * (g0 + kThreads)) : c.src_size;
+  const uint32_t lo = in_lo & ~15u;
+  if (lo >= c.src_size) return st;
+  const uint32_t full = (c.src_size - lo) & ~15u;                 // whole 16-byte units inside the block
+  const uint32_t want = (uint32_t)min((uint64_t)in_hi + 256 - lo, (uint64_t)kStage);
+  st.lo = lo;
+  st.len = min(full, (want + 15) & ~15u);
+  return st;
 }
 
-// ---------------------------------------------------------------------------
-// resolver warp
-// ---------------------------------------------------------------------------
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
-
-// Copy the map entries of step t (2048 x 4 bytes, contiguous in the ring) to mbuf[t & 1].
-__device__ __forceinline__ void fetch_step(Smem& S, const Chunk& c, uint32_t t, uint32_t lane) {
-  const uint32_t* src = c.map + ((t * kStep) & kMapMask);
-  uint32_t* dst = S.mbuf[t & 1];
-  for (uint32_t q = lane; q < kStep / 4; q += 32) cp_async16(dst + 4 * q, src + 4 * q);
+__device__ __forceinline__ void stage_issue(Smem& S, const Chunk& c, const StageRange& st) {
+  for (uint32_t q = 16 * threadIdx.x; q < st.len; q += 16 * kThreads) cp_async16(S.u.stage + q, c.src + st.lo + q);
   cp_async_commit();
 }
 
-__device__ void resolver_body(Smem& S, const Chunk& c, uint32_t lane) {
-  const uint32_t n_steps = (c.out_size + kStep - 1) / kStep;
-  constexpr uint32_t kStepsPerWin = kWindow / kStep;
-  auto ready = [&](uint32_t t) {
-    const uint32_t w = t / kStepsPerWin;
-    return vload(&S.win_ready[w % kMapWindows]) == w + 1;
+// ---------------------------------------------------------------------------
+// phase 2: map one 256-byte slice per thread
+// ---------------------------------------------------------------------------
+__device__ int map_slice(Smem& S, const Chunk& c, const StageRange& st, uint32_t g) {
+  const uint32_t b0 = g * kSlice;
+  if (b0 >= c.out_size) return 0;
+  if (g >= c.n_index) return ZMOE_CHUNK_BAD_DESC;
+  const uint2 ix = __ldg(reinterpret_cast<const uint2*>(c.index) + g);
+  uint32_t ip = ix.x;
+  uint32_t so = ix.y;                                  // output start of the sequence at ip
+  if (so > b0) return ZMOE_CHUNK_BAD_DESC;
+  const uint32_t b1 = min(b0 + kSlice, c.out_size);
+  const uint32_t step0 = b0 & ~(kStep - 1);            // a slice lies inside one step
+  const uint8_t* stage = S.u.stage;
+  auto byte_at = [&](uint32_t q) -> uint32_t {
+    const uint32_t d = q - st.lo;
+    return d < st.len ? (uint32_t)stage[d] : (uint32_t)__ldg(c.src + q);
   };
-  // map entries of step t + 1 are copied while step t resolves
-  if (!spin_until(S, [&] { return ready(0); })) return;
-  __threadfence_block();
-  fetch_step(S, c, 0, lane);
-  bool have_next = true;                              // a copy for step t is in flight
-  for (uint32_t t = 0; t < n_steps; ++t) {
-    const uint32_t s0 = t * kStep, s1 = min(s0 + kStep, c.out_size);
-    if (!have_next) {
-      if (!spin_until(S, [&] { return ready(t); })) return;
-      __threadfence_block();
-      fetch_step(S, c, t, lane);
+  uint4* map4 = reinterpret_cast<uint4*>(c.map);
+  uint32_t e = b0;
+  uint32_t r0 = 0, r1 = 0, r2 = 0;                     // entries waiting for a 128-bit store
+  auto put = [&](uint32_t pos, uint32_t v) {
+    switch (pos & 3) {
+      case 0: r0 = v; break;
+      case 1: r1 = v; break;
+      case 2: r2 = v; break;
+      default: map4[(pos & (kRegion - 1)) >> 2] = make_uint4(r0, r1, r2, v);
     }
-    have_next = false;
-    if (t + 1 < n_steps && ready(t + 1)) {
-      __threadfence_block();
-      fetch_step(S, c, t + 1, lane);
-      have_next = true;
+  };
+  while (e < b1) {
+    Seq s;
+    const int err = read_seq(byte_at, c.src_size, ip, s);
+    if (err) return err;
+    const uint32_t ms = so + s.ll;                     // first match byte
+    const uint32_t me = ms + s.ml;
+    const uint32_t o = s.off;
+    if (s.ml > 0 && (o == 0 || o > ms)) return ZMOE_CHUNK_BAD_OFFSET;
+    // literals
+    for (const uint32_t le = min(b1, ms); e < le; ++e) put(e, kLit | byte_at(s.lit + (e - so)));
+    // match bytes.  Byte e repeats every o bytes back to ms - o.  With
+    // wrap = max(ms, step0), the source cycles through [wrap - o, wrap): below
+    // the step when the copy began before it, else the run's first copy.
+    if (e < b1 && e < me) {
+      const uint32_t wrap = max(ms, step0);
+      const uint32_t d = e - wrap;
+      uint32_t v = wrap - o + (d < o ? d : d % o);
+      for (const uint32_t mend = min(b1, me); e < mend; ++e) {
+        put(e, v >= step0 ? (v | kInner) : v);
+        if (++v == wrap) v -= o;
+      }
+    }
+    if (e < b1) {
+      if (s.last) return ZMOE_CHUNK_SHORT_OUTPUT;
+      ip = s.next;
+      so = me;
+    }
+  }
+  if (e & 3) {                                         // partial group at the chunk end
+    const uint32_t i0 = (e & ~3u) & (kRegion - 1);
+    c.map[i0] = r0;
+    if ((e & 3) > 1) c.map[i0 + 1] = r1;
+    if ((e & 3) > 2) c.map[i0 + 2] = r2;
+  }
+  return 0;
+}
+
+// ---------------------------------------------------------------------------
+// phase 3: resolve the region's steps through the shared-memory window
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void fetch_step(Smem& S, const Chunk& c, uint32_t s0, uint32_t buf) {
+  const uint32_t* src = c.map + (s0 & (kRegion - 1));
+  uint32_t* dst = S.u.mbuf[buf];
+  for (uint32_t q = threadIdx.x; q < kStep / 4; q += kThreads) cp_async16(dst + 4 * q, src + 4 * q);
+  cp_async_commit();
+}
+
+__device__ int resolve_region(Smem& S, const Chunk& c, uint32_t R0, uint32_t R1) {
+  const uint32_t n_steps = (R1 - R0 + kStep - 1) / kStep;
+  int err = 0;
+  fetch_step(S, c, R0, 0);
+  for (uint32_t t = 0; t < n_steps; ++t) {
+    const uint32_t s0 = R0 + t * kStep;
+    if (t + 1 < n_steps) {
+      fetch_step(S, c, s0 + kStep, (t + 1) & 1);      // its buffer was last read before the previous barrier B
       cp_async_wait1();
     } else {
       cp_async_wait0();
     }
-    __syncwarp();
-    if (!spin_until(S, [&] { return vload(&S.flush_pos) + kRing >= s1; })) return;
-    // gather the whole step, then write it (a write may reuse the window slot
-    // of a source read in this step)
-    const uint32_t* mb = S.mbuf[t & 1];
-    uint32_t val[kStep / 128];
+    __syncthreads();                                   // A: step entries landed; earlier writes visible
+    const uint32_t* mb = S.u.mbuf[t & 1];
+    const uint32_t j0 = kPerThread * threadIdx.x;
+    const uint4 m0 = *reinterpret_cast<const uint4*>(mb + j0);
+    const uint4 m1 = *reinterpret_cast<const uint4*>(mb + j0 + 4);
+    const uint32_t m[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
+    const uint32_t e = s0 + j0;
+    uint32_t lo = 0, hi = 0;
 #pragma unroll
-    for (uint32_t i = 0; i < kStep / 128; ++i) {
-      const uint32_t r = 128 * i + 4 * lane;
-      const uint4 m = *reinterpret_cast<const uint4*>(mb + r);
-      const uint32_t mv[4] = {m.x, m.y, m.z, m.w};
-      uint32_t packed = 0;
-#pragma unroll
-      for (uint32_t b = 0; b < 4; ++b) {
-        const uint32_t d = mv[b];
-        uint32_t x = d & 0xFFu;
-        if (!(d & kLit) && s0 + r + b < s1) x = S.ring[c.ri(d)];
-        packed |= x << (8 * b);
+    for (uint32_t b = 0; b < 8; ++b) {
+      uint32_t x = m[b];
+      if (e + b >= R1) x = kLit;                       // past the chunk end: entry never written
+      if (x & kInner) {                                // follow the step's own entries back
+        uint32_t hops = 0;
+        do {
+          const uint32_t j = (x & kPosMask) - s0;
+          if (j >= kStep || ++hops > kStep) { err = ZMOE_CHUNK_BAD_DESC; x = kLit; break; }
+          x = mb[j];
+        } while (x & kInner);
       }
-      val[i] = packed;
+      const uint32_t val = (x & kLit) ? (x & 0xFFu) : (uint32_t)S.ring[c.ri(x)];
+      if (b < 4) lo |= val << (8 * b); else hi |= val << (8 * (b - 4));
     }
-    __syncwarp();
+    __syncthreads();                                   // B: the whole step is gathered
 #pragma unroll
-    for (uint32_t i = 0; i < kStep / 128; ++i) {
-      const uint32_t e = s0 + 128 * i + 4 * lane;
-#pragma unroll
-      for (uint32_t b = 0; b < 4; ++b)
-        if (e + b < s1) S.ring[c.ri(e + b)] = (uint8_t)(val[i] >> (8 * b));
-    }
-    __threadfence_block();
-    __syncwarp();
-    if (lane == 0) {
-      vstore(&S.res_pos, s1);
-      if (s1 == c.out_size || (s1 % kWindow) == 0) vstore(&S.res_win, (s1 + kWindow - 1) / kWindow);
-    }
+    for (uint32_t b = 0; b < 8; ++b)
+      if (e + b < R1) S.ring[c.ri(e + b)] = (uint8_t)((b < 4 ? lo : hi) >> (8 * (b & 3)));
   }
-}
-
-// Every exit waits for the resolver's own asynchronous copies into shared memory.
-__device__ void resolver(Smem& S, const Chunk& c, uint32_t lane) {
-  resolver_body(S, c, lane);
-  cp_async_wait0();
-  __syncwarp();
+  return err;
 }
 
 // ---------------------------------------------------------------------------
-// flusher warp
+// phase 4: BF16 out
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t pack2(uint32_t e4, uint32_t s4, uint32_t sel) {
   const uint32_t e2 = __byte_perm(e4, 0, sel);
@@ -364,68 +301,79 @@ __device__ __forceinline__ uint32_t pack2(uint32_t e4, uint32_t s4, uint32_t sel
   return ((s2 & 0x00800080u) << 8) | (e2 << 7) | (s2 & 0x007F007Fu);
 }
 
-__device__ void flusher(Smem& S, const Chunk& c, uint32_t lane) {
-  const uint32_t N = c.out_size;
-  // vector path when the sign+mantissa plane and the output reach 16-byte
-  // boundaries at the same element
+// Writes positions [f0, f1).  vec: 16-element groups starting at head + 16u are
+// 16-byte aligned in the sign+mantissa plane, the output and the ring.
+__device__ void flush_range(Smem& S, const Chunk& c, uint32_t f0, uint32_t f1, uint32_t head, bool vec) {
+  if (!vec) {
+    for (uint32_t i = f0 + threadIdx.x; i < f1; i += kThreads)
+      c.dst[i] = (uint16_t)recombine(__ldg(c.sm + i), S.ring[c.ri(i)]);
+    return;
+  }
+  // first aligned group start >= f0, last aligned end <= f1
+  const uint32_t v0 = f0 <= head ? head : head + ((f0 - head + 15) & ~15u);
+  const uint32_t v1 = f1 <= head ? head : head + ((f1 - head) & ~15u);
+  if (v0 >= v1) {
+    for (uint32_t i = f0 + threadIdx.x; i < f1; i += kThreads)
+      c.dst[i] = (uint16_t)recombine(__ldg(c.sm + i), S.ring[c.ri(i)]);
+    return;
+  }
+  for (uint32_t i = f0 + threadIdx.x; i < v0; i += kThreads)
+    c.dst[i] = (uint16_t)recombine(__ldg(c.sm + i), S.ring[c.ri(i)]);
+  for (uint32_t i = v1 + threadIdx.x; i < f1; i += kThreads)
+    c.dst[i] = (uint16_t)recombine(__ldg(c.sm + i), S.ring[c.ri(i)]);
+  const uint32_t units = (v1 - v0) / 16;
+  constexpr int kUnroll = 4;                           // sign+mantissa loads in flight per thread
+  for (uint32_t u0 = 0; u0 < units; u0 += kThreads * kUnroll) {
+    uint4 sv[kUnroll];
+#pragma unroll
+    for (int q = 0; q < kUnroll; ++q) {
+      const uint32_t u = u0 + threadIdx.x + kThreads * q;
+      if (u < units) sv[q] = __ldg(reinterpret_cast<const uint4*>(c.sm + v0 + 16 * u));
+    }
+#pragma unroll
+    for (int q = 0; q < kUnroll; ++q) {
+      const uint32_t u = u0 + threadIdx.x + kThreads * q;
+      if (u >= units) break;
+      const uint32_t i = v0 + 16 * u;
+      const uint4 ev = *reinterpret_cast<const uint4*>(&S.ring[c.ri(i)]);
+      uint4 lo, hi;
+      lo.x = pack2(ev.x, sv[q].x, 0x4140); lo.y = pack2(ev.x, sv[q].x, 0x4342);
+      lo.z = pack2(ev.y, sv[q].y, 0x4140); lo.w = pack2(ev.y, sv[q].y, 0x4342);
+      hi.x = pack2(ev.z, sv[q].z, 0x4140); hi.y = pack2(ev.z, sv[q].z, 0x4342);
+      hi.z = pack2(ev.w, sv[q].w, 0x4140); hi.w = pack2(ev.w, sv[q].w, 0x4342);
+      uint4* o = reinterpret_cast<uint4*>(c.dst + i);
+      o[0] = lo;
+      o[1] = hi;
+    }
+  }
+}
+
+__device__ void decode_indexed(Smem& S, const Chunk& c) {
   const uintptr_t sa = reinterpret_cast<uintptr_t>(c.sm), da = reinterpret_cast<uintptr_t>(c.dst);
   const uint32_t head = (uint32_t)((16 - (sa & 15)) & 15);
   const bool vec = ((da + 2 * (uintptr_t)head) & 15) == 0;
-  uint32_t e = 0;
-  while (e < N) {
-    uint32_t avail = 0;
-    if (!spin_until(S, [&] { avail = vload(&S.res_pos); return avail > e; })) return;
+  const bool src_aligned = (reinterpret_cast<uintptr_t>(c.src) & 15) == 0;
+  const uint32_t n_reg = (c.out_size + kRegion - 1) / kRegion;
+  StageRange st = src_aligned ? stage_range(c, 0) : StageRange{0, 0};
+  stage_issue(S, c, st);
+  for (uint32_t r = 0; r < n_reg; ++r) {
+    const uint32_t R0 = r * kRegion, R1 = min(R0 + kRegion, c.out_size);
+    cp_async_wait0();
+    __syncthreads();                                   // staged bytes visible; previous flush done
+    int err = map_slice(S, c, st, r * kThreads + threadIdx.x);
+    if (err) set_err(S, err);
     __threadfence_block();
-    uint32_t stop = avail;
-    if (vec) {
-      // scalar up to the first aligned element, then 16 elements per lane
-      const uint32_t h = min(max(head, e), avail);
-      for (uint32_t i = e + lane; i < h; i += 32)
-        c.dst[i] = (uint16_t)recombine(__ldg(c.sm + i), S.ring[c.ri(i)]);
-      const uint32_t v0 = h;
-      const uint32_t units = (avail - v0) / 16;
-      constexpr int kUnroll = 8;                // sign+mantissa loads in flight per lane
-      for (uint32_t u0 = 0; u0 < units; u0 += 32 * kUnroll) {
-        uint4 sv[kUnroll];
-#pragma unroll
-        for (int q = 0; q < kUnroll; ++q) {
-          const uint32_t u = u0 + lane + 32 * q;
-          if (u < units) sv[q] = __ldg(reinterpret_cast<const uint4*>(c.sm + v0 + 16 * u));
-        }
-#pragma unroll
-        for (int q = 0; q < kUnroll; ++q) {
-          const uint32_t u = u0 + lane + 32 * q;
-          if (u >= units) break;
-          const uint32_t i = v0 + 16 * u;
-          const uint4 ev = *reinterpret_cast<const uint4*>(&S.ring[c.ri(i)]);
-          uint4 lo, hi;
-          lo.x = pack2(ev.x, sv[q].x, 0x4140); lo.y = pack2(ev.x, sv[q].x, 0x4342);
-          lo.z = pack2(ev.y, sv[q].y, 0x4140); lo.w = pack2(ev.y, sv[q].y, 0x4342);
-          hi.x = pack2(ev.z, sv[q].z, 0x4140); hi.y = pack2(ev.z, sv[q].z, 0x4342);
-          hi.z = pack2(ev.w, sv[q].w, 0x4140); hi.w = pack2(ev.w, sv[q].w, 0x4342);
-          uint4* o = reinterpret_cast<uint4*>(c.dst + i);
-          o[0] = lo;
-          o[1] = hi;
-        }
-      }
-      stop = v0 + 16 * units;
-      if (avail == N) {                         // block done: flush the tail too
-        for (uint32_t i = stop + lane; i < N; i += 32)
-          c.dst[i] = (uint16_t)recombine(__ldg(c.sm + i), S.ring[c.ri(i)]);
-        stop = N;
-      }
-      if (stop <= e) {                          // nothing aligned yet: wait for more
-        if (!spin_until(S, [&] { return vload(&S.res_pos) >= min(N, e + 16 + head); })) return;
-        continue;
-      }
-    } else {
-      for (uint32_t i = e + lane; i < avail; i += 32)
-        c.dst[i] = (uint16_t)recombine(__ldg(c.sm + i), S.ring[c.ri(i)]);
+    if (__syncthreads_or(err != 0)) return;           // map written; staging area free
+    err = resolve_region(S, c, R0, R1);
+    if (err) set_err(S, err);
+    if (__syncthreads_or(err != 0)) return;           // region resolved; map buffers free
+    if (r + 1 < n_reg) {
+      st = src_aligned ? stage_range(c, r + 1) : StageRange{0, 0};
+      stage_issue(S, c, st);                           // overlaps the flush
     }
-    __syncwarp();
-    e = stop;
-    if (lane == 0) vstore(&S.flush_pos, e);
+    flush_range(S, c, R0, R1, head, vec);
   }
+  cp_async_wait0();
 }
 
 // ---------------------------------------------------------------------------
@@ -438,9 +386,10 @@ __device__ void flusher(Smem& S, const Chunk& c, uint32_t lane) {
 __device__ int decode_unindexed(const Chunk& c, uint32_t lane) {
   uint32_t ip = 0, op = 0;
   int err = 0;
+  auto byte_at = [&](uint32_t q) -> uint32_t { return __ldg(c.src + q); };
   while (op < c.out_size) {
     Seq s;
-    if (lane == 0) err = read_seq(c.src, c.src_size, ip, s);
+    if (lane == 0) err = read_seq(byte_at, c.src_size, ip, s);
     err = __shfl_sync(kFull, err, 0);
     if (err) return err;
     s.ll = __shfl_sync(kFull, s.ll, 0);
@@ -480,12 +429,10 @@ __device__ int decode_unindexed(const Chunk& c, uint32_t lane) {
   return 0;
 }
 
-__global__ void __launch_bounds__(kWarps * 32)
+__global__ void __launch_bounds__(kThreads, 2)
 decode_kernel(const zmoe_chunk* __restrict__ chunks, int n_chunks, int32_t* __restrict__ status) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   Smem& S = *reinterpret_cast<Smem*>(smem_raw);
-  const int warp = threadIdx.x >> 5;
-  const uint32_t lane = threadIdx.x & 31;
   const zmoe_chunk d = chunks[blockIdx.x];
   Chunk c;
   c.src = d.src;
@@ -500,29 +447,20 @@ decode_kernel(const zmoe_chunk* __restrict__ chunks, int n_chunks, int32_t* __re
     const uint32_t head = (uint32_t)((16 - (reinterpret_cast<uintptr_t>(d.sm) & 15)) & 15);
     c.rofs = (16 - head) & 15;
   }
-  if (threadIdx.x == 0) {
-    bool bad = !c.src || !c.sm || !c.dst || c.src_size == 0;
-    if (c.index && (!c.map || (reinterpret_cast<uintptr_t>(c.map) & 15) || d.seg_bytes != kSlice)) bad = true;
-    S.err = bad ? ZMOE_CHUNK_BAD_DESC : 0;
-    S.res_pos = 0;
-    S.res_win = 0;
-    S.flush_pos = 0;
-    for (uint32_t w = 0; w < kMapWindows; ++w) S.win_ready[w] = 0;
-    for (int p = 0; p < kParsers; ++p) S.n_chase[p] = 0;
-  }
+  bool bad = !c.src || !c.sm || !c.dst || c.src_size == 0 || c.out_size >= kInner;
+  if (c.index && (!c.map || (reinterpret_cast<uintptr_t>(c.map) & 15) ||
+                  (reinterpret_cast<uintptr_t>(c.index) & 7) || d.seg_bytes != kSlice))
+    bad = true;
+  if (threadIdx.x == 0) S.err = bad ? ZMOE_CHUNK_BAD_DESC : 0;
   __syncthreads();
-  if (!S.err && c.out_size > 0) {
+  if (!bad && c.out_size > 0) {
     if (!c.index) {
-      if (warp == 0) {
-        const int e = decode_unindexed(c, lane);
-        if (e && lane == 0) set_err(S, e);
+      if ((threadIdx.x >> 5) == 0) {
+        const int e = decode_unindexed(c, threadIdx.x & 31);
+        if (e && threadIdx.x == 0) set_err(S, e);
       }
-    } else if (warp < kParsers) {
-      parser(S, c, warp, lane);
-    } else if (warp == kResolver) {
-      resolver(S, c, lane);
     } else {
-      flusher(S, c, lane);
+      decode_indexed(S, c);
     }
   }
   __syncthreads();
@@ -535,7 +473,7 @@ zmoe_status launch_decode_chunks(const zmoe_chunk* chunks, int n_chunks, int32_t
   if (n_chunks <= 0) return ZMOE_OK;
   const int smem = (int)sizeof(Smem);
   ZMOE_CUDA_RET(cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-  decode_kernel<<<n_chunks, kWarps * 32, smem, stream>>>(chunks, n_chunks, status);
+  decode_kernel<<<n_chunks, kThreads, smem, stream>>>(chunks, n_chunks, status);
   return launch_status("decode_kernel");
 }
 

@@ -24,7 +24,7 @@ class ZmoeChunk(ctypes.Structure):
 
 
 SLICE_BYTES = 256        # ZMOE_SLICE_BYTES
-MAP_ENTRIES = 32768      # ZMOE_MAP_ENTRIES
+MAP_ENTRIES = 65536      # ZMOE_MAP_ENTRIES
 
 
 class RouterArgs(ctypes.Structure):
