@@ -24,7 +24,7 @@
 //     o bytes), so it is always resolved already; otherwise it is the first
 //     copy of the run, inside the step, and is marked for a chase.
 //  3. Resolve: step by step (2 KiB, 8 bytes per thread), the entries are
-//     copied into shared memory (cp.async, one step ahead) and every byte is
+//     copied into shared memory (cp.async, three steps ahead) and every byte is
 //     gathered from a 64 KiB shared-memory window of decoded exponents; marked
 //     entries first follow the step's own entries back to a literal or to a
 //     byte before the step.  The whole step is gathered before it is written.
@@ -53,6 +53,8 @@ constexpr uint32_t kPerThread = kStep / kThreads;   // bytes resolved per thread
 constexpr uint32_t kRing = 65536;                   // decoded-exponent window
 constexpr uint32_t kRingMask = kRing - 1;
 constexpr uint32_t kStage = 48 * 1024;              // staged compressed bytes per region
+constexpr uint32_t kMapBufs = 4;                    // map-entry buffers of the resolve
+constexpr uint32_t kAhead = kMapBufs - 1;           // steps whose entries are in flight
 constexpr uint32_t kLit = 0x80000000u;              // map entry: literal value in bits 0..7
 constexpr uint32_t kInner = 0x40000000u;            // map entry: source inside its own step
 constexpr uint32_t kPosMask = kInner - 1;
@@ -63,13 +65,13 @@ static_assert(kRegion == ZMOE_MAP_ENTRIES, "one map entry per byte of a region")
 static_assert(kRegion <= kRing, "a region's sources stay inside the window");
 static_assert(kStep % kSlice == 0 && kRegion % kStep == 0, "slices nest in steps nest in regions");
 static_assert(kPerThread == 8, "two 128-bit map loads per thread and step");
-static_assert(2 * kStep * 4 <= kStage, "map double buffer fits the staging area");
+static_assert(kMapBufs * kStep * 4 <= kStage, "map buffers fit the staging area");
 
 struct Smem {
   uint8_t ring[kRing];
   union {
     uint8_t stage[kStage];                          // phase 2: compressed bytes of the region
-    uint32_t mbuf[2][kStep];                        // phase 3: map entries of this/next step
+    uint32_t mbuf[kMapBufs][kStep];                 // phase 3: map entries of the next steps
   } u;
   int32_t err;
 };
@@ -93,8 +95,8 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
                : "memory");
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 // One LZ4 sequence header at ip: literal count and position, match offset and
 // length, position of the next token.  Returns 0 or a ZMOE_CHUNK_* error.
@@ -194,13 +196,12 @@ __device__ int map_slice(Smem& S, const Chunk& c, const StageRange& st, uint32_t
   uint4* map4 = reinterpret_cast<uint4*>(c.map);
   uint32_t e = b0;
   uint32_t r0 = 0, r1 = 0, r2 = 0;                     // entries waiting for a 128-bit store
-  auto put = [&](uint32_t pos, uint32_t v) {
-    switch (pos & 3) {
-      case 0: r0 = v; break;
-      case 1: r1 = v; break;
-      case 2: r2 = v; break;
-      default: map4[(pos & (kRegion - 1)) >> 2] = make_uint4(r0, r1, r2, v);
-    }
+  auto put = [&](uint32_t pos, uint32_t v) {           // selects, not a branch: lanes sit at any pos & 3
+    const uint32_t k = pos & 3;
+    r0 = k == 0 ? v : r0;
+    r1 = k == 1 ? v : r1;
+    r2 = k == 2 ? v : r2;
+    if (k == 3) map4[(pos & (kRegion - 1)) >> 2] = make_uint4(r0, r1, r2, v);
   };
   while (e < b1) {
     Seq s;
@@ -210,19 +211,26 @@ __device__ int map_slice(Smem& S, const Chunk& c, const StageRange& st, uint32_t
     const uint32_t me = ms + s.ml;
     const uint32_t o = s.off;
     if (s.ml > 0 && (o == 0 || o > ms)) return ZMOE_CHUNK_BAD_OFFSET;
-    // literals
-    for (const uint32_t le = min(b1, ms); e < le; ++e) put(e, kLit | byte_at(s.lit + (e - so)));
-    // match bytes.  Byte e repeats every o bytes back to ms - o.  With
-    // wrap = max(ms, step0), the source cycles through [wrap - o, wrap): below
-    // the step when the copy began before it, else the run's first copy.
-    if (e < b1 && e < me) {
-      const uint32_t wrap = max(ms, step0);
+    // Literal bytes, then match bytes, in one loop.  Match byte e repeats
+    // every o bytes back to ms - o.  With wrap = max(ms, step0), its source
+    // cycles through [wrap - o, wrap): below the step when the copy began
+    // before it, else the run's first copy (inside the step: chased later).
+    const uint32_t wrap = max(ms, step0);
+    uint32_t v = wrap - o;                             // e < ms: the match begins at ms >= e >= step0
+    if (e >= ms && s.ml > 0) {                         // the slice starts inside this match
       const uint32_t d = e - wrap;
-      uint32_t v = wrap - o + (d < o ? d : d % o);
-      for (const uint32_t mend = min(b1, me); e < mend; ++e) {
-        put(e, v >= step0 ? (v | kInner) : v);
+      v += d < o ? d : d % o;
+    }
+    const uint32_t lit_base = s.lit - so;
+    for (const uint32_t end = min(b1, me); e < end; ++e) {
+      uint32_t x;
+      if (e < ms) {
+        x = kLit | byte_at(lit_base + e);
+      } else {
+        x = v >= step0 ? (v | kInner) : v;
         if (++v == wrap) v -= o;
       }
+      put(e, x);
     }
     if (e < b1) {
       if (s.last) return ZMOE_CHUNK_SHORT_OUTPUT;
@@ -246,42 +254,58 @@ __device__ __forceinline__ void fetch_step(Smem& S, const Chunk& c, uint32_t s0,
   const uint32_t* src = c.map + (s0 & (kRegion - 1));
   uint32_t* dst = S.u.mbuf[buf];
   for (uint32_t q = threadIdx.x; q < kStep / 4; q += kThreads) cp_async16(dst + 4 * q, src + 4 * q);
-  cp_async_commit();
 }
 
 __device__ int resolve_region(Smem& S, const Chunk& c, uint32_t R0, uint32_t R1) {
   const uint32_t n_steps = (R1 - R0 + kStep - 1) / kStep;
   int err = 0;
-  fetch_step(S, c, R0, 0);
+  // map entries run kAhead steps ahead of the resolve (one commit group per
+  // step, empty past the end, so wait_group counts stay uniform)
+  for (uint32_t p = 0; p < kAhead; ++p) {
+    if (p < n_steps) fetch_step(S, c, R0 + p * kStep, p % kMapBufs);
+    cp_async_commit();
+  }
   for (uint32_t t = 0; t < n_steps; ++t) {
     const uint32_t s0 = R0 + t * kStep;
-    if (t + 1 < n_steps) {
-      fetch_step(S, c, s0 + kStep, (t + 1) & 1);      // its buffer was last read before the previous barrier B
-      cp_async_wait1();
-    } else {
-      cp_async_wait0();
-    }
+    // buffer (t + kAhead) % kMapBufs last held step t - 1, read before its barrier B
+    if (t + kAhead < n_steps) fetch_step(S, c, s0 + kAhead * kStep, (t + kAhead) % kMapBufs);
+    cp_async_commit();
+    cp_async_wait<kAhead>();
     __syncthreads();                                   // A: step entries landed; earlier writes visible
-    const uint32_t* mb = S.u.mbuf[t & 1];
+    const uint32_t* mb = S.u.mbuf[t % kMapBufs];
     const uint32_t j0 = kPerThread * threadIdx.x;
     const uint4 m0 = *reinterpret_cast<const uint4*>(mb + j0);
     const uint4 m1 = *reinterpret_cast<const uint4*>(mb + j0 + 4);
-    const uint32_t m[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
+    uint32_t x[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
     const uint32_t e = s0 + j0;
+    uint32_t pending = 0;                              // entries whose source lies inside the step
+#pragma unroll
+    for (uint32_t b = 0; b < 8; ++b) {
+      if (e + b >= R1) x[b] = kLit;                    // past the chunk end: entry never written
+      pending |= (x[b] & kInner) ? (1u << b) : 0u;
+    }
+    // follow the step's own entries back, one hop for every pending entry per
+    // round (sources strictly precede their byte, so at most kStep rounds)
+    for (uint32_t round = 0; pending; ++round) {
+      if (round >= kStep) {
+        err = ZMOE_CHUNK_BAD_DESC;
+        break;
+      }
+#pragma unroll
+      for (uint32_t b = 0; b < 8; ++b) {
+        if (pending & (1u << b)) {
+          const uint32_t j = (x[b] & kPosMask) - s0;
+          x[b] = j < kStep ? mb[j] : kLit;
+          if (j >= kStep) err = ZMOE_CHUNK_BAD_DESC;
+          if (!(x[b] & kInner)) pending &= ~(1u << b);
+        }
+      }
+    }
     uint32_t lo = 0, hi = 0;
 #pragma unroll
     for (uint32_t b = 0; b < 8; ++b) {
-      uint32_t x = m[b];
-      if (e + b >= R1) x = kLit;                       // past the chunk end: entry never written
-      if (x & kInner) {                                // follow the step's own entries back
-        uint32_t hops = 0;
-        do {
-          const uint32_t j = (x & kPosMask) - s0;
-          if (j >= kStep || ++hops > kStep) { err = ZMOE_CHUNK_BAD_DESC; x = kLit; break; }
-          x = mb[j];
-        } while (x & kInner);
-      }
-      const uint32_t val = (x & kLit) ? (x & 0xFFu) : (uint32_t)S.ring[c.ri(x)];
+      const uint32_t xb = (x[b] & kInner) ? kLit : x[b];
+      const uint32_t val = (xb & kLit) ? (xb & 0xFFu) : (uint32_t)S.ring[c.ri(xb)];
       if (b < 4) lo |= val << (8 * b); else hi |= val << (8 * (b - 4));
     }
     __syncthreads();                                   // B: the whole step is gathered
@@ -289,6 +313,7 @@ __device__ int resolve_region(Smem& S, const Chunk& c, uint32_t R0, uint32_t R1)
     for (uint32_t b = 0; b < 8; ++b)
       if (e + b < R1) S.ring[c.ri(e + b)] = (uint8_t)((b < 4 ? lo : hi) >> (8 * (b & 3)));
   }
+  cp_async_wait<0>();
   return err;
 }
 
@@ -358,7 +383,7 @@ __device__ void decode_indexed(Smem& S, const Chunk& c) {
   stage_issue(S, c, st);
   for (uint32_t r = 0; r < n_reg; ++r) {
     const uint32_t R0 = r * kRegion, R1 = min(R0 + kRegion, c.out_size);
-    cp_async_wait0();
+    cp_async_wait<0>();
     __syncthreads();                                   // staged bytes visible; previous flush done
     int err = map_slice(S, c, st, r * kThreads + threadIdx.x);
     if (err) set_err(S, err);
@@ -373,7 +398,7 @@ __device__ void decode_indexed(Smem& S, const Chunk& c) {
     }
     flush_range(S, c, R0, R1, head, vec);
   }
-  cp_async_wait0();
+  cp_async_wait<0>();
 }
 
 // ---------------------------------------------------------------------------
