@@ -268,7 +268,7 @@ def run_ours(args):
                        "l2": "inputs larger than L2 (decoded + compressed experts > 1 GB)"},
             "e2e": {"value": world * args.tokens / (e2e_ms / 1e3), "unit": UNIT,
                     "h2d_bytes_per_step": x.numel() * 2, "d2h_bytes_per_step": x.numel() * 2},
-            "roofline": {"bound": "hbm", "kernel": "decode_warp_kernel", "achieved": achieved, "peak": hbm,
+            "roofline": {"bound": "hbm", "kernel": "decode_kernel", "achieved": achieved, "peak": hbm,
                          "unit": "GB/s", "frac": achieved / hbm, "peak_source": src, "traffic": traffic,
                          "algorithmic_bytes_per_launch": st["decode_timed_bytes"] / launches,
                          "kernel_ms_per_launch": dec_s * 1e3 / launches},

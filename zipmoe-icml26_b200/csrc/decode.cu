@@ -353,7 +353,7 @@ __device__ void flush_range(Smem& S, const Chunk& c, uint32_t f0, uint32_t f1, u
 #pragma unroll
     for (int q = 0; q < kUnroll; ++q) {
       const uint32_t u = u0 + threadIdx.x + kThreads * q;
-      if (u < units) sv[q] = __ldg(reinterpret_cast<const uint4*>(c.sm + v0 + 16 * u));
+      if (u < units) sv[q] = __ldcs(reinterpret_cast<const uint4*>(c.sm + v0 + 16 * u));
     }
 #pragma unroll
     for (int q = 0; q < kUnroll; ++q) {
@@ -367,8 +367,8 @@ __device__ void flush_range(Smem& S, const Chunk& c, uint32_t f0, uint32_t f1, u
       hi.x = pack2(ev.z, sv[q].z, 0x4140); hi.y = pack2(ev.z, sv[q].z, 0x4342);
       hi.z = pack2(ev.w, sv[q].w, 0x4140); hi.w = pack2(ev.w, sv[q].w, 0x4342);
       uint4* o = reinterpret_cast<uint4*>(c.dst + i);
-      o[0] = lo;
-      o[1] = hi;
+      __stcs(o, lo);                                   // streaming: keep L2 for the map scratch
+      __stcs(o + 1, hi);
     }
   }
 }
