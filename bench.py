@@ -13,8 +13,11 @@ is decoded on the GPU inside the step.  Seeded synthetic data (no checkpoint):
 weights N(0, 0.02) BF16, activations N(0, 1) BF16.
 
 Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-Under torchrun (N > 1) every rank runs its own replica of the layer on its
-own 512 tokens (weak scaling; the layer has no exchange step in this mode).
+Under torchrun (N > 1) the layer is expert-parallel: rank r owns experts
+[r*60//N, (r+1)*60//N) (compressed in its HBM, decoded on its GPU), every rank
+routes its own 512 tokens (weak scaling) and token rows go to their expert's
+rank and back by NCCL all-to-all.  The decoded-expert cache stays 16 experts
+for the whole box, split over the ranks in proportion to the experts they own.
 """
 from __future__ import annotations
 
@@ -184,6 +187,8 @@ def run_reference(args):
 
 def run_ours(args):
     world, rank, local = dist_env()
+    if world > 1:
+        return run_ep(args)
     torch.cuda.set_device(local)
     dist = None
     if world > 1:
@@ -286,6 +291,120 @@ def run_ours(args):
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def run_ep(args):
+    """Expert-parallel layer over WORLD_SIZE ranks (one GPU each)."""
+    import datetime
+    import torch.distributed as dist
+    from zmoe import codec as zc
+    from zmoe import ep
+    from zmoe import synthetic as syn
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+    s = syn.QWEN
+    part = ep.ExpertPartition(s.num_experts, world)
+    mine = part.owned(rank)
+    w = syn.expert_weights(s, 1)[0]
+    wr, sg = syn.router_weights(s)
+    sh = syn.shared_weights(s)
+    bias = syn.zipf_bias(s, 0)
+    threads = max(1, (os.cpu_count() or 1) // world)
+    flat = zc.encode_tensors([t for e in mine for t in w[e]], args.chunks, args.codec, args.level, threads)
+    enc = [None] * s.num_experts
+    for j, e in enumerate(mine):
+        enc[e] = flat[j * 3:(j + 1) * 3]
+    cache = max(1, round(args.cache * len(mine) / s.num_experts))
+    warm = syn.popularity_order(s, 0)[: args.cache]
+    L = ep.build_gpu_layer(s, enc, wr, bias, sg, sh, max_tokens=args.tokens, cache_slots=cache, device=local,
+                           warm=warm)
+    eng = L.engine
+    x = syn.activations(args.tokens, s.hidden, seed=1 + rank).cuda()
+    stream = torch.cuda.current_stream()
+
+    def barrier():
+        dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        L(x)
+    eng.sync()
+    eng.reset_stats()
+    eng.set_timing(True)
+    barrier()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        start.record(stream)
+        for _ in range(args.steps):
+            L(x)
+        stop.record(stream)
+        torch.cuda.synchronize()
+    eng.sync()
+    barrier()
+    ms = start.elapsed_time(stop) / args.steps
+    st = eng.stats()
+    eng.set_timing(False)
+
+    # end to end: pinned host tokens in, host output back, every step
+    xh = x.cpu().pin_memory()
+    oh = torch.empty_like(xh).pin_memory()
+    xd = torch.empty_like(x)
+
+    def host_step():
+        xd.copy_(xh, non_blocking=True)
+        oh.copy_(L(xd), non_blocking=True)
+
+    for _ in range(2):
+        host_step()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        host_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    t = torch.tensor([ms, e2e_ms], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, e2e_ms = float(t[0]), float(t[1])
+    clocks = clk.summary()
+    if rank == 0:
+        hbm, tfl, src = peaks()
+        dec_s = st["decode_ns"] * 1e-9
+        launches = max(st["decode_timed_launches"], 1)
+        achieved = (st["decode_timed_bytes"] / launches) / (dec_s / launches) / 1e9 if dec_s > 0 else 0.0
+        # per step: router 1, permute 3, gathers 2, shared FFN 2, combine 1 + the engine's own
+        ep_launches = 9 * args.steps
+        line = {
+            "metric": METRIC, "value": world * args.tokens / (ms / 1e3), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations)",
+            "config": {"workload": "qwen1.5-moe-layer", "tokens_per_gpu": args.tokens, "hidden": s.hidden,
+                       "experts": s.num_experts, "inter": s.inter, "topk": s.topk, "shared_inter": s.shared_inter,
+                       "cached_experts": args.cache, "cached_experts_rank0": cache,
+                       "experts_rank0": len(mine), "codec": f"{args.codec}-{args.level}",
+                       "num_file_chunks": args.chunks, "zipf_s": s.zipf_s, "parallelism": f"ep{world}",
+                       "exchange": "NCCL all-to-all (counts, BF16 rows out, fp32 rows back)",
+                       "l2": "inputs larger than L2 (decoded + compressed experts > 1 GB)"},
+            "e2e": {"value": world * args.tokens / (e2e_ms / 1e3), "unit": UNIT,
+                    "h2d_bytes_per_step": x.numel() * 2, "d2h_bytes_per_step": x.numel() * 2},
+            "roofline": {"bound": "hbm", "kernel": "decode_kernel", "achieved": achieved, "peak": hbm,
+                         "unit": "GB/s", "frac": achieved / hbm, "peak_source": src, "traffic": None,
+                         "algorithmic_bytes_per_launch": st["decode_timed_bytes"] / launches,
+                         "kernel_ms_per_launch": dec_s * 1e3 / launches},
+            "decode": {"experts_per_step_rank0": st["decoded_experts"] / args.steps,
+                       "gb_per_s": achieved, "share_of_step": dec_s / (ms * 1e-3 * args.steps)},
+            "cache": {"hits": st["hits"], "misses": st["misses"], "evictions": st["evictions"]},
+            "gpu_launches": st["launches"] + ep_launches,
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    eng.close()
+    dist.barrier()
+    dist.destroy_process_group()
 
 
 def cpu_baseline(args, s, enc, extra):

@@ -208,6 +208,14 @@ typedef struct zmoe_combine_args {
 
 zmoe_status zmoe_combine(const zmoe_combine_args* a, zmoe_stream_t stream);
 
+/* Row gather dst[r] = src[index[r]], r < rows, for rows of row_bytes bytes (a
+ * multiple of 16; src and dst 16-byte aligned).  Regroups token rows received
+ * from other ranks by expert, and back, under expert parallelism; the
+ * reference gathers an expert's rows with a libtorch boolean index
+ * (csrc/dispatcher/expert_dispatcher.cpp:326-330). */
+zmoe_status zmoe_gather_rows(const void* src, const int32_t* index, int rows, int row_bytes, void* dst,
+                             zmoe_stream_t stream);
+
 /* --------------------------------------------------------------------------
  * Offload-side codec (host).
  * zmoe_split_planes replaces split_and_extract_from_tensor
@@ -280,6 +288,16 @@ zmoe_status zmoe_layer_warm_cache(zmoe_layer* layer, const int* experts, int n, 
 /* x, out: device [T, H] BF16.  Synchronises once on the stream to read the
  * per-expert token counts. */
 zmoe_status zmoe_layer_forward(zmoe_layer* layer, const uint16_t* x, int T, uint16_t* out, zmoe_stream_t stream);
+/* Expert stage alone, for expert parallelism (the caller routes, permutes and
+ * exchanges rows): x_rows device [rows, H] BF16 grouped by this layer's
+ * experts, counts_host[e] rows of expert e (host array, summing to rows <=
+ * max_tokens * topk); applies the cache decision, decodes misses and runs the
+ * grouped FFN into y, device [rows, H] fp32.  Router and shared-expert weights
+ * are not used.  Replaces, for the experts one rank owns,
+ * ExpertDispatcher::EnqueueExpert .. Wait (csrc/dispatcher/expert_dispatcher.cpp:149-217,285-515).
+ * Synchronises once on the stream. */
+zmoe_status zmoe_layer_experts(zmoe_layer* layer, const uint16_t* x_rows, const int32_t* counts_host, int rows,
+                               float* y, zmoe_stream_t stream);
 /* Same with host buffers (pinned for full speed); returns after out_host is written. */
 zmoe_status zmoe_layer_forward_host(zmoe_layer* layer, const uint16_t* x_host, int T, uint16_t* out_host,
                                     zmoe_stream_t stream);

@@ -20,6 +20,7 @@ zmoe_status launch_router(const zmoe_router_args*, cudaStream_t);
 zmoe_status launch_permute(const zmoe_permute_args*, cudaStream_t);
 zmoe_status launch_combine(const zmoe_combine_args*, cudaStream_t);
 zmoe_status launch_expert_ffn(const zmoe_ffn_args*, cudaStream_t);
+zmoe_status launch_gather_rows(const void*, const int32_t*, int, int, void*, cudaStream_t);
 
 }  // namespace zmoe
 
@@ -52,6 +53,11 @@ zmoe_status zmoe_permute(const zmoe_permute_args* a, zmoe_stream_t stream) {
 
 zmoe_status zmoe_expert_ffn(const zmoe_ffn_args* a, zmoe_stream_t stream) {
   return zmoe::launch_expert_ffn(a, reinterpret_cast<cudaStream_t>(stream));
+}
+
+zmoe_status zmoe_gather_rows(const void* src, const int32_t* index, int rows, int row_bytes, void* dst,
+                             zmoe_stream_t stream) {
+  return zmoe::launch_gather_rows(src, index, rows, row_bytes, dst, reinterpret_cast<cudaStream_t>(stream));
 }
 
 zmoe_status zmoe_combine(const zmoe_combine_args* a, zmoe_stream_t stream) {

@@ -98,6 +98,8 @@ struct Layer {
   int32_t* status_dev = nullptr;
   const uint16_t** wtab_dev = nullptr;
   int32_t* counts_host = nullptr;
+  int32_t* offsets_host = nullptr;     // zmoe_layer_experts: group offsets staged for upload
+  int32_t* offsets_ext = nullptr;      // ... and on the device
   zmoe_chunk* desc_host = nullptr;
   const uint16_t** wtab_host = nullptr;
   int32_t* status_host = nullptr;
@@ -126,6 +128,9 @@ struct Layer {
   ~Layer();
   zmoe_status init(const zmoe_layer_config& c);
   zmoe_status forward(const uint16_t* x, int T, uint16_t* out, cudaStream_t s);
+  zmoe_status run_experts(const uint16_t* xrows, const int32_t* offsets_dev, const int32_t* counts_h, int rows,
+                          float* yrows, cudaStream_t s);
+  zmoe_status experts(const uint16_t* xrows, const int32_t* counts_h, int rows, float* yrows, cudaStream_t s);
   zmoe_status check_status();
   int choose_victim(const std::vector<char>& active);
   zmoe_status decode_into(const std::vector<std::pair<int, int>>& jobs, cudaStream_t s, int wave);
@@ -141,6 +146,7 @@ Layer::~Layer() {
   cudaFree(idx); cudaFree(counts); cudaFree(offsets); cudaFree(row_of); cudaFree(tor);
   cudaFree(tw); cudaFree(sg); cudaFree(y); cudaFree(ysh); cudaFree(xp); cudaFree(h); cudaFree(hsh);
   cudaFree(desc_dev); cudaFree(status_dev); cudaFree(wtab_dev);
+  cudaFree(offsets_ext); cudaFreeHost(offsets_host);
   cudaFreeHost(counts_host); cudaFreeHost(desc_host); cudaFreeHost(wtab_host); cudaFreeHost(status_host);
   cudaFree(x_stage); cudaFree(out_stage); cudaFree(map_scratch);
   if (status_ready) cudaEventDestroy(status_ready);
@@ -226,6 +232,8 @@ zmoe_status Layer::init(const zmoe_layer_config& c) {
   status_dev = dmalloc<int32_t>(max_desc, &st);
   wtab_dev = dmalloc<const uint16_t*>((size_t)max_waves * E * 3, &st);
   counts_host = hmalloc<int32_t>(E, &st);
+  offsets_host = hmalloc<int32_t>(E + 1, &st);
+  offsets_ext = dmalloc<int32_t>(E + 1, &st);
   desc_host = hmalloc<zmoe_chunk>(max_desc, &st);
   wtab_host = hmalloc<const uint16_t*>((size_t)max_waves * E * 3, &st);
   status_host = hmalloc<int32_t>(max_desc, &st);
@@ -344,6 +352,140 @@ zmoe_status Layer::decode_into(const std::vector<std::pair<int, int>>& jobs, cud
   return ZMOE_OK;
 }
 
+// Cache decisions (ProactiveDecision), miss decode waves and the grouped FFN
+// over rows already grouped by expert: group e is rows [offsets[e], offsets[e+1]).
+zmoe_status Layer::run_experts(const uint16_t* xrows, const int32_t* offsets_dev, const int32_t* counts_h, int rows,
+                               float* yrows, cudaStream_t s) {
+  const int E = cfg.num_experts, H = cfg.hidden;
+  zmoe_status st;
+  // 3. cache decisions (ProactiveDecision)
+  std::vector<char> active(E, 0);
+  std::vector<int> act;
+  for (int e = 0; e < E; ++e)
+    if (counts_h[e] > 0) { active[e] = 1; act.push_back(e); global_count[e] += counts_h[e]; }
+  ++clock;
+  std::vector<int> ranked(act);
+  std::vector<std::pair<int, int>> hits_slots;       // (expert, slot) ready to use
+  std::vector<int> misses;
+  for (int e : act) {
+    const int sl = expert_slot[e];
+    if (sl >= 0) {
+      stats.hits++;
+      slot_count[sl] += counts_h[e];
+      slot_stamp[sl] = clock;
+      hits_slots.push_back({e, sl});
+    } else {
+      stats.misses++;
+      misses.push_back(e);
+    }
+  }
+  // rank of each miss by global count (count_up of cache.cpp:230-238)
+  std::vector<std::pair<int, int>> to_cache, to_transient;
+  const double thr_normal = n_cache + cfg.state_margin * E;
+  for (int e : misses) {
+    int up = 0;
+    for (int q = 0; q < E; ++q) up += global_count[q] > global_count[e];
+    int slot = -1;
+    if (n_cache > 0 && up < thr_normal) {
+      slot = choose_victim(active);
+      if (slot >= 0) {
+        if (slot_owner[slot] >= 0) { expert_slot[slot_owner[slot]] = -1; stats.evictions++; }
+        slot_owner[slot] = e;
+        expert_slot[e] = slot;
+        slot_count[slot] = counts_h[e];
+        slot_stamp[slot] = clock;
+        slot_admit[slot] = clock;
+        to_cache.push_back({e, slot});
+        continue;
+      }
+    }
+    to_transient.push_back({e, -1});
+  }
+
+  // 4. waves: decode misses, run the grouped FFN over experts whose weights are ready
+  size_t tpos = 0;
+  int wave = 0;
+  std::vector<std::pair<int, int>> ready(hits_slots);
+  std::vector<std::pair<int, int>> jobs(to_cache);
+  while (true) {
+    int used = 0;
+    while (tpos < to_transient.size() && used < n_transient) {
+      const int slot = n_cache + used;
+      jobs.push_back({to_transient[tpos].first, slot});
+      ++tpos;
+      ++used;
+    }
+    if ((st = decode_into(jobs, s, wave)) != ZMOE_OK) return st;
+    ready.insert(ready.end(), jobs.begin(), jobs.end());
+    if (!ready.empty()) {
+      if (wave >= max_waves - 1) { set_error("too many decode waves"); return ZMOE_EUNSUPPORTED; }
+      const uint16_t** tab = wtab_host + (size_t)wave * E * 3;
+      std::fill(tab, tab + (size_t)E * 3, nullptr);
+      for (auto [e, slot] : ready) {
+        tab[e * 3 + 0] = slot_ptr(slot, 0);
+        tab[e * 3 + 1] = tensors == 3 ? slot_ptr(slot, 1) : nullptr;
+        tab[e * 3 + 2] = slot_ptr(slot, tensors - 1);
+      }
+      zmoe_ffn_args fa{};
+      fa.x = xrows; fa.w = tab; fa.offsets = offsets_dev; fa.G = E; fa.rows_total = rows; fa.H = H;
+      fa.I = cfg.inter; fa.kind = cfg.kind; fa.h = h; fa.y = yrows;
+      int ev = -1;
+      if (timing) {
+        ev = ev_used;
+        cudaEvent_t a = next_event(), b = next_event();
+        if (!a || !b) { set_error("cudaEventCreate failed"); return ZMOE_ECUDA; }
+        ZMOE_CUDA_RET(cudaEventRecord(a, s));
+      }
+      if ((st = launch_expert_ffn(&fa, s)) != ZMOE_OK) return st;
+      if (timing) {
+        ZMOE_CUDA_RET(cudaEventRecord(ev_pool[ev + 1], s));
+        ev_pending.push_back({ev, 1, 0});
+      }
+      stats.launches += 2;
+    }
+    ++wave;
+    ready.clear();
+    jobs.clear();
+    if (tpos >= to_transient.size()) break;
+  }
+
+  return ZMOE_OK;
+}
+
+// Expert stage alone, for callers that route and exchange rows themselves
+// (expert parallelism): counts_h[e] rows of local expert e, grouped in order.
+zmoe_status Layer::experts(const uint16_t* xrows, const int32_t* counts_h, int rows, float* yrows, cudaStream_t s) {
+  const int E = cfg.num_experts;
+  ZMOE_CHECK_ARG(counts_h && (rows == 0 || (xrows && yrows)), "experts: null pointer");
+  ZMOE_CHECK_ARG(rows >= 0 && rows <= max_rows, "experts: rows=%d outside [0, max_tokens*topk=%d]", rows, max_rows);
+  long long sum = 0;
+  for (int e = 0; e < E; ++e) {
+    ZMOE_CHECK_ARG(counts_h[e] >= 0, "experts: negative count for expert %d", e);
+    sum += counts_h[e];
+  }
+  ZMOE_CHECK_ARG(sum == rows, "experts: counts sum to %lld, rows=%d", sum, rows);
+  for (int e = 0; e < E; ++e)
+    for (int t = 0; t < tensors; ++t)
+      ZMOE_CHECK_ARG(store[e][t].dev, "experts: expert %d tensor %d not loaded", e, t);
+  zmoe_status st;
+  // the previous call's pinned offsets may still be in flight
+  ZMOE_CUDA_RET(cudaStreamSynchronize(s));
+  if ((st = check_status()) != ZMOE_OK) return st;
+  desc_cursor = 0;
+  if ((st = fold_timing()) != ZMOE_OK) return st;
+  if (rows == 0) return ZMOE_OK;
+  offsets_host[0] = 0;
+  for (int e = 0; e < E; ++e) {
+    offsets_host[e + 1] = offsets_host[e] + counts_h[e];
+    counts_host[e] = counts_h[e];
+  }
+  ZMOE_CUDA_RET(cudaMemcpyAsync(offsets_ext, offsets_host, sizeof(int32_t) * (E + 1), cudaMemcpyHostToDevice, s));
+  if ((st = run_experts(xrows, offsets_ext, counts_host, rows, yrows, s)) != ZMOE_OK) return st;
+  stats.forwards++;
+  stats.tokens += rows;
+  return ZMOE_OK;
+}
+
 zmoe_status Layer::forward(const uint16_t* x, int T, uint16_t* out, cudaStream_t s) {
   ZMOE_CHECK_ARG(x && out, "forward: null pointer");
   ZMOE_CHECK_ARG(T >= 0 && T <= cfg.max_tokens, "forward: T=%d outside [0, max_tokens=%d]", T, cfg.max_tokens);
@@ -388,96 +530,7 @@ zmoe_status Layer::forward(const uint16_t* x, int T, uint16_t* out, cudaStream_t
   desc_cursor = 0;
   if ((st = fold_timing()) != ZMOE_OK) return st;
 
-  // 3. cache decisions (ProactiveDecision)
-  std::vector<char> active(E, 0);
-  std::vector<int> act;
-  for (int e = 0; e < E; ++e)
-    if (counts_host[e] > 0) { active[e] = 1; act.push_back(e); global_count[e] += counts_host[e]; }
-  ++clock;
-  std::vector<int> ranked(act);
-  std::vector<std::pair<int, int>> hits_slots;       // (expert, slot) ready to use
-  std::vector<int> misses;
-  for (int e : act) {
-    const int sl = expert_slot[e];
-    if (sl >= 0) {
-      stats.hits++;
-      slot_count[sl] += counts_host[e];
-      slot_stamp[sl] = clock;
-      hits_slots.push_back({e, sl});
-    } else {
-      stats.misses++;
-      misses.push_back(e);
-    }
-  }
-  // rank of each miss by global count (count_up of cache.cpp:230-238)
-  std::vector<std::pair<int, int>> to_cache, to_transient;
-  const double thr_normal = n_cache + cfg.state_margin * E;
-  for (int e : misses) {
-    int up = 0;
-    for (int q = 0; q < E; ++q) up += global_count[q] > global_count[e];
-    int slot = -1;
-    if (n_cache > 0 && up < thr_normal) {
-      slot = choose_victim(active);
-      if (slot >= 0) {
-        if (slot_owner[slot] >= 0) { expert_slot[slot_owner[slot]] = -1; stats.evictions++; }
-        slot_owner[slot] = e;
-        expert_slot[e] = slot;
-        slot_count[slot] = counts_host[e];
-        slot_stamp[slot] = clock;
-        slot_admit[slot] = clock;
-        to_cache.push_back({e, slot});
-        continue;
-      }
-    }
-    to_transient.push_back({e, -1});
-  }
-
-  // 4. waves: decode misses, run the grouped FFN over experts whose weights are ready
-  size_t tpos = 0;
-  int wave = 0;
-  std::vector<std::pair<int, int>> ready(hits_slots);
-  std::vector<std::pair<int, int>> jobs(to_cache);
-  while (true) {
-    int used = 0;
-    while (tpos < to_transient.size() && used < n_transient) {
-      const int slot = n_cache + used;
-      jobs.push_back({to_transient[tpos].first, slot});
-      ++tpos;
-      ++used;
-    }
-    if ((st = decode_into(jobs, s, wave)) != ZMOE_OK) return st;
-    ready.insert(ready.end(), jobs.begin(), jobs.end());
-    if (!ready.empty()) {
-      if (wave >= max_waves - 1) { set_error("too many decode waves"); return ZMOE_EUNSUPPORTED; }
-      const uint16_t** tab = wtab_host + (size_t)wave * E * 3;
-      std::fill(tab, tab + (size_t)E * 3, nullptr);
-      for (auto [e, slot] : ready) {
-        tab[e * 3 + 0] = slot_ptr(slot, 0);
-        tab[e * 3 + 1] = tensors == 3 ? slot_ptr(slot, 1) : nullptr;
-        tab[e * 3 + 2] = slot_ptr(slot, tensors - 1);
-      }
-      zmoe_ffn_args fa{};
-      fa.x = xp; fa.w = tab; fa.offsets = offsets; fa.G = E; fa.rows_total = T * k; fa.H = H;
-      fa.I = cfg.inter; fa.kind = cfg.kind; fa.h = h; fa.y = y;
-      int ev = -1;
-      if (timing) {
-        ev = ev_used;
-        cudaEvent_t a = next_event(), b = next_event();
-        if (!a || !b) { set_error("cudaEventCreate failed"); return ZMOE_ECUDA; }
-        ZMOE_CUDA_RET(cudaEventRecord(a, s));
-      }
-      if ((st = launch_expert_ffn(&fa, s)) != ZMOE_OK) return st;
-      if (timing) {
-        ZMOE_CUDA_RET(cudaEventRecord(ev_pool[ev + 1], s));
-        ev_pending.push_back({ev, 1, 0});
-      }
-      stats.launches += 2;
-    }
-    ++wave;
-    ready.clear();
-    jobs.clear();
-    if (tpos >= to_transient.size()) break;
-  }
+  if ((st = run_experts(xp, offsets, counts_host, T * k, y, s)) != ZMOE_OK) return st;
 
   // 5. combine
   zmoe_combine_args ca{};
@@ -645,6 +698,13 @@ zmoe_status zmoe_layer_forward(zmoe_layer* layer, const uint16_t* x, int T, uint
   Layer* L = reinterpret_cast<Layer*>(layer);
   ZMOE_CHECK_ARG(L, "forward: null layer");
   return L->forward(x, T, out, reinterpret_cast<cudaStream_t>(stream));
+}
+
+zmoe_status zmoe_layer_experts(zmoe_layer* layer, const uint16_t* x_rows, const int32_t* counts_host, int rows,
+                               float* y, zmoe_stream_t stream) {
+  Layer* L = reinterpret_cast<Layer*>(layer);
+  ZMOE_CHECK_ARG(L, "experts: null layer");
+  return L->experts(x_rows, counts_host, rows, y, reinterpret_cast<cudaStream_t>(stream));
 }
 
 zmoe_status zmoe_layer_forward_host(zmoe_layer* layer, const uint16_t* x_host, int T, uint16_t* out_host,

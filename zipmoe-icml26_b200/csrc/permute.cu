@@ -127,6 +127,19 @@ gather_kernel(const uint16_t* __restrict__ x, int H, const int32_t* __restrict__
   }
 }
 
+// dst[r] = src[index[r]], 16 bytes per thread and step.
+__global__ void __launch_bounds__(kThreads)
+gather_rows_kernel(const uint4* __restrict__ src, const int32_t* __restrict__ index, int rows, int vec,
+                   uint4* __restrict__ dst) {
+  const size_t total = (size_t)rows * vec;
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+    const size_t r = i / vec;
+    const int c = (int)(i % vec);
+    dst[r * vec + c] = __ldg(src + (size_t)__ldg(index + r) * vec + c);
+  }
+}
+
 }  // namespace
 
 zmoe_status launch_permute(const zmoe_permute_args* a, cudaStream_t stream) {
@@ -157,6 +170,21 @@ zmoe_status launch_permute(const zmoe_permute_args* a, cudaStream_t stream) {
   gather_kernel<<<(unsigned)blocks, kThreads, 0, stream>>>(a->x, a->H, a->offsets, a->E, a->token_of_row,
                                                             a->xp, max_rows);
   return launch_status("gather_kernel");
+}
+
+zmoe_status launch_gather_rows(const void* src, const int32_t* index, int rows, int row_bytes, void* dst,
+                               cudaStream_t stream) {
+  ZMOE_CHECK_ARG(rows >= 0 && row_bytes > 0 && row_bytes % 16 == 0, "gather_rows: rows=%d, row_bytes=%d (multiple of 16)",
+                 rows, row_bytes);
+  if (rows == 0) return ZMOE_OK;
+  ZMOE_CHECK_ARG(src && index && dst && (uintptr_t)src % 16 == 0 && (uintptr_t)dst % 16 == 0,
+                 "gather_rows: null or unaligned pointer");
+  const int vec = row_bytes / 16;
+  size_t blocks = ((size_t)rows * vec + kThreads - 1) / kThreads;
+  if (blocks > (size_t)kNumSMs * 8) blocks = (size_t)kNumSMs * 8;
+  gather_rows_kernel<<<(unsigned)blocks, kThreads, 0, stream>>>(static_cast<const uint4*>(src), index, rows, vec,
+                                                                static_cast<uint4*>(dst));
+  return launch_status("gather_rows_kernel");
 }
 
 }  // namespace zmoe

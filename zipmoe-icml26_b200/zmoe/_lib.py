@@ -79,6 +79,7 @@ SIGNATURES = {
     "zmoe_expert_ffn": (c_int, [ctypes.POINTER(FfnArgs), c_void_p]),
     "zmoe_expert_ffn_noalloc": (c_int, [ctypes.POINTER(FfnArgs), c_void_p]),
     "zmoe_combine": (c_int, [ctypes.POINTER(CombineArgs), c_void_p]),
+    "zmoe_gather_rows": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p]),
     "zmoe_split_planes": (c_int, [c_void_p, ctypes.c_uint64, c_void_p, c_void_p]),
     "zmoe_lz4_compress_bound": (c_int, [c_int]),
     "zmoe_lz4_compress": (c_int, [c_void_p, c_int, c_void_p, c_int, c_int, c_int]),
@@ -92,6 +93,7 @@ SIGNATURES = {
                                        ctypes.c_uint64]),
     "zmoe_layer_warm_cache": (c_int, [c_void_p, ctypes.POINTER(c_int), c_int, c_void_p]),
     "zmoe_layer_forward": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p]),
+    "zmoe_layer_experts": (c_int, [c_void_p, c_void_p, ctypes.POINTER(ctypes.c_int32), c_int, c_void_p, c_void_p]),
     "zmoe_layer_forward_host": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p]),
     "zmoe_layer_sync": (c_int, [c_void_p, c_void_p]),
     "zmoe_layer_get_stats": (c_int, [c_void_p, ctypes.POINTER(LayerStats)]),

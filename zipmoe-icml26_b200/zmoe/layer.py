@@ -116,6 +116,25 @@ class MoELayer:
               "zmoe_layer_forward_host")
         return out
 
+    def experts(self, x_rows: torch.Tensor, counts, y: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Expert stage alone (zmoe_layer_experts): x_rows [rows, H] BF16 grouped
+        by this layer's experts, counts[e] rows of expert e; returns fp32 [rows, H]."""
+        import numpy as np
+        c = np.ascontiguousarray(np.asarray(counts, dtype=np.int32))
+        if c.size != self.shape.num_experts:
+            raise ValueError(f"counts has {c.size} entries, layer has {self.shape.num_experts} experts")
+        rows = int(c.sum())
+        if rows and (not x_rows.is_cuda or x_rows.dtype != torch.bfloat16 or not x_rows.is_contiguous()
+                     or x_rows.shape[0] < rows):
+            raise ValueError("x_rows must be a contiguous CUDA BF16 tensor with sum(counts) rows")
+        if y is None:
+            y = torch.empty(rows, self.shape.hidden, dtype=torch.float32, device=self.device)
+        check(lib.zmoe_layer_experts(self._h, x_rows.data_ptr() if rows else None,
+                                     c.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), rows,
+                                     y.data_ptr() if rows else None,
+                                     torch.cuda.current_stream(self.device).cuda_stream), "zmoe_layer_experts")
+        return y
+
     def sync(self):
         check(lib.zmoe_layer_sync(self._h, torch.cuda.current_stream(self.device).cuda_stream), "zmoe_layer_sync")
 
