@@ -308,6 +308,15 @@ zmoe_status zmoe_layer_reset_stats(zmoe_layer* layer);
 /* Record CUDA events around every decode and routed-FFN launch (stats *_ns). */
 zmoe_status zmoe_layer_set_timing(zmoe_layer* layer, int enable);
 zmoe_status zmoe_layer_cached_experts(const zmoe_layer* layer, int32_t* experts, int cap, int* n);
+/* Decode experts into cache slots ahead of use (victims by the cache policy,
+ * never one of `experts`); returns without waiting for the decode.  Replaces
+ * ExpertDispatcher::SubmitPrefetch / EnqueuePrefetch
+ * (csrc/dispatcher/expert_dispatcher.cpp:220-277). */
+zmoe_status zmoe_layer_prefetch(zmoe_layer* layer, const int* experts, int n, zmoe_stream_t stream);
+/* Zero the per-expert token counts behind the cache decision (the admission
+ * rank and the LFU/ZipMoE victim keys); replaces
+ * ZipMoECacheHandle::reset_global_access_counts (csrc/memory/cache.cpp). */
+zmoe_status zmoe_layer_reset_access_counts(zmoe_layer* layer);
 
 #ifdef __cplusplus
 }

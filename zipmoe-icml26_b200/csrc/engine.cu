@@ -694,6 +694,39 @@ zmoe_status zmoe_layer_warm_cache(zmoe_layer* layer, const int* experts, int n, 
   return L->check_status();
 }
 
+zmoe_status zmoe_layer_prefetch(zmoe_layer* layer, const int* experts, int n, zmoe_stream_t stream) {
+  Layer* L = reinterpret_cast<Layer*>(layer);
+  ZMOE_CHECK_ARG(L && (n == 0 || experts), "prefetch: null pointer");
+  const int E = L->cfg.num_experts;
+  std::vector<char> keep(E, 0);                  // experts of this call are not each other's victims
+  for (int i = 0; i < n; ++i) {
+    ZMOE_CHECK_ARG(experts[i] >= 0 && experts[i] < E, "prefetch: expert %d out of range", experts[i]);
+    for (int t = 0; t < L->tensors; ++t)
+      ZMOE_CHECK_ARG(L->store[experts[i]][t].dev, "prefetch: expert %d not loaded", experts[i]);
+    keep[experts[i]] = 1;
+  }
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  ZMOE_CUDA_RET(cudaStreamSynchronize(s));
+  zmoe_status st = L->check_status();
+  if (st != ZMOE_OK) return st;
+  L->desc_cursor = 0;
+  std::vector<std::pair<int, int>> jobs;
+  for (int i = 0; i < n && L->n_cache > 0; ++i) {
+    const int e = experts[i];
+    if (L->expert_slot[e] >= 0) continue;
+    const int slot = L->choose_victim(keep);
+    if (slot < 0) break;                           // every slot holds an expert of this call
+    if (L->slot_owner[slot] >= 0) { L->expert_slot[L->slot_owner[slot]] = -1; L->stats.evictions++; }
+    L->slot_owner[slot] = e;
+    L->expert_slot[e] = slot;
+    L->slot_count[slot] = 0;
+    L->slot_stamp[slot] = L->clock;
+    L->slot_admit[slot] = L->clock;
+    jobs.push_back({e, slot});
+  }
+  return L->decode_into(jobs, s, 0);
+}
+
 zmoe_status zmoe_layer_forward(zmoe_layer* layer, const uint16_t* x, int T, uint16_t* out, zmoe_stream_t stream) {
   Layer* L = reinterpret_cast<Layer*>(layer);
   ZMOE_CHECK_ARG(L, "forward: null layer");
@@ -751,6 +784,14 @@ zmoe_status zmoe_layer_get_stats(const zmoe_layer* layer, zmoe_layer_stats* out)
   const Layer* L = reinterpret_cast<const Layer*>(layer);
   ZMOE_CHECK_ARG(L && out, "get_stats: null pointer");
   *out = L->stats;
+  return ZMOE_OK;
+}
+
+zmoe_status zmoe_layer_reset_access_counts(zmoe_layer* layer) {
+  Layer* L = reinterpret_cast<Layer*>(layer);
+  ZMOE_CHECK_ARG(L, "reset_access_counts: null layer");
+  std::fill(L->global_count.begin(), L->global_count.end(), 0);
+  std::fill(L->slot_count.begin(), L->slot_count.end(), 0);
   return ZMOE_OK;
 }
 
