@@ -90,6 +90,7 @@ struct Chunk {
 
 __device__ __forceinline__ void set_err(Smem& S, int32_t code) { atomicCAS(&S.err, 0, code); }
 
+
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
                : "memory");
@@ -178,73 +179,138 @@ __device__ __forceinline__ void stage_issue(Smem& S, const Chunk& c, const Stage
 // ---------------------------------------------------------------------------
 // phase 2: map one 256-byte slice per thread
 // ---------------------------------------------------------------------------
-__device__ int map_slice(Smem& S, const Chunk& c, const StageRange& st, uint32_t g) {
+// The sequence being mapped: output bytes [so, ms) are literals (compressed
+// byte lit_base + position), [ms, me) match bytes.  Match byte e repeats every
+// o bytes back to ms - o; with wrap = max(ms, step0) its source cycles through
+// [wrap - o, wrap): below the step when the copy began before it, else the
+// run's first copy (inside the step: chased by the resolve).
+struct Run {
+  uint32_t ms, me, o, wrap, v, lit_base, next;
+  bool last;
+};
+
+template <class ByteAt>
+__device__ __forceinline__ int open_run(ByteAt byte_at, uint32_t size, uint32_t ip, uint32_t so, uint32_t step0,
+                                        Run& r) {
+  Seq s;
+  const int err = read_seq(byte_at, size, ip, s);
+  if (err) return err;
+  r.ms = so + s.ll;
+  r.me = r.ms + s.ml;
+  r.o = s.off;
+  if (s.ml > 0 && (r.o == 0 || r.o > r.ms)) return ZMOE_CHUNK_BAD_OFFSET;
+  r.wrap = max(r.ms, step0);
+  r.v = r.wrap - r.o;                                  // the source of byte ms when ms >= step0
+  r.lit_base = s.lit - so;
+  r.next = s.next;
+  r.last = s.last;
+  return 0;
+}
+
+// Map entry of byte p of the run (p in [so, me), in increasing order).
+template <class ByteAt>
+__device__ __forceinline__ uint32_t run_entry(Run& r, uint32_t p, uint32_t step0, ByteAt byte_at) {
+  if (p < r.ms) return kLit | byte_at(r.lit_base + p);
+  const uint32_t x = r.v >= step0 ? (r.v | kInner) : r.v;
+  if (++r.v == r.wrap) r.v -= r.o;
+  return x;
+}
+
+// Staged compressed bytes, read with a clamped index: a read outside the
+// staged range returns 0 and sets miss (the slice is then mapped again with
+// checked reads).
+struct Staged {
+  const uint8_t* p;
+  uint32_t lo, len;
+  __device__ __forceinline__ uint32_t at(uint32_t q, bool& miss) const {
+    const uint32_t d = q - lo;
+    miss |= d >= len;
+    return d < len ? (uint32_t)p[d] : 0u;
+  }
+};
+
+// run_entry without a branch: the literal byte is read for every position
+// (from shared memory) and selected.
+__device__ __forceinline__ uint32_t run_entry_staged(Run& r, uint32_t p, uint32_t step0, const Staged& sv,
+                                                     bool& miss) {
+  const bool lit = p < r.ms;
+  const uint32_t d = r.lit_base + p - sv.lo;
+  miss |= lit && d >= sv.len;
+  const uint32_t lb = sv.p[min(d, sv.len - 1)];
+  const uint32_t xm = r.v >= step0 ? (r.v | kInner) : r.v;
+  uint32_t nv = r.v + 1;
+  nv = nv == r.wrap ? nv - r.o : nv;
+  r.v = lit ? r.v : nv;
+  return lit ? (kLit | lb) : xm;
+}
+
+// The slice is walked in 64 groups of 4 bytes, the same count in every lane,
+// with at most one new sequence per group (every sequence but the last covers
+// at least 4 bytes): lanes diverge only while a header is parsed, and each
+// group is one 128-bit map store.  kStaged: every read from the staged bytes
+// (the result is void if miss is set); otherwise checked reads that fall back
+// to global memory.
+template <bool kStaged>
+__device__ int map_slice_walk(Smem& S, const Chunk& c, const StageRange& st, uint32_t g, bool& miss) {
   const uint32_t b0 = g * kSlice;
-  if (b0 >= c.out_size) return 0;
-  if (g >= c.n_index) return ZMOE_CHUNK_BAD_DESC;
   const uint2 ix = __ldg(reinterpret_cast<const uint2*>(c.index) + g);
-  uint32_t ip = ix.x;
-  uint32_t so = ix.y;                                  // output start of the sequence at ip
+  const uint32_t so = ix.y;                            // output start of the sequence at ix.x
   if (so > b0) return ZMOE_CHUNK_BAD_DESC;
   const uint32_t b1 = min(b0 + kSlice, c.out_size);
   const uint32_t step0 = b0 & ~(kStep - 1);            // a slice lies inside one step
   const uint8_t* stage = S.u.stage;
-  auto byte_at = [&](uint32_t q) -> uint32_t {
+  const Staged sv{stage, st.lo, st.len};
+  auto checked = [&](uint32_t q) -> uint32_t {
     const uint32_t d = q - st.lo;
     return d < st.len ? (uint32_t)stage[d] : (uint32_t)__ldg(c.src + q);
   };
-  uint4* map4 = reinterpret_cast<uint4*>(c.map);
-  uint32_t e = b0;
-  uint32_t r0 = 0, r1 = 0, r2 = 0;                     // entries waiting for a 128-bit store
-  auto put = [&](uint32_t pos, uint32_t v) {           // selects, not a branch: lanes sit at any pos & 3
-    const uint32_t k = pos & 3;
-    r0 = k == 0 ? v : r0;
-    r1 = k == 1 ? v : r1;
-    r2 = k == 2 ? v : r2;
-    if (k == 3) map4[(pos & (kRegion - 1)) >> 2] = make_uint4(r0, r1, r2, v);
+  auto fast = [&](uint32_t q) -> uint32_t { return sv.at(q, miss); };
+  auto entry = [&](Run& r, uint32_t p) -> uint32_t {
+    if constexpr (kStaged) return run_entry_staged(r, p, step0, sv, miss);
+    else return run_entry(r, p, step0, checked);
   };
-  while (e < b1) {
-    Seq s;
-    const int err = read_seq(byte_at, c.src_size, ip, s);
-    if (err) return err;
-    const uint32_t ms = so + s.ll;                     // first match byte
-    const uint32_t me = ms + s.ml;
-    const uint32_t o = s.off;
-    if (s.ml > 0 && (o == 0 || o > ms)) return ZMOE_CHUNK_BAD_OFFSET;
-    // Literal bytes, then match bytes, in one loop.  Match byte e repeats
-    // every o bytes back to ms - o.  With wrap = max(ms, step0), its source
-    // cycles through [wrap - o, wrap): below the step when the copy began
-    // before it, else the run's first copy (inside the step: chased later).
-    const uint32_t wrap = max(ms, step0);
-    uint32_t v = wrap - o;                             // e < ms: the match begins at ms >= e >= step0
-    if (e >= ms && s.ml > 0) {                         // the slice starts inside this match
-      const uint32_t d = e - wrap;
-      v += d < o ? d : d % o;
-    }
-    const uint32_t lit_base = s.lit - so;
-    for (const uint32_t end = min(b1, me); e < end; ++e) {
-      uint32_t x;
-      if (e < ms) {
-        x = kLit | byte_at(lit_base + e);
-      } else {
-        x = v >= step0 ? (v | kInner) : v;
-        if (++v == wrap) v -= o;
-      }
-      put(e, x);
-    }
-    if (e < b1) {
-      if (s.last) return ZMOE_CHUNK_SHORT_OUTPUT;
-      ip = s.next;
-      so = me;
-    }
+  auto open = [&](uint32_t ip, uint32_t so_, Run& r) -> int {
+    if constexpr (kStaged) return open_run(fast, c.src_size, ip, so_, step0, r);
+    else return open_run(checked, c.src_size, ip, so_, step0, r);
+  };
+  Run r;
+  int err = open(ix.x, so, r);
+  if (err) return err;
+  if (r.me <= b0) return ZMOE_CHUNK_BAD_DESC;          // the index names a sequence ending before b0
+  if (b0 > r.ms) {                                     // the slice starts inside the match
+    const uint32_t d = b0 - r.wrap;
+    r.v += d < r.o ? d : d % r.o;
   }
-  if (e & 3) {                                         // partial group at the chunk end
-    const uint32_t i0 = (e & ~3u) & (kRegion - 1);
-    c.map[i0] = r0;
-    if ((e & 3) > 1) c.map[i0 + 1] = r1;
-    if ((e & 3) > 2) c.map[i0 + 2] = r2;
+  uint4* map4 = reinterpret_cast<uint4*>(c.map);
+  for (uint32_t p0 = b0; p0 < b1; p0 += 4) {
+    const uint32_t me0 = r.me;
+    uint32_t x0 = 0, x1 = 0, x2 = 0, x3 = 0;
+    if (p0 + 0 < me0) x0 = entry(r, p0 + 0);
+    if (p0 + 1 < me0) x1 = entry(r, p0 + 1);
+    if (p0 + 2 < me0) x2 = entry(r, p0 + 2);
+    if (p0 + 3 < me0) x3 = entry(r, p0 + 3);
+    if (me0 <= p0 + 4 && me0 < b1) {                   // the next sequence starts in or right after the group
+      if (r.last) return ZMOE_CHUNK_SHORT_OUTPUT;
+      if ((err = open(r.next, me0, r)) != 0) return err;
+      if (r.me < min(p0 + 4, b1)) return ZMOE_CHUNK_SHORT_OUTPUT;   // only the last one can be this short
+      if (p0 + 1 >= me0) x1 = entry(r, p0 + 1);
+      if (p0 + 2 >= me0) x2 = entry(r, p0 + 2);
+      if (p0 + 3 >= me0) x3 = entry(r, p0 + 3);
+    }
+    map4[(p0 % kRegion) / 4] = make_uint4(x0, x1, x2, x3);
   }
   return 0;
+}
+
+__device__ int map_slice(Smem& S, const Chunk& c, const StageRange& st, uint32_t g) {
+  if (g * kSlice >= c.out_size) return 0;
+  if (g >= c.n_index) return ZMOE_CHUNK_BAD_DESC;
+  bool miss = st.len == 0;
+  if (!miss) {
+    const int err = map_slice_walk<true>(S, c, st, g, miss);
+    if (!miss) return err;
+  }
+  return map_slice_walk<false>(S, c, st, g, miss);   // some byte was not staged: checked reads
 }
 
 // ---------------------------------------------------------------------------
