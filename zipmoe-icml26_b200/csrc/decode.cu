@@ -180,12 +180,9 @@ __device__ __forceinline__ void stage_issue(Smem& S, const Chunk& c, const Stage
 // phase 2: map one 256-byte slice per thread
 // ---------------------------------------------------------------------------
 // The sequence being mapped: output bytes [so, ms) are literals (compressed
-// byte lit_base + position), [ms, me) match bytes.  Match byte e repeats every
-// o bytes back to ms - o; with wrap = max(ms, step0) its source cycles through
-// [wrap - o, wrap): below the step when the copy began before it, else the
-// run's first copy (inside the step: chased by the resolve).
+// byte lit_base + position), [ms, me) match bytes.
 struct Run {
-  uint32_t ms, me, o, wrap, v, lit_base, next;
+  uint32_t ms, me, o, wrap, lit_base, next;
   bool last;
 };
 
@@ -200,20 +197,23 @@ __device__ __forceinline__ int open_run(ByteAt byte_at, uint32_t size, uint32_t 
   r.o = s.off;
   if (s.ml > 0 && (r.o == 0 || r.o > r.ms)) return ZMOE_CHUNK_BAD_OFFSET;
   r.wrap = max(r.ms, step0);
-  r.v = r.wrap - r.o;                                  // the source of byte ms when ms >= step0
   r.lit_base = s.lit - so;
   r.next = s.next;
   r.last = s.last;
   return 0;
 }
 
-// Map entry of byte p of the run (p in [so, me), in increasing order).
-template <class ByteAt>
-__device__ __forceinline__ uint32_t run_entry(Run& r, uint32_t p, uint32_t step0, ByteAt byte_at) {
-  if (p < r.ms) return kLit | byte_at(r.lit_base + p);
-  const uint32_t x = r.v >= step0 ? (r.v | kInner) : r.v;
-  if (++r.v == r.wrap) r.v -= r.o;
-  return x;
+// Source of match byte p (p >= ms) of a copy with offset o.  A plain copy
+// (p - ms < o, all but 0.01% of the bytes of an exponent plane) reads byte
+// p - o.  A byte of a run longer than its offset repeats every o bytes back to
+// ms - o; with wrap = max(ms, step0) its source is the copy in [wrap - o, wrap):
+// below the step when the run began before it, else the run's first copy.
+// Either way a source at or after step0 lies inside the step and is marked
+// for the resolve's chase.
+__device__ __forceinline__ uint32_t match_entry(uint32_t p, uint32_t ms, uint32_t o, uint32_t wrap, uint32_t step0) {
+  uint32_t v = p - o;
+  if (p - ms >= o && o != 0) v = wrap - o + (p - wrap) % o;
+  return v >= step0 ? (v | kInner) : v;
 }
 
 // Staged compressed bytes, read with a clamped index: a read outside the
@@ -229,27 +229,14 @@ struct Staged {
   }
 };
 
-// run_entry without a branch: the literal byte is read for every position
-// (from shared memory) and selected.
-__device__ __forceinline__ uint32_t run_entry_staged(Run& r, uint32_t p, uint32_t step0, const Staged& sv,
-                                                     bool& miss) {
-  const bool lit = p < r.ms;
-  const uint32_t d = r.lit_base + p - sv.lo;
-  miss |= lit && d >= sv.len;
-  const uint32_t lb = sv.p[min(d, sv.len - 1)];
-  const uint32_t xm = r.v >= step0 ? (r.v | kInner) : r.v;
-  uint32_t nv = r.v + 1;
-  nv = nv == r.wrap ? nv - r.o : nv;
-  r.v = lit ? r.v : nv;
-  return lit ? (kLit | lb) : xm;
-}
-
-// The slice is walked in 64 groups of 4 bytes, the same count in every lane,
-// with at most one new sequence per group (every sequence but the last covers
-// at least 4 bytes): lanes diverge only while a header is parsed, and each
-// group is one 128-bit map store.  kStaged: every read from the staged bytes
-// (the result is void if miss is set); otherwise checked reads that fall back
-// to global memory.
+// The slice is walked in 64 groups of 4 bytes, the same count in every lane.
+// A sequence that starts inside (or right after) a group is opened before the
+// group's entries are formed (every sequence but the last covers at least 4
+// bytes, so a group meets at most two), each byte takes its fields from the
+// sequence it belongs to, and the group is one 128-bit map store.  Lanes
+// diverge only while a header is parsed.  kStaged: every read from the staged
+// bytes, the literal byte read for every position and selected (the result is
+// void if miss is set); otherwise checked reads that fall back to global memory.
 template <bool kStaged>
 __device__ int map_slice_walk(Smem& S, const Chunk& c, const StageRange& st, uint32_t g, bool& miss) {
   const uint32_t b0 = g * kSlice;
@@ -265,39 +252,43 @@ __device__ int map_slice_walk(Smem& S, const Chunk& c, const StageRange& st, uin
     return d < st.len ? (uint32_t)stage[d] : (uint32_t)__ldg(c.src + q);
   };
   auto fast = [&](uint32_t q) -> uint32_t { return sv.at(q, miss); };
-  auto entry = [&](Run& r, uint32_t p) -> uint32_t {
-    if constexpr (kStaged) return run_entry_staged(r, p, step0, sv, miss);
-    else return run_entry(r, p, step0, checked);
-  };
   auto open = [&](uint32_t ip, uint32_t so_, Run& r) -> int {
     if constexpr (kStaged) return open_run(fast, c.src_size, ip, so_, step0, r);
     else return open_run(checked, c.src_size, ip, so_, step0, r);
   };
-  Run r;
-  int err = open(ix.x, so, r);
+  auto entry = [&](uint32_t p, const Run& a, const Run& b) -> uint32_t {
+    const bool in_a = p < a.me;
+    const uint32_t ms = in_a ? a.ms : b.ms, o = in_a ? a.o : b.o;
+    const uint32_t wrap = in_a ? a.wrap : b.wrap, lit_base = in_a ? a.lit_base : b.lit_base;
+    if constexpr (kStaged) {
+      const bool lit = p < ms;
+      const uint32_t d = lit_base + p - sv.lo;
+      miss |= lit && d >= sv.len;
+      const uint32_t lb = sv.p[min(d, sv.len - 1)];
+      const uint32_t xm = match_entry(p, ms, o, wrap, step0);
+      return lit ? (kLit | lb) : xm;
+    } else {
+      if (p < ms) return kLit | checked(lit_base + p);
+      return match_entry(p, ms, o, wrap, step0);
+    }
+  };
+  Run cur;
+  int err = open(ix.x, so, cur);
   if (err) return err;
-  if (r.me <= b0) return ZMOE_CHUNK_BAD_DESC;          // the index names a sequence ending before b0
-  if (b0 > r.ms) {                                     // the slice starts inside the match
-    const uint32_t d = b0 - r.wrap;
-    r.v += d < r.o ? d : d % r.o;
-  }
+  if (cur.me <= b0) return ZMOE_CHUNK_BAD_DESC;        // the index names a sequence ending before b0
   uint4* map4 = reinterpret_cast<uint4*>(c.map);
   for (uint32_t p0 = b0; p0 < b1; p0 += 4) {
-    const uint32_t me0 = r.me;
-    uint32_t x0 = 0, x1 = 0, x2 = 0, x3 = 0;
-    if (p0 + 0 < me0) x0 = entry(r, p0 + 0);
-    if (p0 + 1 < me0) x1 = entry(r, p0 + 1);
-    if (p0 + 2 < me0) x2 = entry(r, p0 + 2);
-    if (p0 + 3 < me0) x3 = entry(r, p0 + 3);
-    if (me0 <= p0 + 4 && me0 < b1) {                   // the next sequence starts in or right after the group
-      if (r.last) return ZMOE_CHUNK_SHORT_OUTPUT;
-      if ((err = open(r.next, me0, r)) != 0) return err;
-      if (r.me < min(p0 + 4, b1)) return ZMOE_CHUNK_SHORT_OUTPUT;   // only the last one can be this short
-      if (p0 + 1 >= me0) x1 = entry(r, p0 + 1);
-      if (p0 + 2 >= me0) x2 = entry(r, p0 + 2);
-      if (p0 + 3 >= me0) x3 = entry(r, p0 + 3);
+    Run nxt = cur;
+    const bool turn = cur.me <= p0 + 4 && cur.me < b1;
+    if (turn) {
+      if (cur.last) return ZMOE_CHUNK_SHORT_OUTPUT;
+      if ((err = open(cur.next, cur.me, nxt)) != 0) return err;
+      if (nxt.me < min(p0 + 4, b1)) return ZMOE_CHUNK_SHORT_OUTPUT;   // only the last one can be this short
     }
-    map4[(p0 % kRegion) / 4] = make_uint4(x0, x1, x2, x3);
+    const uint4 x = make_uint4(entry(p0 + 0, cur, nxt), entry(p0 + 1, cur, nxt), entry(p0 + 2, cur, nxt),
+                               entry(p0 + 3, cur, nxt));
+    map4[(p0 % kRegion) / 4] = x;
+    if (turn) cur = nxt;
   }
   return 0;
 }
