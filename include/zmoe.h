@@ -68,14 +68,14 @@ zmoe_status zmoe_tensor_recover(uint16_t* out, const uint8_t* exp, const uint8_t
  * BF16 straight into the destination slot.
  * ------------------------------------------------------------------------ */
 #define ZMOE_SLICE_BYTES 256      /* output bytes per slice-index entry */
-#define ZMOE_MAP_ENTRIES 65536    /* uint32 scratch entries per indexed chunk (256 KiB) */
+#define ZMOE_MAP_ENTRIES 65536    /* map entries per 64 KiB region of output */
 
 typedef struct zmoe_chunk {
   const uint8_t* src;   /* LZ4 block, device memory */
   const uint8_t* sm;    /* sign+mantissa bytes of this chunk's elements */
   uint16_t* dst;        /* BF16 output of this chunk's elements */
   const uint32_t* index;/* device [n_index][2] slice index from zmoe_lz4_build_index, or NULL */
-  uint32_t* map;        /* device scratch, ZMOE_MAP_ENTRIES uint32, 16-byte aligned (with index) */
+  uint32_t* map;        /* device scratch of zmoe_decode_scratch_bytes(out_size), 16-byte aligned (with index) */
   uint32_t src_size;    /* compressed bytes */
   uint32_t out_size;    /* exponent bytes = elements (original_sizes[c]) */
   uint32_t n_index;     /* entries in index */
@@ -88,6 +88,10 @@ typedef struct zmoe_chunk {
  * BF16; without an index one warp decodes the chunk serially. */
 zmoe_status zmoe_decode_chunks(const zmoe_chunk* chunks, int n_chunks, int32_t* status,
                                zmoe_stream_t stream);
+/* Scratch bytes an indexed chunk of out_size exponent bytes needs in
+ * zmoe_chunk.map: one source-map entry per output byte (whole 64 KiB regions)
+ * and one status word per region. */
+uint64_t zmoe_decode_scratch_bytes(uint32_t out_size);
 
 /* Host: slice index of one LZ4 block (no counterpart in the reference; the
  * reference decodes each block serially on one CPU thread).  Entry j =

@@ -83,7 +83,7 @@ def test_decode_many_chunks_one_launch_unaligned_destinations():
         descs.extend(ct.descs(v))
         views.append(v)
         pos += b.size
-    scratch = ops.map_scratch(len(descs), "cuda")
+    scratch = ops.map_scratch([d[4] for d in descs], "cuda")
     table = ops.chunk_table(descs, "cuda", scratch)
     st = ops.decode_chunks(table, len(descs))
     torch.cuda.synchronize()

@@ -9,20 +9,21 @@
 // Exponent planes compress into many short sequences (about one per 7 output
 // bytes, 92% of the bytes in matches, match chains tens deep), so the bytes of
 // a block depend on each other almost serially while the token stream does
-// not.  One CTA of 256 threads decodes one block, 64 KiB of output (a region)
-// at a time, in four barrier-separated phases:
+// not.  Output is handled in 64 KiB regions, by two kernels on one stream:
 //
-//  1. Stage: the region's compressed bytes are copied into shared memory
-//     (cp.async, issued while the previous region is being flushed).
+//  map_kernel, one CTA of 256 threads per region (of every chunk at once):
+//  1. Stage: the region's compressed bytes are copied into shared memory.
 //  2. Map: a slice index built when the block is loaded (zmoe_lz4_build_index)
 //     names, for every 256 output bytes, the sequence that contains the first
-//     of them.  Each thread parses one slice on its own and writes one 32-bit
-//     entry per output byte into a per-chunk map in L2-resident scratch: a
-//     literal value, or the position of an earlier byte with the same value.
-//     For a match byte that position is the latest equal byte before the
-//     2 KiB step holding it when one exists (a run of period o repeats every
-//     o bytes), so it is always resolved already; otherwise it is the first
-//     copy of the run, inside the step, and is marked for a chase.
+//     of them.  Each thread maps one slice on its own and writes one 32-bit
+//     entry per output byte into the chunk's scratch: a literal value, or the
+//     position of an earlier byte with the same value.  For a match byte that
+//     position is the source itself, or, for a run longer than its offset,
+//     the latest equal byte before the 2 KiB step holding it when one exists;
+//     a source inside the byte's own step is marked for a chase.  Each region
+//     also gets a status word.
+//
+//  resolve_kernel, one CTA of 256 threads per chunk, region by region:
 //  3. Resolve: step by step (2 KiB, 8 bytes per thread), the entries are
 //     copied into shared memory (cp.async, three steps ahead) and every byte is
 //     gathered from a 64 KiB shared-memory window of decoded exponents; marked
@@ -31,14 +32,16 @@
 //  4. Flush: 16 exponent bytes and 16 sign+mantissa bytes (128-bit loads)
 //     become 16 BF16 values (two 128-bit stores) per thread and group.
 //
-// A chunk without an index (zmoe_chunk.index == NULL) is decoded by warp 0
-// alone in one pass straight into the output (no scratch needed).
+// Only the resolve is serial within a chunk; mapping every region at once
+// keeps the SMs busy when few chunks are decoded.  A chunk without an index
+// (zmoe_chunk.index == NULL) is decoded by warp 0 of its resolve CTA alone, in
+// one pass straight into the output (no scratch needed).
 //
 // There are no inter-warp flags and no waits other than barriers and the
 // completion of the CTA's own asynchronous copies.  Errors (bad offsets,
 // lengths past the block, a block ending short of out_size, an index that
-// does not match the block) set the chunk's status word; the kernel never
-// traps.  Output past out_size is clipped (the targetOutputSize = out_size
+// does not match the block) set the chunk's status word; the kernels never
+// trap.  Output past out_size is clipped (the targetOutputSize = out_size
 // behaviour of LZ4_decompress_safe_partial).
 #include "common.cuh"
 
@@ -65,14 +68,15 @@ static_assert(kRegion == ZMOE_MAP_ENTRIES, "one map entry per byte of a region")
 static_assert(kRegion <= kRing, "a region's sources stay inside the window");
 static_assert(kStep % kSlice == 0 && kRegion % kStep == 0, "slices nest in steps nest in regions");
 static_assert(kPerThread == 8, "two 128-bit map loads per thread and step");
-static_assert(kMapBufs * kStep * 4 <= kStage, "map buffers fit the staging area");
 
-struct Smem {
+struct MapSmem {                                    // map_kernel
+  uint8_t stage[kStage];                            // compressed bytes of the region
+  int32_t err;
+};
+
+struct Smem {                                       // resolve_kernel
   uint8_t ring[kRing];
-  union {
-    uint8_t stage[kStage];                          // phase 2: compressed bytes of the region
-    uint32_t mbuf[kMapBufs][kStep];                 // phase 3: map entries of the next steps
-  } u;
+  uint32_t mbuf[kMapBufs][kStep];                   // map entries of the next steps
   int32_t err;
 };
 
@@ -88,7 +92,8 @@ struct Chunk {
   __device__ __forceinline__ uint32_t ri(uint32_t pos) const { return (pos + rofs) & kRingMask; }
 };
 
-__device__ __forceinline__ void set_err(Smem& S, int32_t code) { atomicCAS(&S.err, 0, code); }
+template <class SM>
+__device__ __forceinline__ void set_err(SM& S, int32_t code) { atomicCAS(&S.err, 0, code); }
 
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
@@ -171,8 +176,8 @@ __device__ __forceinline__ StageRange stage_range(const Chunk& c, uint32_t r) {
   return st;
 }
 
-__device__ __forceinline__ void stage_issue(Smem& S, const Chunk& c, const StageRange& st) {
-  for (uint32_t q = 16 * threadIdx.x; q < st.len; q += 16 * kThreads) cp_async16(S.u.stage + q, c.src + st.lo + q);
+__device__ __forceinline__ void stage_issue(uint8_t* stage, const Chunk& c, const StageRange& st) {
+  for (uint32_t q = 16 * threadIdx.x; q < st.len; q += 16 * kThreads) cp_async16(stage + q, c.src + st.lo + q);
   cp_async_commit();
 }
 
@@ -238,14 +243,13 @@ struct Staged {
 // bytes, the literal byte read for every position and selected (the result is
 // void if miss is set); otherwise checked reads that fall back to global memory.
 template <bool kStaged>
-__device__ int map_slice_walk(Smem& S, const Chunk& c, const StageRange& st, uint32_t g, bool& miss) {
+__device__ int map_slice_walk(const uint8_t* stage, const Chunk& c, const StageRange& st, uint32_t g, bool& miss) {
   const uint32_t b0 = g * kSlice;
   const uint2 ix = __ldg(reinterpret_cast<const uint2*>(c.index) + g);
   const uint32_t so = ix.y;                            // output start of the sequence at ix.x
   if (so > b0) return ZMOE_CHUNK_BAD_DESC;
   const uint32_t b1 = min(b0 + kSlice, c.out_size);
   const uint32_t step0 = b0 & ~(kStep - 1);            // a slice lies inside one step
-  const uint8_t* stage = S.u.stage;
   const Staged sv{stage, st.lo, st.len};
   auto checked = [&](uint32_t q) -> uint32_t {
     const uint32_t d = q - st.lo;
@@ -293,15 +297,15 @@ __device__ int map_slice_walk(Smem& S, const Chunk& c, const StageRange& st, uin
   return 0;
 }
 
-__device__ int map_slice(Smem& S, const Chunk& c, const StageRange& st, uint32_t g) {
+__device__ int map_slice(const uint8_t* stage, const Chunk& c, const StageRange& st, uint32_t g) {
   if (g * kSlice >= c.out_size) return 0;
   if (g >= c.n_index) return ZMOE_CHUNK_BAD_DESC;
   bool miss = st.len == 0;
   if (!miss) {
-    const int err = map_slice_walk<true>(S, c, st, g, miss);
+    const int err = map_slice_walk<true>(stage, c, st, g, miss);
     if (!miss) return err;
   }
-  return map_slice_walk<false>(S, c, st, g, miss);   // some byte was not staged: checked reads
+  return map_slice_walk<false>(stage, c, st, g, miss);   // some byte was not staged: checked reads
 }
 
 // ---------------------------------------------------------------------------
@@ -309,7 +313,7 @@ __device__ int map_slice(Smem& S, const Chunk& c, const StageRange& st, uint32_t
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void fetch_step(Smem& S, const Chunk& c, uint32_t s0, uint32_t buf) {
   const uint32_t* src = c.map + (s0 & (kRegion - 1));
-  uint32_t* dst = S.u.mbuf[buf];
+  uint32_t* dst = S.mbuf[buf];
   for (uint32_t q = threadIdx.x; q < kStep / 4; q += kThreads) cp_async16(dst + 4 * q, src + 4 * q);
 }
 
@@ -329,7 +333,7 @@ __device__ int resolve_region(Smem& S, const Chunk& c, uint32_t R0, uint32_t R1)
     cp_async_commit();
     cp_async_wait<kAhead>();
     __syncthreads();                                   // A: step entries landed; earlier writes visible
-    const uint32_t* mb = S.u.mbuf[t % kMapBufs];
+    const uint32_t* mb = S.mbuf[t % kMapBufs];
     const uint32_t j0 = kPerThread * threadIdx.x;
     const uint4 m0 = *reinterpret_cast<const uint4*>(mb + j0);
     const uint4 m1 = *reinterpret_cast<const uint4*>(mb + j0 + 4);
@@ -430,32 +434,31 @@ __device__ void flush_range(Smem& S, const Chunk& c, uint32_t f0, uint32_t f1, u
   }
 }
 
-__device__ void decode_indexed(Smem& S, const Chunk& c) {
+// Status word of each region, after the map entries of the chunk's regions.
+__device__ __forceinline__ int32_t* region_status(uint32_t* map, uint32_t n_reg) {
+  return reinterpret_cast<int32_t*>(map + (size_t)n_reg * kRegion);
+}
+
+__device__ void resolve_chunk(Smem& S, const Chunk& c) {
   const uintptr_t sa = reinterpret_cast<uintptr_t>(c.sm), da = reinterpret_cast<uintptr_t>(c.dst);
   const uint32_t head = (uint32_t)((16 - (sa & 15)) & 15);
   const bool vec = ((da + 2 * (uintptr_t)head) & 15) == 0;
-  const bool src_aligned = (reinterpret_cast<uintptr_t>(c.src) & 15) == 0;
   const uint32_t n_reg = (c.out_size + kRegion - 1) / kRegion;
-  StageRange st = src_aligned ? stage_range(c, 0) : StageRange{0, 0};
-  stage_issue(S, c, st);
+  const int32_t* rstat = region_status(c.map, n_reg);
   for (uint32_t r = 0; r < n_reg; ++r) {
     const uint32_t R0 = r * kRegion, R1 = min(R0 + kRegion, c.out_size);
-    cp_async_wait<0>();
-    __syncthreads();                                   // staged bytes visible; previous flush done
-    int err = map_slice(S, c, st, r * kThreads + threadIdx.x);
-    if (err) set_err(S, err);
-    __threadfence_block();
-    if (__syncthreads_or(err != 0)) return;           // map written; staging area free
-    err = resolve_region(S, c, R0, R1);
+    const int32_t mapped = __ldcg(rstat + r);          // written by map_kernel; the same in every thread
+    if (mapped != 0) {
+      if (threadIdx.x == 0) set_err(S, mapped);
+      return;
+    }
+    Chunk cr = c;
+    cr.map = c.map + (size_t)r * kRegion;
+    const int err = resolve_region(S, cr, R0, R1);
     if (err) set_err(S, err);
     if (__syncthreads_or(err != 0)) return;           // region resolved; map buffers free
-    if (r + 1 < n_reg) {
-      st = src_aligned ? stage_range(c, r + 1) : StageRange{0, 0};
-      stage_issue(S, c, st);                           // overlaps the flush
-    }
     flush_range(S, c, R0, R1, head, vec);
   }
-  cp_async_wait<0>();
 }
 
 // ---------------------------------------------------------------------------
@@ -511,11 +514,17 @@ __device__ int decode_unindexed(const Chunk& c, uint32_t lane) {
   return 0;
 }
 
-__global__ void __launch_bounds__(kThreads, 2)
-decode_kernel(const zmoe_chunk* __restrict__ chunks, int n_chunks, int32_t* __restrict__ status) {
-  extern __shared__ __align__(16) uint8_t smem_raw[];
-  Smem& S = *reinterpret_cast<Smem*>(smem_raw);
-  const zmoe_chunk d = chunks[blockIdx.x];
+// Descriptor checks shared by both kernels.
+__device__ __forceinline__ bool bad_desc(const zmoe_chunk& d) {
+  bool bad = !d.src || !d.sm || !d.dst || d.src_size == 0 || d.out_size >= kInner;
+  if (d.index && d.n_index > 0 &&
+      (!d.map || (reinterpret_cast<uintptr_t>(d.map) & 15) || (reinterpret_cast<uintptr_t>(d.index) & 7) ||
+       d.seg_bytes != kSlice))
+    bad = true;
+  return bad;
+}
+
+__device__ __forceinline__ Chunk chunk_of(const zmoe_chunk& d) {
   Chunk c;
   c.src = d.src;
   c.sm = d.sm;
@@ -525,14 +534,49 @@ decode_kernel(const zmoe_chunk* __restrict__ chunks, int n_chunks, int32_t* __re
   c.src_size = d.src_size;
   c.out_size = d.out_size;
   c.n_index = d.n_index;
-  {
-    const uint32_t head = (uint32_t)((16 - (reinterpret_cast<uintptr_t>(d.sm) & 15)) & 15);
-    c.rofs = (16 - head) & 15;
+  const uint32_t head = (uint32_t)((16 - (reinterpret_cast<uintptr_t>(d.sm) & 15)) & 15);
+  c.rofs = (16 - head) & 15;
+  return c;
+}
+
+// Map (phases 1-2) of the regions r = blockIdx.x, r + gridDim.x, ... of chunk
+// blockIdx.y.  Every region's status word is written (0 or the first error),
+// so the scratch needs no clearing between launches.
+__global__ void __launch_bounds__(kThreads, 2)
+map_kernel(const zmoe_chunk* __restrict__ chunks) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  MapSmem& M = *reinterpret_cast<MapSmem*>(smem_raw);
+  const zmoe_chunk d = chunks[blockIdx.y];
+  if (bad_desc(d) || !d.index || d.n_index == 0 || d.out_size == 0) return;   // resolve_kernel reports it
+  const Chunk c = chunk_of(d);
+  const uint32_t n_reg = (c.out_size + kRegion - 1) / kRegion;
+  int32_t* rstat = region_status(d.map, n_reg);
+  const bool src_aligned = (reinterpret_cast<uintptr_t>(c.src) & 15) == 0;
+  for (uint32_t r = blockIdx.x; r < n_reg; r += gridDim.x) {
+    const StageRange st = src_aligned ? stage_range(c, r) : StageRange{0, 0};
+    if (threadIdx.x == 0) M.err = 0;
+    stage_issue(M.stage, c, st);
+    cp_async_wait<0>();
+    __syncthreads();                                   // staged bytes and the cleared error visible
+    Chunk cr = c;
+    cr.map = d.map + (size_t)r * kRegion;
+    const int err = map_slice(M.stage, cr, st, r * kThreads + threadIdx.x);
+    if (err) set_err(M, err);
+    __syncthreads();
+    if (threadIdx.x == 0) rstat[r] = M.err;
+    __syncthreads();                                   // before the stage and the error word are reused
   }
-  bool bad = !c.src || !c.sm || !c.dst || c.src_size == 0 || c.out_size >= kInner;
-  if (c.index && (!c.map || (reinterpret_cast<uintptr_t>(c.map) & 15) ||
-                  (reinterpret_cast<uintptr_t>(c.index) & 7) || d.seg_bytes != kSlice))
-    bad = true;
+}
+
+// Resolve and flush (phases 3-4) of chunk blockIdx.x after map_kernel, or the
+// whole decode of a chunk without an index.
+__global__ void __launch_bounds__(kThreads, 2)
+resolve_kernel(const zmoe_chunk* __restrict__ chunks, int32_t* __restrict__ status) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  Smem& S = *reinterpret_cast<Smem*>(smem_raw);
+  const zmoe_chunk d = chunks[blockIdx.x];
+  const bool bad = bad_desc(d);
+  const Chunk c = chunk_of(d);
   if (threadIdx.x == 0) S.err = bad ? ZMOE_CHUNK_BAD_DESC : 0;
   __syncthreads();
   if (!bad && c.out_size > 0) {
@@ -542,7 +586,7 @@ decode_kernel(const zmoe_chunk* __restrict__ chunks, int n_chunks, int32_t* __re
         if (e && threadIdx.x == 0) set_err(S, e);
       }
     } else {
-      decode_indexed(S, c);
+      resolve_chunk(S, c);
     }
   }
   __syncthreads();
@@ -553,10 +597,21 @@ decode_kernel(const zmoe_chunk* __restrict__ chunks, int n_chunks, int32_t* __re
 
 zmoe_status launch_decode_chunks(const zmoe_chunk* chunks, int n_chunks, int32_t* status, cudaStream_t stream) {
   if (n_chunks <= 0) return ZMOE_OK;
-  const int smem = (int)sizeof(Smem);
-  ZMOE_CUDA_RET(cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-  decode_kernel<<<n_chunks, kThreads, smem, stream>>>(chunks, n_chunks, status);
-  return launch_status("decode_kernel");
+  ZMOE_CHECK_ARG(n_chunks <= 65535, "decode_chunks: %d chunks in one launch (at most 65535)", n_chunks);
+  constexpr int kMapColumns = 16;                     // map CTAs per chunk (each loops over regions)
+  const int msmem = (int)sizeof(MapSmem), rsmem = (int)sizeof(Smem);
+  ZMOE_CUDA_RET(cudaFuncSetAttribute(map_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, msmem));
+  ZMOE_CUDA_RET(cudaFuncSetAttribute(resolve_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, rsmem));
+  map_kernel<<<dim3(kMapColumns, n_chunks), kThreads, msmem, stream>>>(chunks);
+  zmoe_status st = launch_status("map_kernel");
+  if (st != ZMOE_OK) return st;
+  resolve_kernel<<<n_chunks, kThreads, rsmem, stream>>>(chunks, status);
+  return launch_status("resolve_kernel");
 }
 
 }  // namespace zmoe
+
+extern "C" uint64_t zmoe_decode_scratch_bytes(uint32_t out_size) {
+  const uint64_t n_reg = ((uint64_t)out_size + zmoe::kRegion - 1) / zmoe::kRegion;
+  return n_reg * zmoe::kRegion * 4 + (n_reg * 4 + 15) / 16 * 16;
+}

@@ -105,8 +105,8 @@ struct Layer {
   int32_t* status_host = nullptr;
   int max_desc = 0, max_waves = 0;
   int desc_cursor = 0;             // descriptors used by the current forward
-  uint32_t* map_scratch = nullptr; // decoder source-map scratch, ZMOE_MAP_ENTRIES per chunk
-  int map_cap = 0;                 // chunks the scratch can hold
+  uint32_t* map_scratch = nullptr; // decoder source-map scratch (zmoe_decode_scratch_bytes per chunk)
+  uint64_t map_cap = 0;            // bytes of map_scratch
   int pending_status = 0;          // descriptors whose status is still to be checked
   // host-side pass-through buffers for forward_host
   uint16_t* x_stage = nullptr;
@@ -309,17 +309,23 @@ zmoe_status Layer::decode_into(const std::vector<std::pair<int, int>>& jobs, cud
     stats.decoded_experts++;
   }
   const int cnt = nd - base;
-  if (cnt > map_cap) {
+  uint64_t need = 0;
+  for (int i = 0; i < cnt; ++i) need += zmoe_decode_scratch_bytes(desc_host[base + i].out_size);
+  if (need > map_cap) {
     // grows to the largest decode seen (a synchronising allocation, only
     // before the working set is known)
     ZMOE_CUDA_RET(cudaStreamSynchronize(s));
     cudaFree(map_scratch);
     map_scratch = nullptr;
     map_cap = 0;
-    ZMOE_CUDA_RET(cudaMalloc(&map_scratch, (size_t)cnt * ZMOE_MAP_ENTRIES * sizeof(uint32_t)));
-    map_cap = cnt;
+    ZMOE_CUDA_RET(cudaMalloc(&map_scratch, need));
+    map_cap = need;
   }
-  for (int i = 0; i < cnt; ++i) desc_host[base + i].map = map_scratch + (size_t)i * ZMOE_MAP_ENTRIES;
+  uint64_t moff = 0;
+  for (int i = 0; i < cnt; ++i) {
+    desc_host[base + i].map = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(map_scratch) + moff);
+    moff += zmoe_decode_scratch_bytes(desc_host[base + i].out_size);
+  }
   if (cnt == 0) return ZMOE_OK;
   (void)wave;
   // Descriptors and status words of every wave of one forward live side by
@@ -342,7 +348,7 @@ zmoe_status Layer::decode_into(const std::vector<std::pair<int, int>>& jobs, cud
     ZMOE_CUDA_RET(cudaEventRecord(ev_pool[ev + 1], s));
     ev_pending.push_back({ev, 0, bytes});
   }
-  stats.launches++;
+  stats.launches += 2;                        // map_kernel + resolve_kernel
   stats.decode_launches++;
   stats.decoded_chunks += cnt;
   ZMOE_CUDA_RET(cudaMemcpyAsync(status_host + base, status_dev + base, sizeof(int32_t) * cnt,

@@ -337,7 +337,10 @@ torch::Tensor decode_tensor(const Store& s, const Meta& m) {
   auto db = hb.to(dev);
   auto dsm = torch::from_blob(p.sm.data(), {(int64_t)p.sm.size()}, u8).to(dev);
   auto di = hi.to(dev);
-  auto map = torch::empty({(int64_t)n * ZMOE_MAP_ENTRIES}, i32.device(dev));
+  std::vector<uint64_t> moff(n);
+  uint64_t mbytes = 0;
+  for (int c = 0; c < n; ++c) { moff[c] = mbytes; mbytes += zmoe_decode_scratch_bytes(p.original_sizes[c]); }
+  auto map = torch::empty({(int64_t)(mbytes / 4)}, i32.device(dev));
   auto out = torch::empty({(int64_t)m.num_elements}, torch::TensorOptions().dtype(torch::kBFloat16).device(dev));
   std::vector<zmoe_chunk> d(n);
   uint64_t e0 = 0;
@@ -346,7 +349,7 @@ torch::Tensor decode_tensor(const Store& s, const Meta& m) {
     d[c].sm = dsm.data_ptr<uint8_t>() + e0;
     d[c].dst = reinterpret_cast<uint16_t*>(out.data_ptr()) + e0;
     d[c].index = reinterpret_cast<const uint32_t*>(di.data_ptr<int32_t>() + ioff[c]);
-    d[c].map = reinterpret_cast<uint32_t*>(map.data_ptr<int32_t>()) + (size_t)c * ZMOE_MAP_ENTRIES;
+    d[c].map = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(map.data_ptr<int32_t>()) + moff[c]);
     d[c].src_size = p.block_sizes[c];
     d[c].out_size = p.original_sizes[c];
     d[c].n_index = (uint32_t)(idx[c].size() / 2);

@@ -24,7 +24,7 @@ class ZmoeChunk(ctypes.Structure):
 
 
 SLICE_BYTES = 256        # ZMOE_SLICE_BYTES
-MAP_ENTRIES = 65536      # ZMOE_MAP_ENTRIES
+MAP_ENTRIES = 65536      # ZMOE_MAP_ENTRIES (per 64 KiB region)
 
 
 class RouterArgs(ctypes.Structure):
@@ -74,6 +74,7 @@ SIGNATURES = {
     "zmoe_last_error": (ctypes.c_char_p, []),
     "zmoe_tensor_recover": (c_int, [c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
     "zmoe_decode_chunks": (c_int, [c_void_p, c_int, c_void_p, c_void_p]),
+    "zmoe_decode_scratch_bytes": (ctypes.c_uint64, [c_u32]),
     "zmoe_router": (c_int, [ctypes.POINTER(RouterArgs), c_void_p]),
     "zmoe_permute": (c_int, [ctypes.POINTER(PermuteArgs), c_void_p]),
     "zmoe_expert_ffn": (c_int, [ctypes.POINTER(FfnArgs), c_void_p]),

@@ -49,19 +49,30 @@ def tensor_recover(exp: torch.Tensor, sm: torch.Tensor, out: Optional[torch.Tens
 SEG_BYTES = _lib.SLICE_BYTES
 
 
-def map_scratch(n_chunks: int, device) -> torch.Tensor:
-    """Decoder scratch: one source-map ring (ZMOE_MAP_ENTRIES uint32) per indexed chunk."""
-    return torch.empty(max(n_chunks, 1) * _lib.MAP_ENTRIES, dtype=torch.int32, device=device)
+def scratch_bytes(out_size: int) -> int:
+    """Decoder scratch of one indexed chunk (zmoe_decode_scratch_bytes)."""
+    return int(lib.zmoe_decode_scratch_bytes(int(out_size)))
+
+
+def map_scratch(out_sizes: Sequence[int], device) -> torch.Tensor:
+    """Decoder scratch for indexed chunks of the given output sizes, in order."""
+    total = sum(scratch_bytes(o) for o in out_sizes)
+    return torch.empty(max(total, 16) // 4, dtype=torch.int32, device=device)
 
 
 def chunk_table(descs: Sequence[tuple], device, scratch: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Pack (src, sm, dst, src_size, out_size[, index, n_index, seg_bytes]) tuples
-    into a device descriptor array; indexed chunks get consecutive scratch areas."""
+    into a device descriptor array; indexed chunks get consecutive scratch areas
+    (map_scratch of the indexed chunks' out_sizes, in the same order)."""
     arr = (ZmoeChunk * max(len(descs), 1))()
+    off = 0
     for i, d in enumerate(descs):
         src, sm, dst, csz, osz = d[:5]
         idx, nidx, seg = d[5:8] if len(d) >= 8 else (None, 0, 0)
-        mp = scratch.data_ptr() + 4 * i * _lib.MAP_ENTRIES if (idx and scratch is not None) else None
+        mp = None
+        if idx and scratch is not None:
+            mp = scratch.data_ptr() + off
+            off += scratch_bytes(osz)
         arr[i] = ZmoeChunk(src, sm, dst, idx, mp, csz, osz, nidx, seg)
     size = ctypes.sizeof(ZmoeChunk)
     raw = torch.frombuffer(bytearray(bytes(arr)), dtype=torch.uint8)[: size * len(descs)]
@@ -133,7 +144,7 @@ class CompressedTensor:
         if dst is None:
             dst = torch.empty(self.numel, dtype=torch.bfloat16, device=self.blocks.device)
         d = self.descs(dst)
-        scratch = map_scratch(len(d), dst.device) if self.indexes is not None else None
+        scratch = map_scratch([x[4] for x in d], dst.device) if self.indexes is not None else None
         table = chunk_table(d, dst.device, scratch)
         st = decode_chunks(table, len(d))
         self._scratch = scratch                      # alive until the caller synchronises
