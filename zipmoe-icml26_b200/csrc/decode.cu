@@ -23,8 +23,8 @@
 //     a source inside the byte's own step is marked for a chase.  Each region
 //     also gets a status word.
 //
-//  resolve_kernel, one CTA of 256 threads per chunk, region by region:
-//  3. Resolve: step by step (2 KiB, 8 bytes per thread), the entries are
+//  resolve_kernel, one CTA of 512 threads per chunk, region by region:
+//  3. Resolve: step by step (2 KiB, 4 bytes per thread), the entries are
 //     copied into shared memory (cp.async, three steps ahead) and every byte is
 //     gathered from a 64 KiB shared-memory window of decoded exponents; marked
 //     entries first follow the step's own entries back to a literal or to a
@@ -52,7 +52,8 @@ constexpr int kThreads = 256;
 constexpr uint32_t kSlice = 256;                    // output bytes parsed by one thread
 constexpr uint32_t kRegion = kThreads * kSlice;     // output bytes per region (64 KiB)
 constexpr uint32_t kStep = 2048;                    // output bytes resolved per step
-constexpr uint32_t kPerThread = kStep / kThreads;   // bytes resolved per thread and step
+constexpr int kRThreads = 512;                      // threads of a resolve CTA
+constexpr uint32_t kPerThread = kStep / kRThreads;  // bytes resolved per thread and step
 constexpr uint32_t kRing = 65536;                   // decoded-exponent window
 constexpr uint32_t kRingMask = kRing - 1;
 constexpr uint32_t kStage = 48 * 1024;              // staged compressed bytes per region
@@ -67,7 +68,7 @@ static_assert(kSlice == ZMOE_SLICE_BYTES, "slice index granularity");
 static_assert(kRegion == ZMOE_MAP_ENTRIES, "one map entry per byte of a region");
 static_assert(kRegion <= kRing, "a region's sources stay inside the window");
 static_assert(kStep % kSlice == 0 && kRegion % kStep == 0, "slices nest in steps nest in regions");
-static_assert(kPerThread == 8, "two 128-bit map loads per thread and step");
+static_assert(kPerThread == 4, "one 128-bit map load per thread and step");
 
 struct MapSmem {                                    // map_kernel
   uint8_t stage[kStage];                            // compressed bytes of the region
@@ -314,7 +315,7 @@ __device__ int map_slice(const uint8_t* stage, const Chunk& c, const StageRange&
 __device__ __forceinline__ void fetch_step(Smem& S, const Chunk& c, uint32_t s0, uint32_t buf) {
   const uint32_t* src = c.map + (s0 & (kRegion - 1));
   uint32_t* dst = S.mbuf[buf];
-  for (uint32_t q = threadIdx.x; q < kStep / 4; q += kThreads) cp_async16(dst + 4 * q, src + 4 * q);
+  for (uint32_t q = threadIdx.x; q < kStep / 4; q += kRThreads) cp_async16(dst + 4 * q, src + 4 * q);
 }
 
 __device__ int resolve_region(Smem& S, const Chunk& c, uint32_t R0, uint32_t R1) {
@@ -335,13 +336,12 @@ __device__ int resolve_region(Smem& S, const Chunk& c, uint32_t R0, uint32_t R1)
     __syncthreads();                                   // A: step entries landed; earlier writes visible
     const uint32_t* mb = S.mbuf[t % kMapBufs];
     const uint32_t j0 = kPerThread * threadIdx.x;
-    const uint4 m0 = *reinterpret_cast<const uint4*>(mb + j0);
-    const uint4 m1 = *reinterpret_cast<const uint4*>(mb + j0 + 4);
-    uint32_t x[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
+    const uint4 m = *reinterpret_cast<const uint4*>(mb + j0);
+    uint32_t x[4] = {m.x, m.y, m.z, m.w};
     const uint32_t e = s0 + j0;
     uint32_t pending = 0;                              // entries whose source lies inside the step
 #pragma unroll
-    for (uint32_t b = 0; b < 8; ++b) {
+    for (uint32_t b = 0; b < 4; ++b) {
       if (e + b >= R1) x[b] = kLit;                    // past the chunk end: entry never written
       pending |= (x[b] & kInner) ? (1u << b) : 0u;
     }
@@ -353,7 +353,7 @@ __device__ int resolve_region(Smem& S, const Chunk& c, uint32_t R0, uint32_t R1)
         break;
       }
 #pragma unroll
-      for (uint32_t b = 0; b < 8; ++b) {
+      for (uint32_t b = 0; b < 4; ++b) {
         if (pending & (1u << b)) {
           const uint32_t j = (x[b] & kPosMask) - s0;
           x[b] = j < kStep ? mb[j] : kLit;
@@ -362,17 +362,17 @@ __device__ int resolve_region(Smem& S, const Chunk& c, uint32_t R0, uint32_t R1)
         }
       }
     }
-    uint32_t lo = 0, hi = 0;
+    uint32_t word = 0;
 #pragma unroll
-    for (uint32_t b = 0; b < 8; ++b) {
+    for (uint32_t b = 0; b < 4; ++b) {
       const uint32_t xb = (x[b] & kInner) ? kLit : x[b];
       const uint32_t val = (xb & kLit) ? (xb & 0xFFu) : (uint32_t)S.ring[c.ri(xb)];
-      if (b < 4) lo |= val << (8 * b); else hi |= val << (8 * (b - 4));
+      word |= val << (8 * b);
     }
     __syncthreads();                                   // B: the whole step is gathered
 #pragma unroll
-    for (uint32_t b = 0; b < 8; ++b)
-      if (e + b < R1) S.ring[c.ri(e + b)] = (uint8_t)((b < 4 ? lo : hi) >> (8 * (b & 3)));
+    for (uint32_t b = 0; b < 4; ++b)
+      if (e + b < R1) S.ring[c.ri(e + b)] = (uint8_t)(word >> (8 * b));
   }
   cp_async_wait<0>();
   return err;
@@ -391,7 +391,7 @@ __device__ __forceinline__ uint32_t pack2(uint32_t e4, uint32_t s4, uint32_t sel
 // 16-byte aligned in the sign+mantissa plane, the output and the ring.
 __device__ void flush_range(Smem& S, const Chunk& c, uint32_t f0, uint32_t f1, uint32_t head, bool vec) {
   if (!vec) {
-    for (uint32_t i = f0 + threadIdx.x; i < f1; i += kThreads)
+    for (uint32_t i = f0 + threadIdx.x; i < f1; i += kRThreads)
       c.dst[i] = (uint16_t)recombine(__ldg(c.sm + i), S.ring[c.ri(i)]);
     return;
   }
@@ -399,26 +399,26 @@ __device__ void flush_range(Smem& S, const Chunk& c, uint32_t f0, uint32_t f1, u
   const uint32_t v0 = f0 <= head ? head : head + ((f0 - head + 15) & ~15u);
   const uint32_t v1 = f1 <= head ? head : head + ((f1 - head) & ~15u);
   if (v0 >= v1) {
-    for (uint32_t i = f0 + threadIdx.x; i < f1; i += kThreads)
+    for (uint32_t i = f0 + threadIdx.x; i < f1; i += kRThreads)
       c.dst[i] = (uint16_t)recombine(__ldg(c.sm + i), S.ring[c.ri(i)]);
     return;
   }
-  for (uint32_t i = f0 + threadIdx.x; i < v0; i += kThreads)
+  for (uint32_t i = f0 + threadIdx.x; i < v0; i += kRThreads)
     c.dst[i] = (uint16_t)recombine(__ldg(c.sm + i), S.ring[c.ri(i)]);
-  for (uint32_t i = v1 + threadIdx.x; i < f1; i += kThreads)
+  for (uint32_t i = v1 + threadIdx.x; i < f1; i += kRThreads)
     c.dst[i] = (uint16_t)recombine(__ldg(c.sm + i), S.ring[c.ri(i)]);
   const uint32_t units = (v1 - v0) / 16;
   constexpr int kUnroll = 4;                           // sign+mantissa loads in flight per thread
-  for (uint32_t u0 = 0; u0 < units; u0 += kThreads * kUnroll) {
+  for (uint32_t u0 = 0; u0 < units; u0 += kRThreads * kUnroll) {
     uint4 sv[kUnroll];
 #pragma unroll
     for (int q = 0; q < kUnroll; ++q) {
-      const uint32_t u = u0 + threadIdx.x + kThreads * q;
+      const uint32_t u = u0 + threadIdx.x + kRThreads * q;
       if (u < units) sv[q] = __ldcs(reinterpret_cast<const uint4*>(c.sm + v0 + 16 * u));
     }
 #pragma unroll
     for (int q = 0; q < kUnroll; ++q) {
-      const uint32_t u = u0 + threadIdx.x + kThreads * q;
+      const uint32_t u = u0 + threadIdx.x + kRThreads * q;
       if (u >= units) break;
       const uint32_t i = v0 + 16 * u;
       const uint4 ev = *reinterpret_cast<const uint4*>(&S.ring[c.ri(i)]);
@@ -570,7 +570,7 @@ map_kernel(const zmoe_chunk* __restrict__ chunks) {
 
 // Resolve and flush (phases 3-4) of chunk blockIdx.x after map_kernel, or the
 // whole decode of a chunk without an index.
-__global__ void __launch_bounds__(kThreads, 2)
+__global__ void __launch_bounds__(kRThreads, 2)
 resolve_kernel(const zmoe_chunk* __restrict__ chunks, int32_t* __restrict__ status) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   Smem& S = *reinterpret_cast<Smem*>(smem_raw);
@@ -605,7 +605,7 @@ zmoe_status launch_decode_chunks(const zmoe_chunk* chunks, int n_chunks, int32_t
   map_kernel<<<dim3(kMapColumns, n_chunks), kThreads, msmem, stream>>>(chunks);
   zmoe_status st = launch_status("map_kernel");
   if (st != ZMOE_OK) return st;
-  resolve_kernel<<<n_chunks, kThreads, rsmem, stream>>>(chunks, status);
+  resolve_kernel<<<n_chunks, kRThreads, rsmem, stream>>>(chunks, status);
   return launch_status("resolve_kernel");
 }
 
