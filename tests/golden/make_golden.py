@@ -246,8 +246,36 @@ def deepseek_block(ref, tokens=24):
     print("deepseek block:", tuple(y.shape))
 
 
+def predictor_cases(ref):
+    """Replays seeded Zipf-skewed activations through the reference's own
+    ExpertPredictor (experts/expert_predictor.py) and records its predictions."""
+    import json
+    spec = importlib.util.spec_from_file_location("ref_expert_predictor",
+                                                  os.path.join(ref, "experts", "expert_predictor.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    rng = np.random.default_rng(31)
+    cases = []
+    for layers, E, k, topk, window in ((3, 16, 4, 4, 30), (26, 64, 6, 8, 26 * 6 * 10), (2, 8, 2, 20, 7)):
+        pred = mod.ExpertPredictor(layers, topk, window_size=window)
+        p = 1.0 / np.arange(1, E + 1) ** 1.2
+        p /= p.sum()
+        steps = []
+        for step in range(120):
+            layer = step % layers
+            ids = [int(e) for e in rng.choice(E, size=k, replace=False, p=p)]
+            pred.update(layer, ids)
+            nl, got = pred.predict_next_layer(layer)
+            steps.append({"layer": layer, "experts": ids, "next": nl, "predicted": [int(e) for e in got]})
+        cases.append({"layers": layers, "topk": topk, "window": window, "steps": steps})
+    with open(os.path.join(HERE, "predictor_cases.json"), "w") as f:
+        json.dump(cases, f)
+    print("predictor cases:", sum(len(c["steps"]) for c in cases))
+
+
 if __name__ == "__main__":
     ref = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
     codec_cases()
     qwen_block(ref)
     deepseek_block(ref)
+    predictor_cases(ref)
