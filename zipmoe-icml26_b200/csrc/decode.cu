@@ -190,6 +190,7 @@ __device__ __forceinline__ void stage_issue(uint8_t* stage, const Chunk& c, cons
 struct Run {
   uint32_t ms, me, o, wrap, lit_base, next;
   bool last;
+  bool periodic;                                      // the match is longer than its offset
 };
 
 template <class ByteAt>
@@ -206,6 +207,7 @@ __device__ __forceinline__ int open_run(ByteAt byte_at, uint32_t size, uint32_t 
   r.lit_base = s.lit - so;
   r.next = s.next;
   r.last = s.last;
+  r.periodic = s.ml > r.o;
   return 0;
 }
 
@@ -216,9 +218,10 @@ __device__ __forceinline__ int open_run(ByteAt byte_at, uint32_t size, uint32_t 
 // below the step when the run began before it, else the run's first copy.
 // Either way a source at or after step0 lies inside the step and is marked
 // for the resolve's chase.
-__device__ __forceinline__ uint32_t match_entry(uint32_t p, uint32_t ms, uint32_t o, uint32_t wrap, uint32_t step0) {
+__device__ __forceinline__ uint32_t match_entry(uint32_t p, uint32_t ms, uint32_t o, uint32_t wrap, bool periodic,
+                                                uint32_t step0) {
   uint32_t v = p - o;
-  if (p - ms >= o && o != 0) v = wrap - o + (p - wrap) % o;
+  if (periodic && p - ms >= o) v = wrap - o + (p - wrap) % o;
   return v >= step0 ? (v | kInner) : v;
 }
 
@@ -265,16 +268,17 @@ __device__ int map_slice_walk(const uint8_t* stage, const Chunk& c, const StageR
     const bool in_a = p < a.me;
     const uint32_t ms = in_a ? a.ms : b.ms, o = in_a ? a.o : b.o;
     const uint32_t wrap = in_a ? a.wrap : b.wrap, lit_base = in_a ? a.lit_base : b.lit_base;
+    const bool periodic = in_a ? a.periodic : b.periodic;
     if constexpr (kStaged) {
       const bool lit = p < ms;
       const uint32_t d = lit_base + p - sv.lo;
       miss |= lit && d >= sv.len;
       const uint32_t lb = sv.p[min(d, sv.len - 1)];
-      const uint32_t xm = match_entry(p, ms, o, wrap, step0);
+      const uint32_t xm = match_entry(p, ms, o, wrap, periodic, step0);
       return lit ? (kLit | lb) : xm;
     } else {
       if (p < ms) return kLit | checked(lit_base + p);
-      return match_entry(p, ms, o, wrap, step0);
+      return match_entry(p, ms, o, wrap, periodic, step0);
     }
   };
   Run cur;
@@ -282,8 +286,8 @@ __device__ int map_slice_walk(const uint8_t* stage, const Chunk& c, const StageR
   if (err) return err;
   if (cur.me <= b0) return ZMOE_CHUNK_BAD_DESC;        // the index names a sequence ending before b0
   uint4* map4 = reinterpret_cast<uint4*>(c.map);
+  Run nxt = cur;                                       // read only for bytes at or past cur.me
   for (uint32_t p0 = b0; p0 < b1; p0 += 4) {
-    Run nxt = cur;
     const bool turn = cur.me <= p0 + 4 && cur.me < b1;
     if (turn) {
       if (cur.last) return ZMOE_CHUNK_SHORT_OUTPUT;
