@@ -299,7 +299,8 @@ zmoe_status zmoe_layer_forward(zmoe_layer* layer, const uint16_t* x, int T, uint
  * grouped FFN into y, device [rows, H] fp32.  Router and shared-expert weights
  * are not used.  Replaces, for the experts one rank owns,
  * ExpertDispatcher::EnqueueExpert .. Wait (csrc/dispatcher/expert_dispatcher.cpp:149-217,285-515).
- * Synchronises once on the stream. */
+ * Does not wait for the stream: it waits only for this layer's own earlier
+ * copies and decodes (events). */
 zmoe_status zmoe_layer_experts(zmoe_layer* layer, const uint16_t* x_rows, const int32_t* counts_host, int rows,
                                float* y, zmoe_stream_t stream);
 /* Same with host buffers (pinned for full speed); returns after out_host is written. */

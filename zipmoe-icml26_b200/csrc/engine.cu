@@ -112,6 +112,8 @@ struct Layer {
   uint16_t* x_stage = nullptr;
   uint16_t* out_stage = nullptr;
   cudaEvent_t status_ready = nullptr;
+  cudaEvent_t offsets_ready = nullptr;   // zmoe_layer_experts: the pinned offsets were copied
+  bool offsets_pending = false;
 
   // optional per-kernel timing: events around decode and FFN launches on the
   // launch stream, folded into stats at the next synchronisation
@@ -150,6 +152,7 @@ Layer::~Layer() {
   cudaFreeHost(counts_host); cudaFreeHost(desc_host); cudaFreeHost(wtab_host); cudaFreeHost(status_host);
   cudaFree(x_stage); cudaFree(out_stage); cudaFree(map_scratch);
   if (status_ready) cudaEventDestroy(status_ready);
+  if (offsets_ready) cudaEventDestroy(offsets_ready);
   for (auto e : ev_pool) cudaEventDestroy(e);
 }
 
@@ -241,6 +244,7 @@ zmoe_status Layer::init(const zmoe_layer_config& c) {
   out_stage = dmalloc<uint16_t>((size_t)T * H, &st);
   if (st != ZMOE_OK) return st;
   ZMOE_CUDA_RET(cudaEventCreateWithFlags(&status_ready, cudaEventDisableTiming));
+  ZMOE_CUDA_RET(cudaEventCreateWithFlags(&offsets_ready, cudaEventDisableTiming));
   return ZMOE_OK;
 }
 
@@ -474,8 +478,14 @@ zmoe_status Layer::experts(const uint16_t* xrows, const int32_t* counts_h, int r
     for (int t = 0; t < tensors; ++t)
       ZMOE_CHECK_ARG(store[e][t].dev, "experts: expert %d tensor %d not loaded", e, t);
   zmoe_status st;
-  // the previous call's pinned offsets may still be in flight
-  ZMOE_CUDA_RET(cudaStreamSynchronize(s));
+  // Host buffers of the previous call: its pinned offsets copy, its decode
+  // descriptors and status (status_ready comes after both on the stream).
+  // Waiting on these events, not on the stream, lets the caller's queued work
+  // (an exchange, a gather) run on while this call plans and launches.
+  if (offsets_pending) {
+    ZMOE_CUDA_RET(cudaEventSynchronize(offsets_ready));
+    offsets_pending = false;
+  }
   if ((st = check_status()) != ZMOE_OK) return st;
   desc_cursor = 0;
   if ((st = fold_timing()) != ZMOE_OK) return st;
@@ -486,6 +496,8 @@ zmoe_status Layer::experts(const uint16_t* xrows, const int32_t* counts_h, int r
     counts_host[e] = counts_h[e];
   }
   ZMOE_CUDA_RET(cudaMemcpyAsync(offsets_ext, offsets_host, sizeof(int32_t) * (E + 1), cudaMemcpyHostToDevice, s));
+  ZMOE_CUDA_RET(cudaEventRecord(offsets_ready, s));
+  offsets_pending = true;
   if ((st = run_experts(xrows, offsets_ext, counts_host, rows, yrows, s)) != ZMOE_OK) return st;
   stats.forwards++;
   stats.tokens += rows;

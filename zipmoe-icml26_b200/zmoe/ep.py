@@ -150,6 +150,17 @@ class EPMoELayer:
         s, P, El = self.s, self.P, len(self.mine)
         H = s.hidden
         counts, row_of, tw, sg, xp = self.K.route(x)
+        # the shared expert needs only x: on a side stream it overlaps the exchange
+        side = None
+        if x.is_cuda:
+            if getattr(self, "_side", None) is None:
+                self._side = torch.cuda.Stream(device=x.device)
+            side = self._side
+            side.wait_stream(torch.cuda.current_stream(x.device))
+            with torch.cuda.stream(side):
+                y_sh = self.K.shared_expert(x)
+        else:
+            y_sh = self.K.shared_expert(x)
         # 1. counts: rows for expert e of rank r go to r
         recv_counts = torch.empty(P * El, dtype=torch.int32, device=x.device)
         self._a2a(recv_counts, counts, [El] * P, self.part.sizes())
@@ -170,8 +181,11 @@ class EPMoELayer:
         # 4. rows back, in the order they left
         y_back = torch.empty(n_send, H, dtype=y_src.dtype, device=x.device)
         self._a2a(y_back, y_src, send_rows, recv_rows)
-        # 5. shared expert + combine on the local tokens
-        y_sh = self.K.shared_expert(x)
+        # 5. combine with the shared expert on the local tokens
+        if side is not None:
+            torch.cuda.current_stream(x.device).wait_stream(side)
+            if y_sh is not None:
+                y_sh.record_stream(torch.cuda.current_stream(x.device))
         if n_send == 0:                                   # every token dropped (Switch capacity)
             y_back = torch.zeros(1, H, dtype=torch.float32, device=x.device)
         return self.K.combine(y_back, row_of, tw, sg, y_sh, x)
