@@ -324,6 +324,7 @@ __device__ __forceinline__ void fetch_step(Smem& S, const Chunk& c, uint32_t s0,
 
 __device__ int resolve_region(Smem& S, const Chunk& c, uint32_t R0, uint32_t R1) {
   const uint32_t n_steps = (R1 - R0 + kStep - 1) / kStep;
+  const uint32_t rofs = c.rofs;
   int err = 0;
   // map entries run kAhead steps ahead of the resolve (one commit group per
   // step, empty past the end, so wait_group counts stay uniform)
@@ -340,43 +341,54 @@ __device__ int resolve_region(Smem& S, const Chunk& c, uint32_t R0, uint32_t R1)
     __syncthreads();                                   // A: step entries landed; earlier writes visible
     const uint32_t* mb = S.mbuf[t % kMapBufs];
     const uint32_t j0 = kPerThread * threadIdx.x;
+    const uint32_t e = s0 + j0;
     const uint4 m = *reinterpret_cast<const uint4*>(mb + j0);
     uint32_t x[4] = {m.x, m.y, m.z, m.w};
-    const uint32_t e = s0 + j0;
-    uint32_t pending = 0;                              // entries whose source lies inside the step
+    const bool tail = s0 + kStep > R1;                 // the chunk's last step (the same in every thread)
+    if (tail) {
 #pragma unroll
-    for (uint32_t b = 0; b < 4; ++b) {
-      if (e + b >= R1) x[b] = kLit;                    // past the chunk end: entry never written
-      pending |= (x[b] & kInner) ? (1u << b) : 0u;
+      for (uint32_t b = 0; b < 4; ++b)
+        if (e + b >= R1) x[b] = kLit;                  // past the chunk end: entry never written
     }
-    // follow the step's own entries back, one hop for every pending entry per
-    // round (sources strictly precede their byte, so at most kStep rounds)
-    for (uint32_t round = 0; pending; ++round) {
-      if (round >= kStep) {
-        err = ZMOE_CHUNK_BAD_DESC;
-        break;
-      }
+    // entries whose source lies inside the step (bit 30 of each)
+    uint32_t pending = ((x[0] >> 30) & 1u) | ((x[1] >> 29) & 2u) | ((x[2] >> 28) & 4u) | ((x[3] >> 27) & 8u);
+    if (pending) {
+      // follow the step's own entries back, one hop for every pending entry per
+      // round (sources strictly precede their byte, so at most kStep rounds)
+      for (uint32_t round = 0; pending; ++round) {
+        if (round >= kStep) {
+          err = ZMOE_CHUNK_BAD_DESC;
 #pragma unroll
-      for (uint32_t b = 0; b < 4; ++b) {
-        if (pending & (1u << b)) {
-          const uint32_t j = (x[b] & kPosMask) - s0;
-          x[b] = j < kStep ? mb[j] : kLit;
-          if (j >= kStep) err = ZMOE_CHUNK_BAD_DESC;
-          if (!(x[b] & kInner)) pending &= ~(1u << b);
+          for (uint32_t b = 0; b < 4; ++b) if (pending & (1u << b)) x[b] = kLit;
+          break;
+        }
+#pragma unroll
+        for (uint32_t b = 0; b < 4; ++b) {
+          if (pending & (1u << b)) {
+            const uint32_t j = (x[b] & kPosMask) - s0;
+            x[b] = j < kStep ? mb[j] : kLit;
+            if (j >= kStep) err = ZMOE_CHUNK_BAD_DESC;
+            if (!(x[b] & kInner)) pending &= ~(1u << b);
+          }
         }
       }
     }
+    // every entry is now a literal or a position before the step
     uint32_t word = 0;
 #pragma unroll
     for (uint32_t b = 0; b < 4; ++b) {
-      const uint32_t xb = (x[b] & kInner) ? kLit : x[b];
-      const uint32_t val = (xb & kLit) ? (xb & 0xFFu) : (uint32_t)S.ring[c.ri(xb)];
+      const uint32_t val = (x[b] & kLit) ? (x[b] & 0xFFu) : (uint32_t)S.ring[(x[b] + rofs) & kRingMask];
       word |= val << (8 * b);
     }
     __syncthreads();                                   // B: the whole step is gathered
+    if (!tail) {
 #pragma unroll
-    for (uint32_t b = 0; b < 4; ++b)
-      if (e + b < R1) S.ring[c.ri(e + b)] = (uint8_t)(word >> (8 * b));
+      for (uint32_t b = 0; b < 4; ++b) S.ring[(e + b + rofs) & kRingMask] = (uint8_t)(word >> (8 * b));
+    } else {
+#pragma unroll
+      for (uint32_t b = 0; b < 4; ++b)
+        if (e + b < R1) S.ring[(e + b + rofs) & kRingMask] = (uint8_t)(word >> (8 * b));
+    }
   }
   cp_async_wait<0>();
   return err;
