@@ -313,17 +313,22 @@ __device__ int map_slice(const uint8_t* stage, const Chunk& c, const StageRange&
   return map_slice_walk<false>(stage, c, st, g, miss);   // some byte was not staged: checked reads
 }
 
+__device__ void flush_range(Smem& S, const Chunk& c, uint32_t f0, uint32_t f1, uint32_t head, bool vec);
+
 // ---------------------------------------------------------------------------
 // phase 3: resolve the region's steps through the shared-memory window
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void fetch_step(Smem& S, const Chunk& c, uint32_t s0, uint32_t buf) {
-  const uint32_t* src = c.map + (s0 & (kRegion - 1));
+  const uint32_t* src = c.map + s0;                    // the chunk's entries are contiguous by position
   uint32_t* dst = S.mbuf[buf];
   for (uint32_t q = threadIdx.x; q < kStep / 4; q += kRThreads) cp_async16(dst + 4 * q, src + 4 * q);
 }
 
-__device__ int resolve_region(Smem& S, const Chunk& c, uint32_t R0, uint32_t R1) {
-  const uint32_t n_steps = (R1 - R0 + kStep - 1) / kStep;
+// Resolves steps [0, n_steps) of the chunk; the last step of each region is
+// followed by that region's flush.
+__device__ int resolve_steps(Smem& S, const Chunk& c, uint32_t head, bool vec) {
+  const uint32_t R0 = 0, R1 = c.out_size;
+  const uint32_t n_steps = (R1 + kStep - 1) / kStep;
   const uint32_t rofs = c.rofs;
   int err = 0;
   // map entries run kAhead steps ahead of the resolve (one commit group per
@@ -335,6 +340,7 @@ __device__ int resolve_region(Smem& S, const Chunk& c, uint32_t R0, uint32_t R1)
   for (uint32_t t = 0; t < n_steps; ++t) {
     const uint32_t s0 = R0 + t * kStep;
     // buffer (t + kAhead) % kMapBufs last held step t - 1, read before its barrier B
+    // (and before the flush that follows a region's last step)
     if (t + kAhead < n_steps) fetch_step(S, c, s0 + kAhead * kStep, (t + kAhead) % kMapBufs);
     cp_async_commit();
     cp_async_wait<kAhead>();
@@ -388,6 +394,12 @@ __device__ int resolve_region(Smem& S, const Chunk& c, uint32_t R0, uint32_t R1)
 #pragma unroll
       for (uint32_t b = 0; b < 4; ++b)
         if (e + b < R1) S.ring[(e + b + rofs) & kRingMask] = (uint8_t)(word >> (8 * b));
+    }
+    const uint32_t s1 = s0 + kStep;
+    if (s1 % kRegion == 0 || s1 >= R1) {               // a region's last step: write the region out
+      if (__syncthreads_or(err != 0)) break;
+      const uint32_t F0 = (s0 / kRegion) * kRegion;
+      flush_range(S, c, F0, min(F0 + kRegion, R1), head, vec);
     }
   }
   cp_async_wait<0>();
@@ -461,20 +473,15 @@ __device__ void resolve_chunk(Smem& S, const Chunk& c) {
   const bool vec = ((da + 2 * (uintptr_t)head) & 15) == 0;
   const uint32_t n_reg = (c.out_size + kRegion - 1) / kRegion;
   const int32_t* rstat = region_status(c.map, n_reg);
-  for (uint32_t r = 0; r < n_reg; ++r) {
-    const uint32_t R0 = r * kRegion, R1 = min(R0 + kRegion, c.out_size);
-    const int32_t mapped = __ldcg(rstat + r);          // written by map_kernel; the same in every thread
+  for (uint32_t r = 0; r < n_reg; ++r) {               // map_kernel's verdicts (the same in every thread)
+    const int32_t mapped = __ldcg(rstat + r);
     if (mapped != 0) {
       if (threadIdx.x == 0) set_err(S, mapped);
       return;
     }
-    Chunk cr = c;
-    cr.map = c.map + (size_t)r * kRegion;
-    const int err = resolve_region(S, cr, R0, R1);
-    if (err) set_err(S, err);
-    if (__syncthreads_or(err != 0)) return;           // region resolved; map buffers free
-    flush_range(S, c, R0, R1, head, vec);
   }
+  const int err = resolve_steps(S, c, head, vec);
+  if (err) set_err(S, err);
 }
 
 // ---------------------------------------------------------------------------
