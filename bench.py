@@ -73,7 +73,8 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle-reason samples during the timed region."""
+    """nvidia-smi clock / throttle-reason samples during the timed region (one
+    GPU; inactive when index is None, so that only one rank polls the driver)."""
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -84,6 +85,8 @@ class ClockSampler:
         self.p = None
 
     def __enter__(self):
+        if self.index is None:
+            return self
         try:
             self.p = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
                                        "--format=csv,noheader,nounits", "-lms", "20"],
@@ -107,6 +110,9 @@ class ClockSampler:
                 self.p.kill()
 
     def summary(self):
+        if self.index is None:
+            os.unlink(self.f.name)
+            return None
         self.f.flush()
         rows = []
         with open(self.f.name) as fh:
@@ -343,7 +349,7 @@ def run_ep(args):
     eng.set_timing(True)
     barrier()
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
+    with ClockSampler(local if rank == 0 else None) as clk:
         start.record(stream)
         for _ in range(args.steps):
             L(x)
