@@ -82,10 +82,13 @@ typedef struct zmoe_chunk {
   uint32_t seg_bytes;   /* output bytes per index entry: ZMOE_SLICE_BYTES */
 } zmoe_chunk;
 
-/* chunks and status are device arrays of n_chunks entries.  One CTA decodes
- * one chunk: with an index, 4 warps map sources (one 256-byte slice per lane)
- * while one warp resolves bytes from a shared-memory window and one writes
- * BF16; without an index one warp decodes the chunk serially. */
+/* chunks and status are device arrays of n_chunks entries.  Indexed chunks
+ * are decoded by two launches on the stream: the map kernel (one thread per
+ * 256-byte slice, 16 CTAs per chunk) writes the source of every output byte
+ * into zmoe_chunk.map; the resolve kernel (one CTA per chunk) follows the
+ * sources in 2 KiB steps through a 64 KiB shared-memory ring and writes the
+ * recombined BF16.  A chunk without an index is decoded serially by one warp.
+ * status[c] is always written (ZMOE_CHUNK_OK or the first error found). */
 zmoe_status zmoe_decode_chunks(const zmoe_chunk* chunks, int n_chunks, int32_t* status,
                                zmoe_stream_t stream);
 /* Scratch bytes an indexed chunk of out_size exponent bytes needs in

@@ -11,7 +11,8 @@
 // a block depend on each other almost serially while the token stream does
 // not.  Output is handled in 64 KiB regions, by two kernels on one stream:
 //
-//  map_kernel, one CTA of 256 threads per region (of every chunk at once):
+//  map_kernel, 16 CTAs of 256 threads per chunk, each mapping every 16th
+//  region (every chunk at once), one region at a time:
 //  1. Stage: the region's compressed bytes are copied into shared memory.
 //  2. Map: a slice index built when the block is loaded (zmoe_lz4_build_index)
 //     names, for every 256 output bytes, the sequence that contains the first
@@ -19,17 +20,19 @@
 //     entry per output byte into the chunk's scratch: a literal value, or the
 //     position of an earlier byte with the same value.  For a match byte that
 //     position is the source itself, or, for a run longer than its offset,
-//     the latest equal byte before the 2 KiB step holding it when one exists;
-//     a source inside the byte's own step is marked for a chase.  Each region
-//     also gets a status word.
+//     the latest equal byte before the 2 KiB step holding it when one exists.
+//  3. Chase: once the whole region is mapped, the 4-byte groups holding an
+//     entry whose source lies inside its own step are listed, and the CTA's
+//     threads share the list: each such entry is replaced by following the
+//     step's entries back to a literal or to a byte before the step.  Each
+//     region also gets a status word.
 //
 //  resolve_kernel, one CTA of 512 threads per chunk, region by region:
-//  3. Resolve: step by step (2 KiB, 4 bytes per thread), the entries are
+//  4. Resolve: step by step (2 KiB, 4 bytes per thread), the entries are
 //     copied into shared memory (cp.async, three steps ahead) and every byte is
-//     gathered from a 64 KiB shared-memory window of decoded exponents; marked
-//     entries first follow the step's own entries back to a literal or to a
-//     byte before the step.  The whole step is gathered before it is written.
-//  4. Flush: 16 exponent bytes and 16 sign+mantissa bytes (128-bit loads)
+//     gathered from a 64 KiB shared-memory window of decoded exponents.  The
+//     whole step is gathered before it is written.
+//  5. Flush: 16 exponent bytes and 16 sign+mantissa bytes (128-bit loads)
 //     become 16 BF16 values (two 128-bit stores) per thread and group.
 //
 // Only the resolve is serial within a chunk; mapping every region at once
@@ -69,9 +72,11 @@ static_assert(kRegion == ZMOE_MAP_ENTRIES, "one map entry per byte of a region")
 static_assert(kRegion <= kRing, "a region's sources stay inside the window");
 static_assert(kStep % kSlice == 0 && kRegion % kStep == 0, "slices nest in steps nest in regions");
 static_assert(kPerThread == 4, "one 128-bit map load per thread and step");
+static_assert((kRegion / 4) * sizeof(uint16_t) <= kStage && kRegion / 4 <= 65536, "the chase list fits the stage");
 
 struct MapSmem {                                    // map_kernel
-  uint8_t stage[kStage];                            // compressed bytes of the region
+  uint8_t stage[kStage];                            // compressed bytes of the region, then the chase list
+  uint32_t wsum[kThreads / 32];
   int32_t err;
 };
 
@@ -247,7 +252,8 @@ struct Staged {
 // bytes, the literal byte read for every position and selected (the result is
 // void if miss is set); otherwise checked reads that fall back to global memory.
 template <bool kStaged>
-__device__ int map_slice_walk(const uint8_t* stage, const Chunk& c, const StageRange& st, uint32_t g, bool& miss) {
+__device__ int map_slice_walk(const uint8_t* stage, const Chunk& c, const StageRange& st, uint32_t g, bool& miss,
+                              uint64_t& inner) {
   const uint32_t b0 = g * kSlice;
   const uint2 ix = __ldg(reinterpret_cast<const uint2*>(c.index) + g);
   const uint32_t so = ix.y;                            // output start of the sequence at ix.x
@@ -297,26 +303,120 @@ __device__ int map_slice_walk(const uint8_t* stage, const Chunk& c, const StageR
     const uint4 x = make_uint4(entry(p0 + 0, cur, nxt), entry(p0 + 1, cur, nxt), entry(p0 + 2, cur, nxt),
                                entry(p0 + 3, cur, nxt));
     map4[(p0 % kRegion) / 4] = x;
+    if ((x.x | x.y | x.z | x.w) & kInner) inner |= 1ull << ((p0 - b0) / 4);
     if (turn) cur = nxt;
   }
   return 0;
 }
 
-__device__ int map_slice(const uint8_t* stage, const Chunk& c, const StageRange& st, uint32_t g) {
+// inner: bit k set when group k (bytes 4k..4k+3 of the slice) holds an entry
+// whose source lies inside its own step.
+__device__ int map_slice(const uint8_t* stage, const Chunk& c, const StageRange& st, uint32_t g, uint64_t& inner) {
+  inner = 0;
   if (g * kSlice >= c.out_size) return 0;
   if (g >= c.n_index) return ZMOE_CHUNK_BAD_DESC;
   bool miss = st.len == 0;
   if (!miss) {
-    const int err = map_slice_walk<true>(stage, c, st, g, miss);
+    const int err = map_slice_walk<true>(stage, c, st, g, miss, inner);
     if (!miss) return err;
+    inner = 0;
   }
-  return map_slice_walk<false>(stage, c, st, g, miss);   // some byte was not staged: checked reads
+  return map_slice_walk<false>(stage, c, st, g, miss, inner);   // some byte was not staged: checked reads
+}
+
+// ---------------------------------------------------------------------------
+// phase 3: chase the entries whose source lies inside their own step
+// ---------------------------------------------------------------------------
+// Once every slice of the region is mapped, each entry whose source lies
+// inside its own step is replaced by the entry of that source, followed back
+// to a literal or to a position before the step; the resolve then gathers each
+// step with no chase.  Other threads rewrite entries of the step at the same
+// time; whichever value a read sees (marked or final) names the same byte
+// value.  Positions strictly decrease along a chase, so it ends within a
+// step's length; a chase that leaves the step or does not move back is an
+// index/block mismatch.
+//
+// The groups to chase are gathered into one list for the CTA, so that a slice
+// with many of them (a long run of short copies) is shared by all threads
+// instead of holding the region's barrier for one thread.  Each thread takes
+// two groups at a time and follows their eight entries in lockstep, one hop
+// (an L2 load) per round for every entry still marked.
+constexpr uint32_t kChaseGroups = 2;
+
+__device__ int chase_groups(const Chunk& c, uint32_t rbase, const uint16_t* list, uint32_t total) {
+  uint4* map4 = reinterpret_cast<uint4*>(c.map);
+  int err = 0;
+  for (uint32_t i0 = threadIdx.x; i0 < total; i0 += kThreads * kChaseGroups) {
+    uint32_t gi[kChaseGroups], x[4 * kChaseGroups], cur[4 * kChaseGroups];
+    bool live[kChaseGroups];
+#pragma unroll
+    for (uint32_t k = 0; k < kChaseGroups; ++k) {
+      const uint32_t i = i0 + k * kThreads;
+      live[k] = i < total;
+      gi[k] = live[k] ? list[i] : 0u;
+    }
+#pragma unroll
+    for (uint32_t k = 0; k < kChaseGroups; ++k) {
+      const uint4 v = live[k] ? __ldcg(map4 + gi[k]) : make_uint4(kLit, kLit, kLit, kLit);
+      x[4 * k + 0] = v.x; x[4 * k + 1] = v.y; x[4 * k + 2] = v.z; x[4 * k + 3] = v.w;
+#pragma unroll
+      for (uint32_t b = 0; b < 4; ++b) {
+        cur[4 * k + b] = rbase + 4 * gi[k] + b;
+        if (cur[4 * k + b] >= c.out_size) x[4 * k + b] &= ~kInner;   // padding of the last group: never read
+      }
+    }
+    for (;;) {
+      bool any = false;
+#pragma unroll
+      for (uint32_t q = 0; q < 4 * kChaseGroups; ++q) {
+        if (x[q] & kInner) {
+          const uint32_t src = x[q] & kPosMask;
+          const uint32_t step0 = cur[q] & ~(kStep - 1);
+          if (src >= cur[q] || src < step0) {
+            err = ZMOE_CHUNK_BAD_DESC;
+            x[q] = kLit;
+          } else {
+            cur[q] = src;
+            x[q] = __ldcg(c.map + (src - rbase));
+            any = true;
+          }
+        }
+      }
+      if (!any) break;
+    }
+#pragma unroll
+    for (uint32_t k = 0; k < kChaseGroups; ++k)
+      if (live[k]) __stcg(map4 + gi[k], make_uint4(x[4 * k], x[4 * k + 1], x[4 * k + 2], x[4 * k + 3]));
+  }
+  return err;
+}
+
+// Exclusive prefix sum of v over the CTA; total gets the sum.  wsum: kThreads / 32 words.
+__device__ __forceinline__ uint32_t block_scan(uint32_t v, uint32_t* wsum, uint32_t& total) {
+  const uint32_t lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  uint32_t inc = v;
+#pragma unroll
+  for (uint32_t d = 1; d < 32; d <<= 1) {
+    const uint32_t y = __shfl_up_sync(kFull, inc, d);
+    if (lane >= d) inc += y;
+  }
+  if (lane == 31) wsum[w] = inc;
+  __syncthreads();
+  uint32_t before = 0;
+  total = 0;
+#pragma unroll
+  for (uint32_t k = 0; k < kThreads / 32; ++k) {
+    const uint32_t t = wsum[k];
+    before += k < w ? t : 0u;
+    total += t;
+  }
+  return before + inc - v;
 }
 
 __device__ void flush_range(Smem& S, const Chunk& c, uint32_t f0, uint32_t f1, uint32_t head, bool vec);
 
 // ---------------------------------------------------------------------------
-// phase 3: resolve the region's steps through the shared-memory window
+// phase 4: resolve the region's steps through the shared-memory window
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void fetch_step(Smem& S, const Chunk& c, uint32_t s0, uint32_t buf) {
   const uint32_t* src = c.map + s0;                    // the chunk's entries are contiguous by position
@@ -356,30 +456,12 @@ __device__ int resolve_steps(Smem& S, const Chunk& c, uint32_t head, bool vec) {
       for (uint32_t b = 0; b < 4; ++b)
         if (e + b >= R1) x[b] = kLit;                  // past the chunk end: entry never written
     }
-    // entries whose source lies inside the step (bit 30 of each)
-    uint32_t pending = ((x[0] >> 30) & 1u) | ((x[1] >> 29) & 2u) | ((x[2] >> 28) & 4u) | ((x[3] >> 27) & 8u);
-    if (pending) {
-      // follow the step's own entries back, one hop for every pending entry per
-      // round (sources strictly precede their byte, so at most kStep rounds)
-      for (uint32_t round = 0; pending; ++round) {
-        if (round >= kStep) {
-          err = ZMOE_CHUNK_BAD_DESC;
+    // map_kernel left every entry a literal or a position before the step
+    if ((x[0] | x[1] | x[2] | x[3]) & kInner) {
+      err = ZMOE_CHUNK_BAD_DESC;
 #pragma unroll
-          for (uint32_t b = 0; b < 4; ++b) if (pending & (1u << b)) x[b] = kLit;
-          break;
-        }
-#pragma unroll
-        for (uint32_t b = 0; b < 4; ++b) {
-          if (pending & (1u << b)) {
-            const uint32_t j = (x[b] & kPosMask) - s0;
-            x[b] = j < kStep ? mb[j] : kLit;
-            if (j >= kStep) err = ZMOE_CHUNK_BAD_DESC;
-            if (!(x[b] & kInner)) pending &= ~(1u << b);
-          }
-        }
-      }
+      for (uint32_t b = 0; b < 4; ++b) x[b] = kLit;
     }
-    // every entry is now a literal or a position before the step
     uint32_t word = 0;
 #pragma unroll
     for (uint32_t b = 0; b < 4; ++b) {
@@ -407,7 +489,7 @@ __device__ int resolve_steps(Smem& S, const Chunk& c, uint32_t head, bool vec) {
 }
 
 // ---------------------------------------------------------------------------
-// phase 4: BF16 out
+// phase 5: BF16 out
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t pack2(uint32_t e4, uint32_t s4, uint32_t sel) {
   const uint32_t e2 = __byte_perm(e4, 0, sel);
@@ -562,7 +644,7 @@ __device__ __forceinline__ Chunk chunk_of(const zmoe_chunk& d) {
   return c;
 }
 
-// Map (phases 1-2) of the regions r = blockIdx.x, r + gridDim.x, ... of chunk
+// Map and chase (phases 1-3) of the regions r = blockIdx.x, r + gridDim.x, ... of chunk
 // blockIdx.y.  Every region's status word is written (0 or the first error),
 // so the scratch needs no clearing between launches.
 __global__ void __launch_bounds__(kThreads, 2)
@@ -583,7 +665,21 @@ map_kernel(const zmoe_chunk* __restrict__ chunks) {
     __syncthreads();                                   // staged bytes and the cleared error visible
     Chunk cr = c;
     cr.map = d.map + (size_t)r * kRegion;
-    const int err = map_slice(M.stage, cr, st, r * kThreads + threadIdx.x);
+    const uint32_t g = r * kThreads + threadIdx.x;
+    uint64_t inner;
+    int err = map_slice(M.stage, cr, st, g, inner);
+    if (err) inner = 0;
+    // list the groups to chase (group index within the region), in the stage
+    uint32_t total;
+    uint32_t at = block_scan((uint32_t)__popcll(inner), M.wsum, total);   // its barrier: the stage is free
+    uint16_t* list = reinterpret_cast<uint16_t*>(M.stage);
+    while (inner) {
+      list[at++] = (uint16_t)(threadIdx.x * (kSlice / 4) + (uint32_t)__ffsll((long long)inner) - 1);
+      inner &= inner - 1;
+    }
+    __syncthreads();                                   // the list and every entry of the region written
+    const int cerr = chase_groups(cr, r * kRegion, list, total);
+    if (!err) err = cerr;
     if (err) set_err(M, err);
     __syncthreads();
     if (threadIdx.x == 0) rstat[r] = M.err;
@@ -591,7 +687,7 @@ map_kernel(const zmoe_chunk* __restrict__ chunks) {
   }
 }
 
-// Resolve and flush (phases 3-4) of chunk blockIdx.x after map_kernel, or the
+// Resolve and flush (phases 4-5) of chunk blockIdx.x after map_kernel, or the
 // whole decode of a chunk without an index.
 __global__ void __launch_bounds__(kRThreads, 2)
 resolve_kernel(const zmoe_chunk* __restrict__ chunks, int32_t* __restrict__ status) {
