@@ -60,6 +60,8 @@ constexpr uint32_t kPerThread = kStep / kRThreads;  // bytes resolved per thread
 constexpr uint32_t kRing = 65536;                   // decoded-exponent window
 constexpr uint32_t kRingMask = kRing - 1;
 constexpr uint32_t kStage = 48 * 1024;              // staged compressed bytes per region
+constexpr uint32_t kTGroups = 8;                    // groups per lane between transposed map stores
+constexpr uint32_t kTPitch = kTGroups + 1;          // uint4 per lane in tbuf (padded: no bank conflicts)
 constexpr uint32_t kMapBufs = 4;                    // map-entry buffers of the resolve
 constexpr uint32_t kAhead = kMapBufs - 1;           // steps whose entries are in flight
 constexpr uint32_t kLit = 0x80000000u;              // map entry: literal value in bits 0..7
@@ -72,10 +74,12 @@ static_assert(kRegion == ZMOE_MAP_ENTRIES, "one map entry per byte of a region")
 static_assert(kRegion <= kRing, "a region's sources stay inside the window");
 static_assert(kStep % kSlice == 0 && kRegion % kStep == 0, "slices nest in steps nest in regions");
 static_assert(kPerThread == 4, "one 128-bit map load per thread and step");
+static_assert(kTGroups * 4 * 4 == 128 && (kSlice / 4) % kTGroups == 0, "a lane's transposed groups fill one 128-byte line");
 static_assert((kRegion / 4) * sizeof(uint16_t) <= kStage && kRegion / 4 <= 65536, "the chase list fits the stage");
 
 struct MapSmem {                                    // map_kernel
   uint8_t stage[kStage];                            // compressed bytes of the region, then the chase list
+  uint4 tbuf[kThreads * kTPitch];                    // per warp: 32 lanes x kTPitch (map_slice_staged)
   uint32_t wsum[kThreads / 32];
   int32_t err;
 };
@@ -193,14 +197,13 @@ __device__ __forceinline__ void stage_issue(uint8_t* stage, const Chunk& c, cons
 // The sequence being mapped: output bytes [so, ms) are literals (compressed
 // byte lit_base + position), [ms, me) match bytes.
 struct Run {
-  uint32_t ms, me, o, wrap, lit_base, next;
+  uint32_t ms, me, o, lit_base, next;
   bool last;
   bool periodic;                                      // the match is longer than its offset
 };
 
 template <class ByteAt>
-__device__ __forceinline__ int open_run(ByteAt byte_at, uint32_t size, uint32_t ip, uint32_t so, uint32_t step0,
-                                        Run& r) {
+__device__ __forceinline__ int open_run(ByteAt byte_at, uint32_t size, uint32_t ip, uint32_t so, Run& r) {
   Seq s;
   const int err = read_seq(byte_at, size, ip, s);
   if (err) return err;
@@ -208,7 +211,6 @@ __device__ __forceinline__ int open_run(ByteAt byte_at, uint32_t size, uint32_t 
   r.me = r.ms + s.ml;
   r.o = s.off;
   if (s.ml > 0 && (r.o == 0 || r.o > r.ms)) return ZMOE_CHUNK_BAD_OFFSET;
-  r.wrap = max(r.ms, step0);
   r.lit_base = s.lit - so;
   r.next = s.next;
   r.last = s.last;
@@ -222,73 +224,176 @@ __device__ __forceinline__ int open_run(ByteAt byte_at, uint32_t size, uint32_t 
 // ms - o; with wrap = max(ms, step0) its source is the copy in [wrap - o, wrap):
 // below the step when the run began before it, else the run's first copy.
 // Either way a source at or after step0 lies inside the step and is marked
-// for the resolve's chase.
-__device__ __forceinline__ uint32_t match_entry(uint32_t p, uint32_t ms, uint32_t o, uint32_t wrap, bool periodic,
-                                                uint32_t step0) {
+// for the chase.
+__device__ __forceinline__ uint32_t periodic_source(uint32_t p, uint32_t ms, uint32_t o, uint32_t step0) {
+  const uint32_t wrap = max(ms, step0);
+  return wrap - o + (p - wrap) % o;
+}
+__device__ __forceinline__ uint32_t match_entry(uint32_t p, uint32_t ms, uint32_t o, bool periodic, uint32_t step0) {
   uint32_t v = p - o;
-  if (periodic && p - ms >= o) v = wrap - o + (p - wrap) % o;
+  if (periodic && p - ms >= o) v = periodic_source(p, ms, o, step0);
   return v >= step0 ? (v | kInner) : v;
 }
-
-// Staged compressed bytes, read with a clamped index: a read outside the
-// staged range returns 0 and sets miss (the slice is then mapped again with
-// checked reads).
-struct Staged {
-  const uint8_t* p;
-  uint32_t lo, len;
-  __device__ __forceinline__ uint32_t at(uint32_t q, bool& miss) const {
-    const uint32_t d = q - lo;
-    miss |= d >= len;
-    return d < len ? (uint32_t)p[d] : 0u;
-  }
-};
 
 // The slice is walked in 64 groups of 4 bytes, the same count in every lane.
 // A sequence that starts inside (or right after) a group is opened before the
 // group's entries are formed (every sequence but the last covers at least 4
 // bytes, so a group meets at most two), each byte takes its fields from the
 // sequence it belongs to, and the group is one 128-bit map store.  Lanes
-// diverge only while a header is parsed.  kStaged: every read from the staged
-// bytes, the literal byte read for every position and selected (the result is
-// void if miss is set); otherwise checked reads that fall back to global memory.
-template <bool kStaged>
-__device__ int map_slice_walk(const uint8_t* stage, const Chunk& c, const StageRange& st, uint32_t g, bool& miss,
-                              uint64_t& inner) {
+// diverge only while a header is parsed.
+//
+// Staged walk: a header is read from the staged bytes only when the header
+// and its literals lie wholly inside them (one range check per sequence);
+// otherwise the walk stops with miss set and the slice is mapped again by the
+// checked walk.  The block's last sequence (no match part) always misses, as
+// the stage holds whole 16-byte units only.
+struct FastRun {
+  uint32_t ms, me, o, lit_t, pe, next;   // literal p is stage[p + lit_t]; p >= pe: periodic byte
+};
+
+// Opens the sequence whose token is at compressed position ip and whose
+// output starts at so.  Returns false if any of its header or literal bytes
+// is outside the stage; a bad offset sets err and leaves r as it was.
+__device__ __forceinline__ bool fast_open(const uint8_t* stage, uint32_t lo, uint32_t len, uint32_t ip, uint32_t so,
+                                          FastRun& r, int& err) {
+  uint32_t q = ip - lo;
+  if (q >= len) return false;
+  const uint32_t tok = stage[q++];
+  uint32_t ll = tok >> 4;
+  if (ll == 15) {
+    uint32_t b;
+    do {
+      if (q >= len) return false;
+      b = stage[q++];
+      ll += b;
+    } while (b == 255);
+  }
+  const uint32_t lit = q;                              // ll < 255 * len: no overflow below
+  if (q + ll + 2 > len) return false;
+  q += ll;
+  const uint32_t o = stage[q] | ((uint32_t)stage[q + 1] << 8);
+  q += 2;
+  uint32_t ml = tok & 15;
+  if (ml == 15) {
+    uint32_t b;
+    do {
+      if (q >= len) return false;
+      b = stage[q++];
+      ml += b;
+    } while (b == 255);
+  }
+  ml += 4;
+  const uint32_t ms = so + ll;
+  if (o == 0 || o > ms) {                              // r keeps its fields: a dead lane reads them
+    err = ZMOE_CHUNK_BAD_OFFSET;
+    return true;
+  }
+  r.ms = ms;
+  r.me = ms + ml;
+  r.o = o;
+  r.lit_t = lit - so;
+  r.pe = ml > o ? r.ms + o : 0xFFFFFFFFu;
+  r.next = lo + q;
+  return true;
+}
+
+// Every lane of the warp runs the staged walk for the same 64 groups (a lane
+// with no slice to map, or one that met an error or a miss, goes on as a dead
+// lane whose entries are discarded), so that the warp can store its entries
+// through a transpose: each lane puts 8 groups (128 bytes of its slice) into
+// tbuf, then each store instruction writes 4 whole 128-byte lines, 8 lanes per
+// line, instead of 32 lanes each writing 16 bytes into a different line.
+// tbuf: this warp's 32 x kTPitch uint4.
+__device__ int map_slice_staged(const uint8_t* stage, uint4* tbuf, const Chunk& c, const StageRange& st, uint32_t g,
+                                bool active, bool& miss, uint64_t& inner) {
+  const uint32_t lane = threadIdx.x & 31;
+  const uint32_t b0 = g * kSlice;
+  const uint32_t b1 = min(b0 + kSlice, c.out_size);
+  const uint32_t step0 = b0 & ~(kStep - 1);            // a slice lies inside one step
+  int err = 0;
+  bool dead = !active;
+  FastRun cur{0u, 0u, 1u, 0u, 0xFFFFFFFFu, 0u};        // a dead lane's fields: match bytes, stage index 0
+  if (!dead) {
+    const uint2 ix = __ldg(reinterpret_cast<const uint2*>(c.index) + g);
+    const uint32_t so = ix.y;                          // output start of the sequence at ix.x
+    if (so > b0) {
+      err = ZMOE_CHUNK_BAD_DESC;
+      dead = true;
+    } else if (!fast_open(stage, st.lo, st.len, ix.x, so, cur, err)) {
+      miss = true;
+      dead = true;
+    } else if (err || cur.me <= b0) {                  // cur.me <= b0: the index names a sequence ending before b0
+      if (!err) err = ZMOE_CHUNK_BAD_DESC;
+      dead = true;
+    }
+  }
+  // c.map: the region's entries; this warp's 32 slices start at slice g - lane
+  uint4* wmap = reinterpret_cast<uint4*>(c.map) + (size_t)(threadIdx.x - lane) * (kSlice / 4);
+  FastRun nxt = cur;                                   // read only for bytes at or past cur.me
+  for (uint32_t k = 0; k < kSlice / 4; ++k) {
+    const uint32_t p0 = b0 + 4 * k;
+    // a live lane has cur.me > p0 here, and an opened sequence covers at least 4 bytes
+    const bool turn = !dead && cur.me <= p0 + 4 && cur.me < b1;
+    if (turn) {
+      if (!fast_open(stage, st.lo, st.len, cur.next, cur.me, nxt, err)) {
+        miss = true;
+        dead = true;
+      } else if (err) {
+        dead = true;
+      }
+    }
+    uint32_t x[4];
+#pragma unroll
+    for (uint32_t b = 0; b < 4; ++b) {
+      const uint32_t p = p0 + b;
+      const bool in_a = p < cur.me;
+      const uint32_t ms = in_a ? cur.ms : nxt.ms, lit_t = in_a ? cur.lit_t : nxt.lit_t;
+      const uint32_t o = in_a ? cur.o : nxt.o, pe = in_a ? cur.pe : nxt.pe;
+      const bool lit = p < ms;
+      const uint32_t lb = stage[lit ? p + lit_t : 0u];
+      uint32_t v = p - o;
+      if (p >= pe) v = periodic_source(p, ms, o, step0);
+      v = v >= step0 ? (v | kInner) : v;
+      x[b] = lit ? (kLit | lb) : v;
+    }
+    tbuf[lane * kTPitch + k % kTGroups] = make_uint4(x[0], x[1], x[2], x[3]);
+    if (!dead && p0 < b1 && ((x[0] | x[1] | x[2] | x[3]) & kInner)) inner |= 1ull << k;
+    if (turn && !dead) cur = nxt;
+    if (k % kTGroups == kTGroups - 1) {
+      __syncwarp();
+      const uint32_t piece = lane % kTGroups, k0 = k + 1 - kTGroups;
+#pragma unroll
+      for (uint32_t it = 0; it < kTGroups; ++it) {
+        const uint32_t src = it * (32 / kTGroups) + lane / kTGroups;   // lane whose line this lane writes
+        wmap[src * (kSlice / 4) + k0 + piece] = tbuf[src * kTPitch + piece];
+      }
+      __syncwarp();
+    }
+  }
+  return dead ? err : 0;
+}
+
+// Checked walk: every compressed byte is read from the stage when it lies
+// there and from global memory otherwise, with every bound checked.
+__device__ int map_slice_checked(const uint8_t* stage, const Chunk& c, const StageRange& st, uint32_t g,
+                                 uint64_t& inner) {
   const uint32_t b0 = g * kSlice;
   const uint2 ix = __ldg(reinterpret_cast<const uint2*>(c.index) + g);
   const uint32_t so = ix.y;                            // output start of the sequence at ix.x
   if (so > b0) return ZMOE_CHUNK_BAD_DESC;
   const uint32_t b1 = min(b0 + kSlice, c.out_size);
   const uint32_t step0 = b0 & ~(kStep - 1);            // a slice lies inside one step
-  const Staged sv{stage, st.lo, st.len};
   auto checked = [&](uint32_t q) -> uint32_t {
     const uint32_t d = q - st.lo;
     return d < st.len ? (uint32_t)stage[d] : (uint32_t)__ldg(c.src + q);
   };
-  auto fast = [&](uint32_t q) -> uint32_t { return sv.at(q, miss); };
-  auto open = [&](uint32_t ip, uint32_t so_, Run& r) -> int {
-    if constexpr (kStaged) return open_run(fast, c.src_size, ip, so_, step0, r);
-    else return open_run(checked, c.src_size, ip, so_, step0, r);
-  };
   auto entry = [&](uint32_t p, const Run& a, const Run& b) -> uint32_t {
-    const bool in_a = p < a.me;
-    const uint32_t ms = in_a ? a.ms : b.ms, o = in_a ? a.o : b.o;
-    const uint32_t wrap = in_a ? a.wrap : b.wrap, lit_base = in_a ? a.lit_base : b.lit_base;
-    const bool periodic = in_a ? a.periodic : b.periodic;
-    if constexpr (kStaged) {
-      const bool lit = p < ms;
-      const uint32_t d = lit_base + p - sv.lo;
-      miss |= lit && d >= sv.len;
-      const uint32_t lb = sv.p[min(d, sv.len - 1)];
-      const uint32_t xm = match_entry(p, ms, o, wrap, periodic, step0);
-      return lit ? (kLit | lb) : xm;
-    } else {
-      if (p < ms) return kLit | checked(lit_base + p);
-      return match_entry(p, ms, o, wrap, periodic, step0);
-    }
+    const Run& r = p < a.me ? a : b;
+    if (p < r.ms) return kLit | checked(r.lit_base + p);
+    return match_entry(p, r.ms, r.o, r.periodic, step0);
   };
   Run cur;
-  int err = open(ix.x, so, cur);
+  int err = open_run(checked, c.src_size, ix.x, so, cur);
   if (err) return err;
   if (cur.me <= b0) return ZMOE_CHUNK_BAD_DESC;        // the index names a sequence ending before b0
   uint4* map4 = reinterpret_cast<uint4*>(c.map);
@@ -297,7 +402,7 @@ __device__ int map_slice_walk(const uint8_t* stage, const Chunk& c, const StageR
     const bool turn = cur.me <= p0 + 4 && cur.me < b1;
     if (turn) {
       if (cur.last) return ZMOE_CHUNK_SHORT_OUTPUT;
-      if ((err = open(cur.next, cur.me, nxt)) != 0) return err;
+      if ((err = open_run(checked, c.src_size, cur.next, cur.me, nxt)) != 0) return err;
       if (nxt.me < min(p0 + 4, b1)) return ZMOE_CHUNK_SHORT_OUTPUT;   // only the last one can be this short
     }
     const uint4 x = make_uint4(entry(p0 + 0, cur, nxt), entry(p0 + 1, cur, nxt), entry(p0 + 2, cur, nxt),
@@ -311,17 +416,22 @@ __device__ int map_slice_walk(const uint8_t* stage, const Chunk& c, const StageR
 
 // inner: bit k set when group k (bytes 4k..4k+3 of the slice) holds an entry
 // whose source lies inside its own step.
-__device__ int map_slice(const uint8_t* stage, const Chunk& c, const StageRange& st, uint32_t g, uint64_t& inner) {
+// Called by every thread of the CTA (the staged walk stores warp-wide).
+__device__ int map_slice(const uint8_t* stage, uint4* tbuf, const Chunk& c, const StageRange& st, uint32_t g,
+                         uint64_t& inner) {
   inner = 0;
-  if (g * kSlice >= c.out_size) return 0;
-  if (g >= c.n_index) return ZMOE_CHUNK_BAD_DESC;
-  bool miss = st.len == 0;
-  if (!miss) {
-    const int err = map_slice_walk<true>(stage, c, st, g, miss, inner);
-    if (!miss) return err;
+  const bool have = g * kSlice < c.out_size;
+  const bool valid = have && g < c.n_index;
+  bool miss = false;
+  int err = 0;
+  if (st.len != 0) {                                   // the same in every thread of the CTA
+    err = map_slice_staged(stage, tbuf, c, st, g, valid, miss, inner);
+    if (!miss && valid) return err;
     inner = 0;
   }
-  return map_slice_walk<false>(stage, c, st, g, miss, inner);   // some byte was not staged: checked reads
+  if (!have) return 0;
+  if (!valid) return ZMOE_CHUNK_BAD_DESC;
+  return map_slice_checked(stage, c, st, g, inner);   // some byte was not staged: checked reads
 }
 
 // ---------------------------------------------------------------------------
@@ -667,7 +777,7 @@ map_kernel(const zmoe_chunk* __restrict__ chunks) {
     cr.map = d.map + (size_t)r * kRegion;
     const uint32_t g = r * kThreads + threadIdx.x;
     uint64_t inner;
-    int err = map_slice(M.stage, cr, st, g, inner);
+    int err = map_slice(M.stage, M.tbuf + (threadIdx.x / 32) * 32 * kTPitch, cr, st, g, inner);
     if (err) inner = 0;
     // list the groups to chase (group index within the region), in the stage
     uint32_t total;
