@@ -60,7 +60,7 @@ constexpr uint32_t kPerThread = kStep / kRThreads;  // bytes resolved per thread
 constexpr uint32_t kRing = 65536;                   // decoded-exponent window
 constexpr uint32_t kRingMask = kRing - 1;
 constexpr uint32_t kStage = 48 * 1024;              // staged compressed bytes per region
-constexpr uint32_t kTGroups = 8;                    // groups per lane between transposed map stores
+constexpr uint32_t kTGroups = 4;                    // groups per lane between transposed map stores
 constexpr uint32_t kTPitch = kTGroups + 1;          // uint4 per lane in tbuf (padded: no bank conflicts)
 constexpr uint32_t kMapBufs = 4;                    // map-entry buffers of the resolve
 constexpr uint32_t kAhead = kMapBufs - 1;           // steps whose entries are in flight
@@ -74,7 +74,8 @@ static_assert(kRegion == ZMOE_MAP_ENTRIES, "one map entry per byte of a region")
 static_assert(kRegion <= kRing, "a region's sources stay inside the window");
 static_assert(kStep % kSlice == 0 && kRegion % kStep == 0, "slices nest in steps nest in regions");
 static_assert(kPerThread == 4, "one 128-bit map load per thread and step");
-static_assert(kTGroups * 4 * 4 == 128 && (kSlice / 4) % kTGroups == 0, "a lane's transposed groups fill one 128-byte line");
+static_assert((kTGroups * 16) % 32 == 0 && 32 % kTGroups == 0 && (kSlice / 4) % kTGroups == 0,
+              "a lane's transposed groups fill whole 32-byte sectors");
 static_assert((kRegion / 4) * sizeof(uint16_t) <= kStage && kRegion / 4 <= 65536, "the chase list fits the stage");
 
 struct MapSmem {                                    // map_kernel
@@ -300,9 +301,10 @@ __device__ __forceinline__ bool fast_open(const uint8_t* stage, uint32_t lo, uin
 // Every lane of the warp runs the staged walk for the same 64 groups (a lane
 // with no slice to map, or one that met an error or a miss, goes on as a dead
 // lane whose entries are discarded), so that the warp can store its entries
-// through a transpose: each lane puts 8 groups (128 bytes of its slice) into
-// tbuf, then each store instruction writes 4 whole 128-byte lines, 8 lanes per
-// line, instead of 32 lanes each writing 16 bytes into a different line.
+// through a transpose: each lane puts kTGroups = 4 groups (64 bytes of its
+// slice) into tbuf, then each store instruction writes 8 runs of 64 bytes (two
+// whole 32-byte sectors each), 4 lanes per run, instead of 32 lanes each
+// writing 16 bytes into a different line.
 // tbuf: this warp's 32 x kTPitch uint4.
 __device__ int map_slice_staged(const uint8_t* stage, uint4* tbuf, const Chunk& c, const StageRange& st, uint32_t g,
                                 bool active, bool& miss, uint64_t& inner) {
