@@ -88,6 +88,7 @@ struct MapSmem {                                    // map_kernel
 struct Smem {                                       // resolve_kernel
   uint8_t ring[kRing];
   uint32_t mbuf[kMapBufs][kStep];                   // map entries of the next steps
+  uint32_t sbuf[kMapBufs][kStep / 4];               // sign+mantissa words of the next steps' flush windows
   int32_t err;
 };
 
@@ -109,6 +110,10 @@ __device__ __forceinline__ void set_err(SM& S, int32_t code) { atomicCAS(&S.err,
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
                : "memory");
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
@@ -230,10 +235,13 @@ __device__ __forceinline__ uint32_t periodic_source(uint32_t p, uint32_t ms, uin
   const uint32_t wrap = max(ms, step0);
   return wrap - o + (p - wrap) % o;
 }
-__device__ __forceinline__ uint32_t match_entry(uint32_t p, uint32_t ms, uint32_t o, bool periodic, uint32_t step0) {
+// Match entries hold the source position plus the chunk's ring offset rofs,
+// so the resolve's ring index is the entry's low 16 bits.
+__device__ __forceinline__ uint32_t match_entry(uint32_t p, uint32_t ms, uint32_t o, bool periodic, uint32_t step0,
+                                                uint32_t rofs) {
   uint32_t v = p - o;
   if (periodic && p - ms >= o) v = periodic_source(p, ms, o, step0);
-  return v >= step0 ? (v | kInner) : v;
+  return (v + rofs) | (v >= step0 ? kInner : 0u);
 }
 
 // The slice is walked in 64 groups of 4 bytes, the same count in every lane.
@@ -355,7 +363,7 @@ __device__ int map_slice_staged(const uint8_t* stage, uint4* tbuf, const Chunk& 
       const uint32_t lb = stage[lit ? p + lit_t : 0u];
       uint32_t v = p - o;
       if (p >= pe) v = periodic_source(p, ms, o, step0);
-      v = v >= step0 ? (v | kInner) : v;
+      v = (v + c.rofs) | (v >= step0 ? kInner : 0u);
       x[b] = lit ? (kLit | lb) : v;
     }
     tbuf[lane * kTPitch + k % kTGroups] = make_uint4(x[0], x[1], x[2], x[3]);
@@ -392,7 +400,7 @@ __device__ int map_slice_checked(const uint8_t* stage, const Chunk& c, const Sta
   auto entry = [&](uint32_t p, const Run& a, const Run& b) -> uint32_t {
     const Run& r = p < a.me ? a : b;
     if (p < r.ms) return kLit | checked(r.lit_base + p);
-    return match_entry(p, r.ms, r.o, r.periodic, step0);
+    return match_entry(p, r.ms, r.o, r.periodic, step0, c.rofs);
   };
   Run cur;
   int err = open_run(checked, c.src_size, ix.x, so, cur);
@@ -482,7 +490,7 @@ __device__ int chase_groups(const Chunk& c, uint32_t rbase, const uint16_t* list
 #pragma unroll
       for (uint32_t q = 0; q < 4 * kChaseGroups; ++q) {
         if (x[q] & kInner) {
-          const uint32_t src = x[q] & kPosMask;
+          const uint32_t src = (x[q] & kPosMask) - c.rofs;
           const uint32_t step0 = cur[q] & ~(kStep - 1);
           if (src >= cur[q] || src < step0) {
             err = ZMOE_CHUNK_BAD_DESC;
@@ -530,73 +538,99 @@ __device__ void flush_range(Smem& S, const Chunk& c, uint32_t f0, uint32_t f1, u
 // ---------------------------------------------------------------------------
 // phase 4: resolve the region's steps through the shared-memory window
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void fetch_step(Smem& S, const Chunk& c, uint32_t s0, uint32_t buf) {
-  const uint32_t* src = c.map + s0;                    // the chunk's entries are contiguous by position
-  uint32_t* dst = S.mbuf[buf];
-  for (uint32_t q = threadIdx.x; q < kStep / 4; q += kRThreads) cp_async16(dst + 4 * q, src + 4 * q);
-}
+__device__ __forceinline__ uint32_t pack2(uint32_t e4, uint32_t s4, uint32_t sel);
 
-// Resolves steps [0, n_steps) of the chunk; the last step of each region is
-// followed by that region's flush.
-__device__ int resolve_steps(Smem& S, const Chunk& c, uint32_t head, bool vec) {
-  const uint32_t R0 = 0, R1 = c.out_size;
+// Resolves steps [0, n_steps) of the chunk.  Thread q copies (cp.async) map
+// entries 4q..4q+3 of every step; warp v resolves bytes 128v..128v+127, lane
+// l the bytes l, l + 32, l + 64 and l + 96 of those.
+//
+// The output is written as it leaves the ring: step t overwrites the slots of
+// positions 64 KiB before it, so from step kLag = 32 on, each step first
+// writes BF16 for its flush window, positions
+// [(t - kLag) * kStep + head, + kStep): thread q takes 4 of them, whose
+// sign+mantissa word came in with the step's entries (cp.async, 4 bytes,
+// aligned because sm + head is).  The window's lowest positions were written
+// by the previous step's window, and its highest are overwritten only by the
+// next step.  Positions [0, head) go out at step kLag, and whatever no window
+// covered (the whole chunk when it has at most kLag steps) after the last
+// step.
+__device__ int resolve_steps(Smem& S, const Chunk& c, uint32_t head, bool vec, bool vec8) {
+  constexpr uint32_t kLag = kRegion / kStep;
+  const uint32_t R1 = c.out_size;
   const uint32_t n_steps = (R1 + kStep - 1) / kStep;
-  const uint32_t rofs = c.rofs;
+  const uint32_t q = threadIdx.x;
+  const uint32_t j0 = kPerThread * q;
   int err = 0;
-  // map entries run kAhead steps ahead of the resolve (one commit group per
-  // step, empty past the end, so wait_group counts stay uniform)
+  // map entries (and window words) run kAhead steps ahead of the resolve (one
+  // commit group per step, empty past the end, so wait_group counts stay uniform)
+  const uint32_t* fsrc = c.map + j0;                   // this thread's entries of the next step to fetch
+  uint32_t* mrow = &S.mbuf[0][j0];                     // its entries in buffer 0; buffer k is k * kStep further
+  auto fetch = [&](uint32_t tf) {
+    cp_async16(mrow + (tf % kMapBufs) * kStep, fsrc);
+    if (tf >= kLag) cp_async4(&S.sbuf[tf % kMapBufs][q], c.sm + (tf - kLag) * kStep + head + j0);
+  };
   for (uint32_t p = 0; p < kAhead; ++p) {
-    if (p < n_steps) fetch_step(S, c, R0 + p * kStep, p % kMapBufs);
+    if (p < n_steps) fetch(p);
     cp_async_commit();
+    fsrc += kStep;
   }
+  const uint32_t jb = 128 * (q / 32) + (q % 32);      // this thread's first byte of a step
+  uint32_t w = (jb + c.rofs) & kRingMask;              // its ring index
   for (uint32_t t = 0; t < n_steps; ++t) {
-    const uint32_t s0 = R0 + t * kStep;
-    // buffer (t + kAhead) % kMapBufs last held step t - 1, read before its barrier B
-    // (and before the flush that follows a region's last step)
-    if (t + kAhead < n_steps) fetch_step(S, c, s0 + kAhead * kStep, (t + kAhead) % kMapBufs);
+    const uint32_t s0 = t * kStep;
+    // buffer (t + kAhead) % kMapBufs last held step t - 1, which this thread has read
+    if (t + kAhead < n_steps) fetch(t + kAhead);
+    fsrc += kStep;
     cp_async_commit();
     cp_async_wait<kAhead>();
-    __syncthreads();                                   // A: step entries landed; earlier writes visible
-    const uint32_t* mb = S.mbuf[t % kMapBufs];
-    const uint32_t j0 = kPerThread * threadIdx.x;
-    const uint32_t e = s0 + j0;
-    const uint4 m = *reinterpret_cast<const uint4*>(mb + j0);
-    uint32_t x[4] = {m.x, m.y, m.z, m.w};
+    __syncthreads();                                   // A: the step's entries landed; the previous steps' bytes visible
+    // this thread's bytes: positions s0 + jb + 32k, k = 0..3 (a warp takes 128
+    // consecutive bytes, so one gather instruction reads a few runs of
+    // consecutive sources instead of 32 scattered ones)
+    const uint32_t* mb = S.mbuf[t % kMapBufs] + jb;
+    uint32_t x[4];
+#pragma unroll
+    for (uint32_t k = 0; k < 4; ++k) x[k] = mb[32 * k];
     const bool tail = s0 + kStep > R1;                 // the chunk's last step (the same in every thread)
     if (tail) {
 #pragma unroll
-      for (uint32_t b = 0; b < 4; ++b)
-        if (e + b >= R1) x[b] = kLit;                  // past the chunk end: entry never written
+      for (uint32_t k = 0; k < 4; ++k)
+        if (s0 + jb + 32 * k >= R1) x[k] = kLit;       // past the chunk end: entry never written
     }
     // map_kernel left every entry a literal or a position before the step
     if ((x[0] | x[1] | x[2] | x[3]) & kInner) {
       err = ZMOE_CHUNK_BAD_DESC;
 #pragma unroll
-      for (uint32_t b = 0; b < 4; ++b) x[b] = kLit;
+      for (uint32_t k = 0; k < 4; ++k) x[k] = kLit;
     }
-    uint32_t word = 0;
+    uint32_t val[4];
 #pragma unroll
-    for (uint32_t b = 0; b < 4; ++b) {
-      const uint32_t val = (x[b] & kLit) ? (x[b] & 0xFFu) : (uint32_t)S.ring[(x[b] + rofs) & kRingMask];
-      word |= val << (8 * b);
+    for (uint32_t k = 0; k < 4; ++k) val[k] = (x[k] & kLit) ? (x[k] & 0xFFu) : (uint32_t)S.ring[x[k] & kRingMask];
+    if (t >= kLag) {                                   // the flush window, before its slots are overwritten
+      const uint32_t i = (t - kLag) * kStep + head + j0;
+      const uint32_t ev = *reinterpret_cast<const uint32_t*>(&S.ring[c.ri(i)]);
+      const uint32_t sv = S.sbuf[t % kMapBufs][q];
+      const uint32_t lo = pack2(ev, sv, 0x4140), hi = pack2(ev, sv, 0x4342);
+      if (vec8) {
+        __stcs(reinterpret_cast<uint2*>(c.dst + i), make_uint2(lo, hi));
+      } else {
+        c.dst[i] = (uint16_t)lo;
+        c.dst[i + 1] = (uint16_t)(lo >> 16);
+        c.dst[i + 2] = (uint16_t)hi;
+        c.dst[i + 3] = (uint16_t)(hi >> 16);
+      }
+      if (t == kLag && q < head) c.dst[q] = (uint16_t)recombine(__ldg(c.sm + q), S.ring[c.ri(q)]);
     }
-    __syncthreads();                                   // B: the whole step is gathered
-    if (!tail) {
+    __syncthreads();                                   // B: the whole step is gathered, the window read
 #pragma unroll
-      for (uint32_t b = 0; b < 4; ++b) S.ring[(e + b + rofs) & kRingMask] = (uint8_t)(word >> (8 * b));
-    } else {
-#pragma unroll
-      for (uint32_t b = 0; b < 4; ++b)
-        if (e + b < R1) S.ring[(e + b + rofs) & kRingMask] = (uint8_t)(word >> (8 * b));
-    }
-    const uint32_t s1 = s0 + kStep;
-    if (s1 % kRegion == 0 || s1 >= R1) {               // a region's last step: write the region out
-      if (__syncthreads_or(err != 0)) break;
-      const uint32_t F0 = (s0 / kRegion) * kRegion;
-      flush_range(S, c, F0, min(F0 + kRegion, R1), head, vec);
-    }
+    for (uint32_t k = 0; k < 4; ++k)
+      if (!tail || s0 + jb + 32 * k < R1) S.ring[(w + 32 * k) & kRingMask] = (uint8_t)val[k];
+    w = (w + kStep) & kRingMask;
   }
   cp_async_wait<0>();
+  __syncthreads();                                     // the last step's bytes visible
+  const uint32_t f0 = n_steps > kLag ? (n_steps - kLag) * kStep + head : 0u;
+  flush_range(S, c, min(f0, R1), R1, head, vec);
   return err;
 }
 
@@ -665,6 +699,7 @@ __device__ void resolve_chunk(Smem& S, const Chunk& c) {
   const uintptr_t sa = reinterpret_cast<uintptr_t>(c.sm), da = reinterpret_cast<uintptr_t>(c.dst);
   const uint32_t head = (uint32_t)((16 - (sa & 15)) & 15);
   const bool vec = ((da + 2 * (uintptr_t)head) & 15) == 0;
+  const bool vec8 = ((da + 2 * (uintptr_t)head) & 7) == 0;
   const uint32_t n_reg = (c.out_size + kRegion - 1) / kRegion;
   const int32_t* rstat = region_status(c.map, n_reg);
   for (uint32_t r = 0; r < n_reg; ++r) {               // map_kernel's verdicts (the same in every thread)
@@ -674,7 +709,7 @@ __device__ void resolve_chunk(Smem& S, const Chunk& c) {
       return;
     }
   }
-  const int err = resolve_steps(S, c, head, vec);
+  const int err = resolve_steps(S, c, head, vec, vec8);
   if (err) set_err(S, err);
 }
 
