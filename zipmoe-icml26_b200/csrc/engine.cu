@@ -113,6 +113,7 @@ struct Layer {
   uint16_t* out_stage = nullptr;
   cudaEvent_t status_ready = nullptr;
   cudaEvent_t offsets_ready = nullptr;   // zmoe_layer_experts: the pinned offsets were copied
+  cudaEvent_t counts_ready = nullptr;    // forward: the per-expert counts reached the host
   bool offsets_pending = false;
 
   // optional per-kernel timing: events around decode and FFN launches on the
@@ -153,6 +154,7 @@ Layer::~Layer() {
   cudaFree(x_stage); cudaFree(out_stage); cudaFree(map_scratch);
   if (status_ready) cudaEventDestroy(status_ready);
   if (offsets_ready) cudaEventDestroy(offsets_ready);
+  if (counts_ready) cudaEventDestroy(counts_ready);
   for (auto e : ev_pool) cudaEventDestroy(e);
 }
 
@@ -245,6 +247,7 @@ zmoe_status Layer::init(const zmoe_layer_config& c) {
   if (st != ZMOE_OK) return st;
   ZMOE_CUDA_RET(cudaEventCreateWithFlags(&status_ready, cudaEventDisableTiming));
   ZMOE_CUDA_RET(cudaEventCreateWithFlags(&offsets_ready, cudaEventDisableTiming));
+  ZMOE_CUDA_RET(cudaEventCreateWithFlags(&counts_ready, cudaEventDisableTiming));
   return ZMOE_OK;
 }
 
@@ -533,8 +536,10 @@ zmoe_status Layer::forward(const uint16_t* x, int T, uint16_t* out, cudaStream_t
   if ((st = launch_permute(&pa, s)) != ZMOE_OK) return st;
   stats.launches += 3;
   ZMOE_CUDA_RET(cudaMemcpyAsync(counts_host, counts, sizeof(int32_t) * E, cudaMemcpyDeviceToHost, s));
+  ZMOE_CUDA_RET(cudaEventRecord(counts_ready, s));
 
-  // shared expert first: it needs no decoded weights
+  // shared expert first: it needs no decoded weights, and it keeps the GPU
+  // busy while the host waits for the counts and makes the cache decisions
   if (cfg.shared_inter > 0 && w_shared[0]) {
     zmoe_ffn_args fa{};
     const uint16_t* tab[3] = {w_shared[0], w_shared[1], w_shared[2]};   // host table
@@ -543,7 +548,9 @@ zmoe_status Layer::forward(const uint16_t* x, int T, uint16_t* out, cudaStream_t
     if ((st = launch_expert_ffn(&fa, s)) != ZMOE_OK) return st;
     stats.launches += 2;
   }
-  ZMOE_CUDA_RET(cudaStreamSynchronize(s));
+  // everything before the counts copy is done, the previous forward's decode
+  // and pinned-buffer copies included
+  ZMOE_CUDA_RET(cudaEventSynchronize(counts_ready));
   if ((st = check_status()) != ZMOE_OK) return st;   // previous forward's decode
   desc_cursor = 0;
   if ((st = fold_timing()) != ZMOE_OK) return st;

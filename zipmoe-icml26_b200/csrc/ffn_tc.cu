@@ -17,7 +17,10 @@
 // TMEM lanes 32*(w%4)..+31).  Operands land in shared memory through 2D tensor
 // maps with 128-byte swizzle (K-major, 64 bf16 per row); a 4-stage (up) or
 // 6-stage (down) mbarrier ring overlaps loads with MMAs.  Accumulators: fp32
-// in TMEM (gate at columns 0..127, up at 128..255).
+// in TMEM, two of them, so the MMAs of a CTA's next unit run while the
+// epilogue drains the last one (up: gate at columns 0..127 and up at 128..255
+// of each 256-column accumulator; down: 128 columns each).  The 192 KB operand
+// ring keeps one CTA per SM, so the 512 columns are always free.
 //
 // Every mbarrier wait is bounded; on a timeout the CTA records an error code
 // in zmoe's device error word, waits (bounded) for the loads it issued,
@@ -157,15 +160,16 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_tc_kernel(const __grid_consta
   constexpr int NA = MODE == 0 ? 2 : 1;
   constexpr int STAGES = MODE == 0 ? 4 : 6;
   constexpr int kStageBytes = (NA + 1) * kTileBytes;
-  constexpr uint32_t kTmemCols = MODE == 0 ? 256 : 128;
+  constexpr uint32_t kAccCols = MODE == 0 ? 256 : 128;   // TMEM columns of one accumulator
+  constexpr uint32_t kTmemCols = 2 * kAccCols;            // two accumulators: MMA and epilogue overlap
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * kStageBytes);
   uint64_t* empty = full + STAGES;
-  uint64_t* tmem_full = empty + STAGES;
-  uint64_t* tmem_empty = tmem_full + 1;
-  uint64_t* drain = tmem_empty + 1;
+  uint64_t* tmem_full = empty + STAGES;                // [2]
+  uint64_t* tmem_empty = tmem_full + 2;               // [2]
+  uint64_t* drain = tmem_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   int32_t* cta_err = reinterpret_cast<int32_t*>(tmem_slot + 1);
   int32_t* prefix = cta_err + 1;              // [g_count + 1] tile prefix
@@ -183,8 +187,10 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_tc_kernel(const __grid_consta
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(tmem_full, 1);
-    mbar_init(tmem_empty, 4);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tmem_full[b], 1);
+      mbar_init(&tmem_empty[b], 4);
+    }
     mbar_init(drain, 1);
     *cta_err = 0;
     int acc = 0;
@@ -266,15 +272,18 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_tc_kernel(const __grid_consta
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       int stage = 0;
-      uint32_t phase = 0, acc_phase = 0;
+      uint32_t phase = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
+      for (int u = blockIdx.x, i = 0; u < total && ok; u += gridDim.x, ++i) {
         int g, mt, nt;
         unit_of(u, g, mt, nt);
         const int valid = min(BN, rows[g] - nt * BN);
         const int n = max(16, (valid + 15) & ~15);
         const uint32_t idesc = instr_desc(n);
-        if (!mbar_wait(tmem_empty, acc_phase ^ 1u, cta_err)) break;
+        const int ab = i & 1;                           // accumulator of this unit
+        const uint32_t acc_phase = (uint32_t)(i >> 1) & 1u;
+        const uint32_t tacc = tmem + (uint32_t)ab * kAccCols;
+        if (!mbar_wait(&tmem_empty[ab], acc_phase ^ 1u, cta_err)) break;
         tc_fence_after();
         for (int ks = 0; ks < KS; ++ks) {
           if (!mbar_wait(&full[stage], phase, cta_err)) { ok = false; break; }
@@ -286,15 +295,14 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_tc_kernel(const __grid_consta
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk) {
             const uint32_t accf = (ks | kk) != 0;
-            tc_mma(tmem, da0 + 2 * kk, db + 2 * kk, idesc, accf);
-            if (NA == 2) tc_mma(tmem + 128, da1 + 2 * kk, db + 2 * kk, idesc, accf);
+            tc_mma(tacc, da0 + 2 * kk, db + 2 * kk, idesc, accf);
+            if (NA == 2) tc_mma(tacc + 128, da1 + 2 * kk, db + 2 * kk, idesc, accf);
           }
           tc_commit(&empty[stage]);
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
         }
         if (!ok) break;
-        tc_commit(tmem_full);
-        acc_phase ^= 1u;
+        tc_commit(&tmem_full[ab]);
       }
       if (!ok || *(volatile int32_t*)cta_err) {
         // error path: wait (bounded) until every MMA issued here has finished
@@ -307,17 +315,17 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_tc_kernel(const __grid_consta
   } else {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;                     // TMEM lane quarter of this warp
-    uint32_t acc_phase = 0;
-    for (int u = blockIdx.x; u < total; u += gridDim.x) {
+    for (int u = blockIdx.x, i = 0; u < total; u += gridDim.x, ++i) {
       int g, mt, nt;
       unit_of(u, g, mt, nt);
       const int valid = min(BN, rows[g] - nt * BN);
       const int n = max(16, (valid + 15) & ~15);
-      if (!mbar_wait(tmem_full, acc_phase, cta_err)) break;
+      const int ab = i & 1;
+      if (!mbar_wait(&tmem_full[ab], (uint32_t)(i >> 1) & 1u, cta_err)) break;
       tc_fence_after();
       const int feat = mt * BM + q * 32 + lane;   // output feature of this thread
       const size_t rbase = (size_t)(row0[g] + nt * BN);
-      const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16);
+      const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)ab * kAccCols;
       for (int c0 = 0; c0 < n; c0 += 16) {
         uint32_t a[16], b[16];
         tmem_ld16(taddr + c0, a);
@@ -340,8 +348,7 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_tc_kernel(const __grid_consta
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(tmem_empty);
-      acc_phase ^= 1u;
+      if (lane == 0) mbar_arrive(&tmem_empty[ab]);
     }
   }
   tc_fence_before();
@@ -356,7 +363,7 @@ template <int MODE>
 constexpr int smem_bytes() {
   constexpr int NA = MODE == 0 ? 2 : 1;
   constexpr int STAGES = MODE == 0 ? 4 : 6;
-  return 1024 + STAGES * (NA + 1) * kTileBytes + 2 * STAGES * 8 + 24 + 8 + 4 * (4 * kMaxGroups + 2);
+  return 1024 + STAGES * (NA + 1) * kTileBytes + 2 * STAGES * 8 + 40 + 8 + 4 * (4 * kMaxGroups + 2);
 }
 
 // ---------------------------------------------------------------------------
