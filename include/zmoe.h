@@ -309,6 +309,18 @@ zmoe_status zmoe_layer_experts(zmoe_layer* layer, const uint16_t* x_rows, const 
 /* Same with host buffers (pinned for full speed); returns after out_host is written. */
 zmoe_status zmoe_layer_forward_host(zmoe_layer* layer, const uint16_t* x_host, int T, uint16_t* out_host,
                                     zmoe_stream_t stream);
+/* Pipelined form of zmoe_layer_forward_host: queues the input copy, the
+ * forward on `stream` and the output copy, and returns once the forward is
+ * launched (it waits only for this step's expert counts, like
+ * zmoe_layer_forward).  Copies run on the layer's own copy streams through two
+ * device staging slots, so one step's copies overlap the neighbouring steps'
+ * compute.  x_host must stay unchanged and out_host unread until
+ * zmoe_layer_join_host and a wait on its stream. */
+zmoe_status zmoe_layer_submit_host(zmoe_layer* layer, const uint16_t* x_host, int T, uint16_t* out_host,
+                                   zmoe_stream_t stream);
+/* Makes `stream` wait (without blocking the host) until the output copies of
+ * every submitted step have completed. */
+zmoe_status zmoe_layer_join_host(zmoe_layer* layer, zmoe_stream_t stream);
 /* Wait for the stream and report any decode error of earlier forwards. */
 zmoe_status zmoe_layer_sync(zmoe_layer* layer, zmoe_stream_t stream);
 zmoe_status zmoe_layer_get_stats(const zmoe_layer* layer, zmoe_layer_stats* out);

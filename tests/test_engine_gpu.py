@@ -103,6 +103,27 @@ def test_engine_forward_host_matches_device():
     assert torch.equal(d, oh)
 
 
+def test_engine_submit_host_pipeline_matches_device():
+    # five steps with different inputs through the two staging slots; each
+    # step's output lands in its own pinned buffer
+    s = QWEN_SMALL
+    L, *_ = _build(s, 2)
+    xs = [syn.activations(16, s.hidden, seed=20 + i) for i in range(5)]
+    want = [L(x.cuda()).cpu() for x in xs]
+    xh = [x.pin_memory() for x in xs]
+    oh = [torch.zeros_like(x).pin_memory() for x in xh]
+    for a, b in zip(xh, oh):
+        L.submit_host(a, b)
+    L.join_host()
+    torch.cuda.current_stream().synchronize()
+    for w, o in zip(want, oh):
+        assert torch.equal(w, o)
+    # the synchronous call after pipelined steps still sees its own input
+    o2 = torch.empty_like(xh[0]).pin_memory()
+    L.forward_host(xh[0], o2)
+    assert torch.equal(want[0], o2)
+
+
 def test_engine_rejects_bad_inputs():
     from zmoe._lib import ZmoeError
     s = QWEN_SMALL

@@ -111,6 +111,13 @@ struct Layer {
   // host-side pass-through buffers for forward_host
   uint16_t* x_stage = nullptr;
   uint16_t* out_stage = nullptr;
+  // submit_host: two staging slots, copies on their own streams
+  uint16_t* x_slot[2] = {nullptr, nullptr};
+  uint16_t* out_slot[2] = {nullptr, nullptr};
+  cudaStream_t copy_in = nullptr, copy_out = nullptr;
+  cudaEvent_t in_done[2] = {nullptr, nullptr}, fwd_done[2] = {nullptr, nullptr}, out_done[2] = {nullptr, nullptr};
+  uint64_t submitted = 0;
+  zmoe_status submit_host(const uint16_t* x_host, int T, uint16_t* out_host, cudaStream_t s);
   cudaEvent_t status_ready = nullptr;
   cudaEvent_t offsets_ready = nullptr;   // zmoe_layer_experts: the pinned offsets were copied
   cudaEvent_t counts_ready = nullptr;    // forward: the per-expert counts reached the host
@@ -152,6 +159,12 @@ Layer::~Layer() {
   cudaFree(offsets_ext); cudaFreeHost(offsets_host);
   cudaFreeHost(counts_host); cudaFreeHost(desc_host); cudaFreeHost(wtab_host); cudaFreeHost(status_host);
   cudaFree(x_stage); cudaFree(out_stage); cudaFree(map_scratch);
+  cudaFree(x_slot[1]); cudaFree(out_slot[1]);          // slot 0 is x_stage / out_stage
+  for (int i = 0; i < 2; ++i)
+    for (cudaEvent_t e : {in_done[i], fwd_done[i], out_done[i]})
+      if (e) cudaEventDestroy(e);
+  if (copy_in) cudaStreamDestroy(copy_in);
+  if (copy_out) cudaStreamDestroy(copy_out);
   if (status_ready) cudaEventDestroy(status_ready);
   if (offsets_ready) cudaEventDestroy(offsets_ready);
   if (counts_ready) cudaEventDestroy(counts_ready);
@@ -244,7 +257,18 @@ zmoe_status Layer::init(const zmoe_layer_config& c) {
   status_host = hmalloc<int32_t>(max_desc, &st);
   x_stage = dmalloc<uint16_t>((size_t)T * H, &st);
   out_stage = dmalloc<uint16_t>((size_t)T * H, &st);
+  x_slot[0] = x_stage;
+  out_slot[0] = out_stage;
+  x_slot[1] = dmalloc<uint16_t>((size_t)T * H, &st);
+  out_slot[1] = dmalloc<uint16_t>((size_t)T * H, &st);
   if (st != ZMOE_OK) return st;
+  ZMOE_CUDA_RET(cudaStreamCreateWithFlags(&copy_in, cudaStreamNonBlocking));
+  ZMOE_CUDA_RET(cudaStreamCreateWithFlags(&copy_out, cudaStreamNonBlocking));
+  for (int i = 0; i < 2; ++i) {
+    ZMOE_CUDA_RET(cudaEventCreateWithFlags(&in_done[i], cudaEventDisableTiming));
+    ZMOE_CUDA_RET(cudaEventCreateWithFlags(&fwd_done[i], cudaEventDisableTiming));
+    ZMOE_CUDA_RET(cudaEventCreateWithFlags(&out_done[i], cudaEventDisableTiming));
+  }
   ZMOE_CUDA_RET(cudaEventCreateWithFlags(&status_ready, cudaEventDisableTiming));
   ZMOE_CUDA_RET(cudaEventCreateWithFlags(&offsets_ready, cudaEventDisableTiming));
   ZMOE_CUDA_RET(cudaEventCreateWithFlags(&counts_ready, cudaEventDisableTiming));
@@ -569,6 +593,29 @@ zmoe_status Layer::forward(const uint16_t* x, int T, uint16_t* out, cudaStream_t
   return ZMOE_OK;
 }
 
+// One step with host buffers, pipelined: the input copy (copy_in) into staging
+// slot k = step % 2, the forward on s, the output copy (copy_out) from slot k.
+// Slot k's input is rewritten only after the forward of two steps ago has run
+// (fwd_done), and its output only after that step's output copy (out_done),
+// so the next step's input copy and this step's output copy overlap compute.
+zmoe_status Layer::submit_host(const uint16_t* x_host, int T, uint16_t* out_host, cudaStream_t s) {
+  const int k = (int)(submitted & 1);
+  const size_t bytes = (size_t)T * cfg.hidden * 2;
+  if (submitted >= 2) ZMOE_CUDA_RET(cudaStreamWaitEvent(copy_in, fwd_done[k], 0));
+  ZMOE_CUDA_RET(cudaMemcpyAsync(x_slot[k], x_host, bytes, cudaMemcpyHostToDevice, copy_in));
+  ZMOE_CUDA_RET(cudaEventRecord(in_done[k], copy_in));
+  ZMOE_CUDA_RET(cudaStreamWaitEvent(s, in_done[k], 0));
+  if (submitted >= 2) ZMOE_CUDA_RET(cudaStreamWaitEvent(s, out_done[k], 0));
+  zmoe_status st = forward(x_slot[k], T, out_slot[k], s);
+  if (st != ZMOE_OK) return st;
+  ZMOE_CUDA_RET(cudaEventRecord(fwd_done[k], s));
+  ZMOE_CUDA_RET(cudaStreamWaitEvent(copy_out, fwd_done[k], 0));
+  ZMOE_CUDA_RET(cudaMemcpyAsync(out_host, out_slot[k], bytes, cudaMemcpyDeviceToHost, copy_out));
+  ZMOE_CUDA_RET(cudaEventRecord(out_done[k], copy_out));
+  ++submitted;
+  return ZMOE_OK;
+}
+
 }  // namespace zmoe
 
 using zmoe::Layer;
@@ -772,11 +819,30 @@ zmoe_status zmoe_layer_forward_host(zmoe_layer* layer, const uint16_t* x_host, i
   ZMOE_CHECK_ARG(T >= 0 && T <= L->cfg.max_tokens, "forward_host: T=%d outside [0, max_tokens]", T);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const size_t bytes = (size_t)T * L->cfg.hidden * 2;
+  if (L->submitted > 0)                                // slot 0 is shared with submit_host's steps
+    for (int k = 0; k < 2; ++k) ZMOE_CUDA_RET(cudaStreamWaitEvent(s, L->out_done[k], 0));
   ZMOE_CUDA_RET(cudaMemcpyAsync(L->x_stage, x_host, bytes, cudaMemcpyHostToDevice, s));
   zmoe_status st = L->forward(L->x_stage, T, L->out_stage, s);
   if (st != ZMOE_OK) return st;
   ZMOE_CUDA_RET(cudaMemcpyAsync(out_host, L->out_stage, bytes, cudaMemcpyDeviceToHost, s));
   ZMOE_CUDA_RET(cudaStreamSynchronize(s));
+  return ZMOE_OK;
+}
+
+zmoe_status zmoe_layer_submit_host(zmoe_layer* layer, const uint16_t* x_host, int T, uint16_t* out_host,
+                                   zmoe_stream_t stream) {
+  Layer* L = reinterpret_cast<Layer*>(layer);
+  ZMOE_CHECK_ARG(L && x_host && out_host, "submit_host: null pointer");
+  ZMOE_CHECK_ARG(T >= 0 && T <= L->cfg.max_tokens, "submit_host: T=%d outside [0, max_tokens]", T);
+  return L->submit_host(x_host, T, out_host, reinterpret_cast<cudaStream_t>(stream));
+}
+
+zmoe_status zmoe_layer_join_host(zmoe_layer* layer, zmoe_stream_t stream) {
+  Layer* L = reinterpret_cast<Layer*>(layer);
+  ZMOE_CHECK_ARG(L, "join_host: null pointer");
+  if (L->submitted == 0) return ZMOE_OK;
+  const int k = (int)((L->submitted - 1) & 1);         // the last step; copy_out runs its copies in order
+  ZMOE_CUDA_RET(cudaStreamWaitEvent(reinterpret_cast<cudaStream_t>(stream), L->out_done[k], 0));
   return ZMOE_OK;
 }
 

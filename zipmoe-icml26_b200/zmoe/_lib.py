@@ -96,6 +96,8 @@ SIGNATURES = {
     "zmoe_layer_forward": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p]),
     "zmoe_layer_experts": (c_int, [c_void_p, c_void_p, ctypes.POINTER(ctypes.c_int32), c_int, c_void_p, c_void_p]),
     "zmoe_layer_forward_host": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p]),
+    "zmoe_layer_submit_host": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p]),
+    "zmoe_layer_join_host": (c_int, [c_void_p, c_void_p]),
     "zmoe_layer_sync": (c_int, [c_void_p, c_void_p]),
     "zmoe_layer_get_stats": (c_int, [c_void_p, ctypes.POINTER(LayerStats)]),
     "zmoe_layer_reset_stats": (c_int, [c_void_p]),

@@ -116,6 +116,20 @@ class MoELayer:
               "zmoe_layer_forward_host")
         return out
 
+    def submit_host(self, x: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        """Pipelined forward_host (zmoe_layer_submit_host): returns once the step
+        is queued; out is written after join_host() and a wait on the stream.
+        x and out must be pinned host BF16 [T, H] and stay untouched until then."""
+        check(lib.zmoe_layer_submit_host(self._h, x.data_ptr(), x.shape[0], out.data_ptr(),
+                                         torch.cuda.current_stream(self.device).cuda_stream),
+              "zmoe_layer_submit_host")
+        return out
+
+    def join_host(self):
+        """The current stream waits for every submitted step's output copy."""
+        check(lib.zmoe_layer_join_host(self._h, torch.cuda.current_stream(self.device).cuda_stream),
+              "zmoe_layer_join_host")
+
     def experts(self, x_rows: torch.Tensor, counts, y: Optional[torch.Tensor] = None) -> torch.Tensor:
         """Expert stage alone (zmoe_layer_experts): x_rows [rows, H] BF16 grouped
         by this layer's experts, counts[e] rows of expert e; returns fp32 [rows, H]."""
