@@ -27,13 +27,15 @@
 //     step's entries back to a literal or to a byte before the step.  Each
 //     region also gets a status word.
 //
-//  resolve_kernel, one CTA of 512 threads per chunk, region by region:
+//  resolve_kernel, one CTA of 512 threads per chunk:
 //  4. Resolve: step by step (2 KiB, 4 bytes per thread), the entries are
 //     copied into shared memory (cp.async, three steps ahead) and every byte is
 //     gathered from a 64 KiB shared-memory window of decoded exponents.  The
 //     whole step is gathered before it is written.
-//  5. Flush: 16 exponent bytes and 16 sign+mantissa bytes (128-bit loads)
-//     become 16 BF16 values (two 128-bit stores) per thread and group.
+//  5. Flush: each step first writes out the 2 KiB it is about to overwrite in
+//     the window (decoded 32 steps earlier) as BF16, with sign+mantissa bytes
+//     that came in with the step's entries; the last 64 KiB follow the last
+//     step.
 //
 // Only the resolve is serial within a chunk; mapping every region at once
 // keeps the SMs busy when few chunks are decoded.  A chunk without an index
