@@ -20,6 +20,10 @@ Fixtures:
   tokens, which is what ``ExpertDispatcher::GPUExecFunc`` computes
   (``csrc/dispatcher/expert_module.cpp:39-50``), returning results in expert
   order.
+* ``predictor_cases.json`` — the reference ExpertPredictor's predictions on a
+  seeded replay.
+* ``cache_planning_cases.json`` — outputs of the reference's cache-pool planner
+  (runtime/cache_planning.py) on seeded routing traces and small inputs.
 """
 from __future__ import annotations
 
@@ -273,9 +277,72 @@ def predictor_cases(ref):
     print("predictor cases:", sum(len(c["steps"]) for c in cases))
 
 
+def cache_planning_cases(ref):
+    """Runs the reference's runtime/cache_planning.py functions (PlanCache and
+    the pieces it is built from) on seeded synthetic routing traces and small
+    hand-picked inputs, and records their outputs.  Its one GPU query (the
+    device's total memory) is answered with a fixed size."""
+    import json
+    import tempfile
+    spec = importlib.util.spec_from_file_location("ref_cache_planning", os.path.join(ref, "runtime", "cache_planning.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    real = torch.cuda.get_device_properties
+    out = {"calculate_prob": [], "delay_simu": [], "scale_to_k": [], "coverage_to_weight": [], "plan": []}
+    rng = np.random.default_rng(47)
+    for n in (0, 1, 5, 17):
+        p = [float(v) for v in rng.uniform(0.0, 1.0, n)]
+        out["calculate_prob"].append({"probs": p, "out": [float(v) for v in mod.CalculateProb(p)]})
+    for args in ((4, 0, 0, 0.5, 0.2, 0.7, 3, 3, 4), (4, 2, 1, 0.5, 0.2, 0.7, 3, 3, 4), (8, 3, 5, 1.3, 0.05, 0.82, 5, 2, 7),
+                 (6, 6, 0, 0.4, 0.3, 0.6, 3, 3, 2)):
+        out["delay_simu"].append({"args": list(args), "out": float(mod.DelaySimu(*args))})
+    for probs, k in (([0.5, 0.2, 0.2, 0.1], 2), ([0.7, 0.1, 0.1, 0.05, 0.05], 3), ([0.0, 0.0], 1),
+                     ([float(v) for v in sorted(rng.zipf(1.3, 24).astype(float), reverse=True)], 6)):
+        out["scale_to_k"].append({"probs": probs, "k": k, "out": [float(v) for v in mod.scale_to_k(probs, k)]})
+    for n, k in ((8, 2), (16, 4), (60, 4)):
+        curve = 1.0 / np.arange(1, n + 1) ** 1.1
+        target = mod.scale_to_k(list(curve / curve.sum()), k)
+        out["coverage_to_weight"].append({"target": [float(v) for v in target], "k": k,
+                                          "out": [float(v) for v in mod.CoverageToWeight(target, k)]})
+    # PlanCache on seeded traces: trace[prompt][layer][expert] = invocations
+    plans = ((24, 4, 16, 4, 4, 3, 1000, 432000, 0.5, 0.05), (40, 6, 16, 2, 8, 3, 1000, 600000, 0.5, 0.01),
+             (30, 3, 20, 4, 5, 2, 2048, 2400000, 0.6, 0.05))
+    for prompts, layers, E, k, batch, tensors, elems, total_memory, dev_ratio, step in plans:
+        pop = 1.0 / np.arange(1, E + 1) ** 1.2
+        pop /= pop.sum()
+        trace = []
+        for _ in range(prompts):
+            per_layer = []
+            for _ in range(layers):
+                counts = np.zeros(E, dtype=np.int64)
+                for _ in range(6):                                  # 6 tokens per prompt
+                    counts[rng.choice(E, size=k, replace=False, p=rng.permutation(pop))] += 1
+                per_layer.append([int(c) for c in counts])
+            trace.append(per_layer)
+        torch.cuda.get_device_properties = lambda i, m=total_memory: types.SimpleNamespace(total_memory=m)
+        try:
+            with tempfile.NamedTemporaryFile(suffix=".pt") as f:
+                torch.save(trace, f.name)
+                dist = mod.ObtainDistFromTrace(batch, f.name)
+                args = dict(batch_size=batch, k=k, num_experts=E, num_sparse_layers=layers, tensors_per_expert=tensors,
+                            num_elements_per_tensor=elems, compression_ratio=0.72, num_file_chunks=3,
+                            compute_pool_size=4, device_memory_ratio=dev_ratio, decompression_delay=0.45,
+                            SM_IO_delay=0.21, step_size=step)
+                ratio, feasible = mod.PlanCache(trace_path=f.name, **args)
+        finally:
+            torch.cuda.get_device_properties = real
+        out["plan"].append({"trace": trace, "total_memory": total_memory, "args": args, "dist": [float(v) for v in dist],
+                            "ratio": float(ratio), "feasible": bool(feasible)})
+    with open(os.path.join(HERE, "cache_planning_cases.json"), "w") as f:
+        json.dump(out, f)
+    print("cache planning cases:", {kk: len(v) for kk, v in out.items()},
+          [(c["ratio"], c["feasible"]) for c in out["plan"]])
+
+
 if __name__ == "__main__":
     ref = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
     codec_cases()
     qwen_block(ref)
     deepseek_block(ref)
     predictor_cases(ref)
+    cache_planning_cases(ref)
