@@ -54,6 +54,8 @@ def parse():
     ap.add_argument("--codec", default="LZ4HC")
     ap.add_argument("--level", type=int, default=9)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--store", default="device", choices=["device", "host"],
+                    help="where the compressed experts live (host: pinned memory, copied in per miss)")
     return ap.parse_args()
 
 
@@ -143,7 +145,8 @@ def build_workload(args, device_index=0, threads=0):
     wr, sg = syn.router_weights(s)
     sh = syn.shared_weights(s)
     bias = syn.zipf_bias(s, 0)
-    L = MoELayer(s, max_tokens=args.tokens, cache_slots=args.cache, device=device_index)
+    L = MoELayer(s, max_tokens=args.tokens, cache_slots=args.cache, device=device_index,
+                 store=getattr(args, "store", "device"))
     L.set_router(wr, bias, sg)
     L.set_shared(*sh)
     enc = L.load_experts(w, num_file_chunks=args.chunks, codec=args.codec, level=args.level, threads=threads)
@@ -294,6 +297,7 @@ def run_ours(args):
                        "cached_experts": args.cache, "codec": f"{args.codec}-{args.level}",
                        "num_file_chunks": args.chunks, "zipf_s": s.zipf_s,
                        "parallelism": "replicas" if world > 1 else "single",
+                       "store": args.store,
                        "l2": "inputs larger than L2 (decoded + compressed experts > 1 GB)"},
             "e2e": {"value": world * args.tokens / (e2e_ms / 1e3), "unit": UNIT,
                     "h2d_bytes_per_step": x.numel() * 2, "d2h_bytes_per_step": x.numel() * 2},

@@ -275,6 +275,7 @@ typedef struct zmoe_layer_stats {
   uint64_t launches, decode_errors, store_bytes;
   /* filled when timing is on: CUDA-event durations on the launch stream */
   uint64_t decode_ns, decode_timed_bytes, decode_timed_launches, ffn_ns, ffn_timed_launches;
+  uint64_t host_copy_bytes;   /* host tier: compressed bytes copied to the GPU for decodes */
 } zmoe_layer_stats;
 
 zmoe_status zmoe_layer_create(const zmoe_layer_config* cfg, zmoe_layer** out);
@@ -290,6 +291,16 @@ zmoe_status zmoe_layer_set_shared(zmoe_layer* layer, const uint16_t* gate, const
 zmoe_status zmoe_layer_load_expert(zmoe_layer* layer, int expert, int tensor, const uint8_t* const* blocks,
                                    const uint32_t* block_sizes, const uint32_t* original_sizes, int n_chunks,
                                    const uint8_t* sm, uint64_t numel);
+/* Where the compressed experts live, chosen before the first
+ * zmoe_layer_load_expert: ZMOE_STORE_DEVICE (default, HBM) or ZMOE_STORE_HOST
+ * (pinned host memory; every decode first copies each missed tensor's
+ * compressed blocks, index and sign+mantissa plane into a device staging area
+ * on the stream).  The host tier is for models whose compressed experts do not
+ * fit the GPU; a miss then costs a PCIe copy of the compressed tensor.  It
+ * replaces the reference's per-miss reads of the stored planes
+ * (tensor_engine.cpp:380-417, pread into pinned docks). */
+enum { ZMOE_STORE_DEVICE = 0, ZMOE_STORE_HOST = 1 };
+zmoe_status zmoe_layer_set_store(zmoe_layer* layer, int where);
 /* Decode the given experts into free cache slots now. */
 zmoe_status zmoe_layer_warm_cache(zmoe_layer* layer, const int* experts, int n, zmoe_stream_t stream);
 /* x, out: device [T, H] BF16.  Synchronises once on the stream to read the

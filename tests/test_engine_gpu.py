@@ -103,6 +103,27 @@ def test_engine_forward_host_matches_device():
     assert torch.equal(d, oh)
 
 
+def test_engine_host_store_matches_device_store():
+    # compressed experts in pinned host memory, copied in per decode: the same
+    # outputs as the HBM store, over several forwards with misses and evictions
+    from zmoe.layer import MoELayer
+    s = QWEN_SMALL
+    L, w, wr, sg, sh = _build(s, 2)
+    Lh = MoELayer(s, max_tokens=64, cache_slots=2, store="host")
+    Lh.set_router(wr, None, sg)
+    Lh.set_shared(*sh)
+    Lh.load_experts(w, num_file_chunks=3)
+    for i in range(4):
+        x = syn.activations(16 + 8 * i, s.hidden, seed=40 + i).cuda()
+        assert torch.equal(L(x), Lh(x))
+    st, sth = L.stats(), Lh.stats()
+    assert sth["misses"] == st["misses"] > 0
+    assert sth["host_copy_bytes"] > 0 and st["host_copy_bytes"] == 0
+    from zmoe._lib import ZmoeError, check, lib
+    with pytest.raises(ZmoeError):
+        check(lib.zmoe_layer_set_store(Lh._h, 0), "zmoe_layer_set_store")   # experts already loaded
+
+
 def test_engine_submit_host_pipeline_matches_device():
     # five steps with different inputs through the two staging slots; each
     # step's output lands in its own pinned buffer

@@ -26,7 +26,7 @@ zmoe_status launch_gather_rows(const void*, const int32_t*, int, int, void*, cud
 
 extern "C" {
 
-int zmoe_abi_version(void) { return 1; }
+int zmoe_abi_version(void) { return 2; }
 
 const char* zmoe_last_error(void) { return zmoe::g_err; }
 

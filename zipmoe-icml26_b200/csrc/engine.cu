@@ -32,8 +32,11 @@ zmoe_status launch_expert_ffn(const zmoe_ffn_args*, cudaStream_t);
 namespace {
 
 struct TensorStore {
-  // [LZ4 blocks, each 16-byte aligned][sign+mantissa plane][segment indexes]
+  // [LZ4 blocks, each 16-byte aligned][sign+mantissa plane][segment indexes],
+  // in device memory, or in pinned host memory for a host-tier layer
   uint8_t* dev = nullptr;
+  uint8_t* host = nullptr;
+  bool loaded() const { return dev || host; }
   std::vector<uint32_t> block_off, block_size, orig_size;
   std::vector<uint64_t> idx_off;   // byte offset of each block's index
   std::vector<uint32_t> idx_n;     // entries of each block's index
@@ -106,6 +109,9 @@ struct Layer {
   int max_desc = 0, max_waves = 0;
   int desc_cursor = 0;             // descriptors used by the current forward
   uint32_t* map_scratch = nullptr; // decoder source-map scratch (zmoe_decode_scratch_bytes per chunk)
+  bool host_store = false;         // compressed experts in pinned host memory, copied in per miss
+  uint8_t* stage_buf = nullptr;    // host tier: device copies of the compressed tensors being decoded
+  uint64_t stage_cap = 0;
   uint64_t map_cap = 0;            // bytes of map_scratch
   int pending_status = 0;          // descriptors whose status is still to be checked
   // host-side pass-through buffers for forward_host
@@ -149,7 +155,8 @@ struct Layer {
 
 Layer::~Layer() {
   for (auto& e : store)
-    for (auto& t : e) cudaFree(t.dev);
+    for (auto& t : e) { cudaFree(t.dev); cudaFreeHost(t.host); }
+  cudaFree(stage_buf);
   cudaFree(slots);
   cudaFree(w_router); cudaFree(bias); cudaFree(w_sgate);
   for (auto* p : w_shared) cudaFree(p);
@@ -313,9 +320,34 @@ zmoe_status Layer::check_status() {
 zmoe_status Layer::decode_into(const std::vector<std::pair<int, int>>& jobs, cudaStream_t s, int wave) {
   const int base = desc_cursor;
   int nd = base;
+  // host tier: each tensor's packed buffer is copied into the staging area
+  // ahead of the decode (stream order keeps the previous decode's reads of the
+  // area before these copies)
+  if (host_store) {
+    uint64_t need = 0;
+    for (auto [e, slot] : jobs)
+      for (int t = 0; t < tensors; ++t) need += store[e][t].bytes;
+    if (need > stage_cap) {
+      ZMOE_CUDA_RET(cudaStreamSynchronize(s));
+      cudaFree(stage_buf);
+      stage_buf = nullptr;
+      stage_cap = 0;
+      ZMOE_CUDA_RET(cudaMalloc(&stage_buf, need));
+      stage_cap = need;
+    }
+  }
+  uint64_t stage_off = 0;
   for (auto [e, slot] : jobs) {
     for (int t = 0; t < tensors; ++t) {
       const TensorStore& ts = store[e][t];
+      const uint8_t* buf = ts.dev;
+      if (host_store) {
+        uint8_t* at = stage_buf + stage_off;           // offsets stay 16-byte aligned (bytes is)
+        ZMOE_CUDA_RET(cudaMemcpyAsync(at, ts.host, ts.bytes, cudaMemcpyHostToDevice, s));
+        stats.host_copy_bytes += ts.bytes;
+        stage_off += ts.bytes;
+        buf = at;
+      }
       uint64_t e0 = 0;
       uint16_t* dst = slot_ptr(slot, t);
       for (size_t c = 0; c < ts.block_off.size(); ++c) {
@@ -324,12 +356,12 @@ zmoe_status Layer::decode_into(const std::vector<std::pair<int, int>>& jobs, cud
           return ZMOE_EUNSUPPORTED;
         }
         zmoe_chunk& d = desc_host[nd++];
-        d.src = ts.dev + ts.block_off[c];
-        d.sm = ts.dev + ts.sm_off + e0;
+        d.src = buf + ts.block_off[c];
+        d.sm = buf + ts.sm_off + e0;
         d.dst = dst + e0;
         d.src_size = ts.block_size[c];
         d.out_size = ts.orig_size[c];
-        d.index = reinterpret_cast<const uint32_t*>(ts.dev + ts.idx_off[c]);
+        d.index = reinterpret_cast<const uint32_t*>(buf + ts.idx_off[c]);
         d.n_index = ts.idx_n[c];
         d.seg_bytes = kSegBytes;
         d.map = nullptr;                     // assigned below, one scratch area per chunk
@@ -503,7 +535,7 @@ zmoe_status Layer::experts(const uint16_t* xrows, const int32_t* counts_h, int r
   ZMOE_CHECK_ARG(sum == rows, "experts: counts sum to %lld, rows=%d", sum, rows);
   for (int e = 0; e < E; ++e)
     for (int t = 0; t < tensors; ++t)
-      ZMOE_CHECK_ARG(store[e][t].dev, "experts: expert %d tensor %d not loaded", e, t);
+      ZMOE_CHECK_ARG(store[e][t].loaded(), "experts: expert %d tensor %d not loaded", e, t);
   zmoe_status st;
   // Host buffers of the previous call: its pinned offsets copy, its decode
   // descriptors and status (status_ready comes after both on the stream).
@@ -538,7 +570,7 @@ zmoe_status Layer::forward(const uint16_t* x, int T, uint16_t* out, cudaStream_t
   const int E = cfg.num_experts, k = cfg.topk, H = cfg.hidden;
   for (int e = 0; e < E; ++e)
     for (int t = 0; t < tensors; ++t)
-      ZMOE_CHECK_ARG(store[e][t].dev, "forward: expert %d tensor %d not loaded", e, t);
+      ZMOE_CHECK_ARG(store[e][t].loaded(), "forward: expert %d tensor %d not loaded", e, t);
   if (T == 0) return ZMOE_OK;
   zmoe_status st;
 
@@ -721,10 +753,16 @@ zmoe_status zmoe_layer_load_expert(zmoe_layer* layer, int expert, int tensor, co
   for (int c = 0; c < n_chunks; ++c) memcpy(host.data() + ts.block_off[c], blocks[c], block_sizes[c]);
   memcpy(host.data() + ts.sm_off, sm, numel);
   for (int c = 0; c < n_chunks; ++c) memcpy(host.data() + ts.idx_off[c], idx[c].data(), idx[c].size() * 4);
-  zmoe_status st = upload((void**)&ts.dev, host.data(), ts.bytes);
-  if (st != ZMOE_OK) return st;
+  if (L->host_store) {
+    ZMOE_CUDA_RET(cudaHostAlloc((void**)&ts.host, ts.bytes, cudaHostAllocDefault));
+    memcpy(ts.host, host.data(), ts.bytes);
+  } else {
+    zmoe_status st = upload((void**)&ts.dev, host.data(), ts.bytes);
+    if (st != ZMOE_OK) return st;
+  }
   auto& slot = L->store[expert][tensor];
   cudaFree(slot.dev);
+  cudaFreeHost(slot.host);
   L->stats.store_bytes += ts.bytes - slot.bytes;
   slot = std::move(ts);
   // a re-loaded expert must be decoded again
@@ -732,6 +770,16 @@ zmoe_status zmoe_layer_load_expert(zmoe_layer* layer, int expert, int tensor, co
     L->slot_owner[L->expert_slot[expert]] = -1;
     L->expert_slot[expert] = -1;
   }
+  return ZMOE_OK;
+}
+
+zmoe_status zmoe_layer_set_store(zmoe_layer* layer, int where) {
+  Layer* L = reinterpret_cast<Layer*>(layer);
+  ZMOE_CHECK_ARG(L, "set_store: null pointer");
+  ZMOE_CHECK_ARG(where == ZMOE_STORE_DEVICE || where == ZMOE_STORE_HOST, "set_store: unknown store %d", where);
+  for (auto& e : L->store)
+    for (auto& t : e) ZMOE_CHECK_ARG(!t.loaded(), "set_store: experts are already loaded");
+  L->host_store = where == ZMOE_STORE_HOST;
   return ZMOE_OK;
 }
 
@@ -744,7 +792,7 @@ zmoe_status zmoe_layer_warm_cache(zmoe_layer* layer, const int* experts, int n, 
     const int e = experts[i];
     ZMOE_CHECK_ARG(e >= 0 && e < L->cfg.num_experts, "warm_cache: expert %d out of range", e);
     for (int t = 0; t < L->tensors; ++t)
-      ZMOE_CHECK_ARG(L->store[e][t].dev, "warm_cache: expert %d not loaded", e);
+      ZMOE_CHECK_ARG(L->store[e][t].loaded(), "warm_cache: expert %d not loaded", e);
     if (L->expert_slot[e] >= 0) continue;
     int slot = -1;
     for (int s2 = 0; s2 < L->n_cache; ++s2)
@@ -774,7 +822,7 @@ zmoe_status zmoe_layer_prefetch(zmoe_layer* layer, const int* experts, int n, zm
   for (int i = 0; i < n; ++i) {
     ZMOE_CHECK_ARG(experts[i] >= 0 && experts[i] < E, "prefetch: expert %d out of range", experts[i]);
     for (int t = 0; t < L->tensors; ++t)
-      ZMOE_CHECK_ARG(L->store[experts[i]][t].dev, "prefetch: expert %d not loaded", experts[i]);
+      ZMOE_CHECK_ARG(L->store[experts[i]][t].loaded(), "prefetch: expert %d not loaded", experts[i]);
     keep[experts[i]] = 1;
   }
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);

@@ -64,7 +64,8 @@ class LayerStats(ctypes.Structure):
     _fields_ = [(n, ctypes.c_uint64) for n in (
         "forwards", "tokens", "hits", "misses", "evictions", "decoded_experts", "decoded_chunks",
         "decoded_bytes", "decode_launches", "launches", "decode_errors", "store_bytes",
-        "decode_ns", "decode_timed_bytes", "decode_timed_launches", "ffn_ns", "ffn_timed_launches")]
+        "decode_ns", "decode_timed_bytes", "decode_timed_launches", "ffn_ns", "ffn_timed_launches",
+        "host_copy_bytes")]
 
 
 # (name, restype, argtypes) of every exported symbol; tests check the header
@@ -93,6 +94,7 @@ SIGNATURES = {
                                        ctypes.POINTER(c_u32), ctypes.POINTER(c_u32), c_int, c_void_p,
                                        ctypes.c_uint64]),
     "zmoe_layer_warm_cache": (c_int, [c_void_p, ctypes.POINTER(c_int), c_int, c_void_p]),
+    "zmoe_layer_set_store": (c_int, [c_void_p, c_int]),
     "zmoe_layer_forward": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p]),
     "zmoe_layer_experts": (c_int, [c_void_p, c_void_p, ctypes.POINTER(ctypes.c_int32), c_int, c_void_p, c_void_p]),
     "zmoe_layer_forward_host": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p]),

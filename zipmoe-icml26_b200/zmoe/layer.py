@@ -17,6 +17,7 @@ from ._lib import LayerConfig, LayerStats, check, lib
 from .synthetic import LayerShape
 
 POLICIES = {"ZipMoE": 0, "LFU": 1, "LRU": 2, "FIFO": 3}
+STORES = {"device": 0, "host": 1}
 
 
 def route_mode(s: LayerShape) -> int:
@@ -27,7 +28,7 @@ def route_mode(s: LayerShape) -> int:
 
 class MoELayer:
     def __init__(self, shape: LayerShape, max_tokens: int, cache_slots: int, transient_slots: int = 0,
-                 policy: str = "ZipMoE", state_margin: float = 0.1, device: int = 0):
+                 policy: str = "ZipMoE", state_margin: float = 0.1, device: int = 0, store: str = "device"):
         self.shape = shape
         self.device = torch.device("cuda", device)
         torch.cuda.set_device(self.device)
@@ -37,6 +38,10 @@ class MoELayer:
         h = ctypes.c_void_p()
         check(lib.zmoe_layer_create(ctypes.byref(cfg), ctypes.byref(h)), "zmoe_layer_create")
         self._h = h
+        if store not in STORES:
+            raise ValueError(f"store must be one of {sorted(STORES)}")
+        # "host": compressed experts in pinned host memory, copied in per miss
+        check(lib.zmoe_layer_set_store(h, STORES[store]), "zmoe_layer_set_store")
         self.max_tokens = max_tokens
 
     def close(self):
