@@ -28,7 +28,9 @@ import statistics
 import subprocess
 import sys
 import tempfile
+import threading
 import time
+from typing import Optional
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 PKG = os.path.join(ROOT, "zipmoe-icml26_b200")
@@ -75,20 +77,67 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle-reason samples during the timed region (one
-    GPU; inactive when index is None, so that only one rank polls the driver)."""
+    """SM clock / throttle-reason samples during the timed region, on one GPU
+    (inactive when index is None, so that only one rank polls the driver).
+
+    index: the CUDA device.  Samples come from NVML on a thread, every 20 ms:
+    SM clock, max SM clock and the clock-event reasons, nothing more, since a
+    heavier query (power, the full reason list of nvidia-smi) can hold the
+    driver long enough to delay the step's own synchronisations, and in
+    expert-parallel steps every rank then waits at the next collective.  The
+    GPU is found by its UUID, so NVML's numbering cannot point at another one.
+    Without NVML, nvidia-smi does the sampling."""
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+    PERIOD_S = 0.02
 
-    def __init__(self, index: int):
+    def __init__(self, index: Optional[int]):
         self.index = index
-        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.rows = []            # (sm_mhz, sm_max_mhz, [active flags in NAMES order])
         self.p = None
+        self.thread = None
+        self.f = None
+
+    def _nvml_handle(self):
+        import pynvml
+        pynvml.nvmlInit()
+        uid = str(torch.cuda.get_device_properties(self.index).uuid)
+        for key in (uid, "GPU-" + uid):
+            try:
+                return pynvml, pynvml.nvmlDeviceGetHandleByUUID(key)
+            except pynvml.NVMLError:
+                continue
+        raise RuntimeError("no NVML device with UUID " + uid)
 
     def __enter__(self):
         if self.index is None:
             return self
+        try:
+            nv, h = self._nvml_handle()
+            bits = [nv.nvmlClocksEventReasonHwSlowdown, nv.nvmlClocksEventReasonHwThermalSlowdown,
+                    nv.nvmlClocksEventReasonSwThermalSlowdown, nv.nvmlClocksEventReasonSwPowerCap]
+            sm_max = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+            self.stop = threading.Event()
+
+            def sample():
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                self.rows.append((nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM), sm_max,
+                                  [bool(r & b) for b in bits]))
+
+            def loop():
+                while not self.stop.wait(self.PERIOD_S):
+                    sample()
+
+            sample()                                     # one sample as the timed region starts
+            self.thread = threading.Thread(target=loop, daemon=True)
+            self.thread.start()
+            self._end_sample = sample
+            return self
+        except Exception:
+            self.thread = None
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
         try:
             self.p = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
                                        "--format=csv,noheader,nounits", "-lms", "20"],
@@ -104,6 +153,10 @@ class ClockSampler:
         return self
 
     def __exit__(self, *a):
+        if self.thread is not None:
+            self.stop.set()
+            self.thread.join(timeout=5)
+            self._end_sample()                           # and one as it ends
         if self.p is not None:
             self.p.terminate()
             try:
@@ -113,28 +166,28 @@ class ClockSampler:
 
     def summary(self):
         if self.index is None:
-            os.unlink(self.f.name)
             return None
-        self.f.flush()
-        rows = []
-        with open(self.f.name) as fh:
-            fh.seek(getattr(self, "start_size", 0))
-            lines = fh.readlines()
-        for line in lines:
-            parts = [x.strip() for x in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                rows.append((float(parts[1]), float(parts[2]), parts[5:9]))
-            except ValueError:
-                continue
-        os.unlink(self.f.name)
+        rows = list(self.rows)
+        if self.f is not None:
+            self.f.flush()
+            with open(self.f.name) as fh:
+                fh.seek(getattr(self, "start_size", 0))
+                lines = fh.readlines()
+            os.unlink(self.f.name)
+            for line in lines:
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    rows.append((float(parts[1]), float(parts[2]), [v.lower() == "active" for v in parts[5:9]]))
+                except ValueError:
+                    continue
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for _, _, r in rows for i, v in enumerate(r) if v.lower() == "active"})
+        reasons = sorted({self.NAMES[i] for _, _, r in rows for i, v in enumerate(r) if v})
         return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
-                "reasons": reasons, "samples": len(rows)}
+                "reasons": reasons, "samples": len(rows),
+                "source": "nvml" if self.f is None else "nvidia-smi"}
 
 
 def build_workload(args, device_index=0, threads=0):
