@@ -28,7 +28,6 @@ import statistics
 import subprocess
 import sys
 import tempfile
-import threading
 import time
 from typing import Optional
 
@@ -77,117 +76,106 @@ def peaks():
 
 
 class ClockSampler:
-    """SM clock / throttle-reason samples during the timed region, on one GPU
-    (inactive when index is None, so that only one rank polls the driver).
+    """SM clock and throttle reasons around and during the timed region, on
+    one GPU (inactive when index is None, so that only one rank takes part).
 
-    index: the CUDA device.  Samples come from NVML on a thread, every 20 ms:
-    SM clock, max SM clock and the clock-event reasons, nothing more, since a
-    heavier query (power, the full reason list of nvidia-smi) can hold the
-    driver long enough to delay the step's own synchronisations, and in
-    expert-parallel steps every rank then waits at the next collective.  The
-    GPU is found by its UUID, so NVML's numbering cannot point at another one.
-    Without NVML, nvidia-smi does the sampling."""
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    During the region the clock is measured on the GPU itself: at five points
+    of the loop (probe()) a one-thread kernel on a side stream counts SM cycles
+    against the GPU's nanosecond timer for 100 us, next to the step's own
+    kernels.  The driver is not queried while steps run: an NVML or
+    nvidia-smi query stalls the host's synchronisations for milliseconds, and
+    in expert-parallel steps every rank then waits at the next collective (it
+    cost a third of the 2-GPU throughput).  The throttle reasons, the max
+    clock and one more clock reading come from NVML before the region (then
+    100 ms pass and the ranks meet at a barrier) and right after it (the GPU
+    found by UUID); without NVML they come from one nvidia-smi query at each
+    edge."""
     NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-    PERIOD_S = 0.02
+    Q = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    PROBE_NS = 100_000
 
     def __init__(self, index: Optional[int]):
         self.index = index
-        self.rows = []            # (sm_mhz, sm_max_mhz, [active flags in NAMES order])
-        self.p = None
-        self.thread = None
-        self.f = None
+        self.edges = []          # (sm_mhz, sm_max_mhz, [active flags in NAMES order]) before and after
+        self.probes = []
+        self.source = None
 
-    def _nvml_handle(self):
-        import pynvml
-        pynvml.nvmlInit()
-        uid = str(torch.cuda.get_device_properties(self.index).uuid)
-        for key in (uid, "GPU-" + uid):
+    def _edge(self):
+        try:
+            import pynvml
+            if self.source is None:
+                pynvml.nvmlInit()
+                uid = str(torch.cuda.get_device_properties(self.index).uuid)
+                self.h = None
+                for key in (uid, "GPU-" + uid):
+                    try:
+                        self.h = pynvml.nvmlDeviceGetHandleByUUID(key)
+                        break
+                    except pynvml.NVMLError:
+                        continue
+                if self.h is None:
+                    raise RuntimeError("no NVML device with UUID " + uid)
+                self.source = "nvml"
+            nv, h = pynvml, self.h
+            bits = [nv.nvmlClocksEventReasonHwSlowdown, nv.nvmlClocksEventReasonHwThermalSlowdown,
+                    nv.nvmlClocksEventReasonSwThermalSlowdown, nv.nvmlClocksEventReasonSwPowerCap]
+            r = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+            self.edges.append((nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM),
+                               nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM), [bool(r & b) for b in bits]))
+        except Exception:
+            self.source = "nvidia-smi"
             try:
-                return pynvml, pynvml.nvmlDeviceGetHandleByUUID(key)
-            except pynvml.NVMLError:
-                continue
-        raise RuntimeError("no NVML device with UUID " + uid)
+                line = subprocess.run(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                                       "--format=csv,noheader,nounits"], capture_output=True, text=True,
+                                      timeout=30).stdout.strip().splitlines()[0]
+                parts = [x.strip() for x in line.split(",")]
+                self.edges.append((float(parts[0]), float(parts[1]), [v.lower() == "active" for v in parts[2:6]]))
+            except Exception:
+                pass
 
     def __enter__(self):
         if self.index is None:
             return self
-        try:
-            nv, h = self._nvml_handle()
-            bits = [nv.nvmlClocksEventReasonHwSlowdown, nv.nvmlClocksEventReasonHwThermalSlowdown,
-                    nv.nvmlClocksEventReasonSwThermalSlowdown, nv.nvmlClocksEventReasonSwPowerCap]
-            sm_max = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
-            self.stop = threading.Event()
-
-            def sample():
-                r = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
-                self.rows.append((nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM), sm_max,
-                                  [bool(r & b) for b in bits]))
-
-            def loop():
-                while not self.stop.wait(self.PERIOD_S):
-                    sample()
-
-            sample()                                     # one sample as the timed region starts
-            self.thread = threading.Thread(target=loop, daemon=True)
-            self.thread.start()
-            self._end_sample = sample
-            return self
-        except Exception:
-            self.thread = None
-        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
-        try:
-            self.p = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
-                                       "--format=csv,noheader,nounits", "-lms", "20"],
-                                      stdout=self.f, stderr=subprocess.DEVNULL)
-        except OSError:
-            self.p = None
-            return self
-        # the timed region is tens of milliseconds: start it once sampling runs
-        t0 = time.time()
-        while time.time() - t0 < 5.0 and os.path.getsize(self.f.name) == 0 and self.p.poll() is None:
-            time.sleep(0.01)
-        self.start_size = os.path.getsize(self.f.name)
+        self._edge()
+        time.sleep(0.1)          # driver work that a query starts can outlast the call
+        from zmoe._lib import lib
+        self.lib = lib
+        self.buf = torch.zeros(5, 2, dtype=torch.int64, device=torch.device("cuda", self.index))
+        self.side = torch.cuda.Stream(device=torch.device("cuda", self.index))
         return self
 
+    def probe(self, i: int, steps: int):
+        """Call before step i of steps: probes at 5 evenly spread steps."""
+        if self.index is None:
+            return
+        points = sorted({0, steps // 4, steps // 2, (3 * steps) // 4, max(steps - 1, 0)})
+        if i in points and len(self.probes) < 5:
+            slot = len(self.probes)
+            self.probes.append(slot)
+            st = self.lib.zmoe_clock_probe(self.buf[slot].data_ptr(), self.PROBE_NS, self.side.cuda_stream)
+            if st != 0:
+                self.probes.pop()
+
     def __exit__(self, *a):
-        if self.thread is not None:
-            self.stop.set()
-            self.thread.join(timeout=5)
-            self._end_sample()                           # and one as it ends
-        if self.p is not None:
-            self.p.terminate()
-            try:
-                self.p.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.p.kill()
+        if self.index is None:
+            return
+        torch.cuda.synchronize(self.index)
+        self._edge()
 
     def summary(self):
         if self.index is None:
             return None
-        rows = list(self.rows)
-        if self.f is not None:
-            self.f.flush()
-            with open(self.f.name) as fh:
-                fh.seek(getattr(self, "start_size", 0))
-                lines = fh.readlines()
-            os.unlink(self.f.name)
-            for line in lines:
-                parts = [x.strip() for x in line.split(",")]
-                if len(parts) < 9:
-                    continue
-                try:
-                    rows.append((float(parts[1]), float(parts[2]), [v.lower() == "active" for v in parts[5:9]]))
-                except ValueError:
-                    continue
-        if not rows:
+        got = self.buf[: len(self.probes)].cpu().tolist() if self.probes else []
+        mhz = [c * 1000.0 / ns for c, ns in got if ns > 0]
+        if not mhz and not self.edges:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
-        reasons = sorted({self.NAMES[i] for _, _, r in rows for i, v in enumerate(r) if v})
-        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
-                "reasons": reasons, "samples": len(rows),
-                "source": "nvml" if self.f is None else "nvidia-smi"}
+        reasons = sorted({self.NAMES[i] for _, _, r in self.edges for i, v in enumerate(r) if v})
+        return {"sm_mhz": round(statistics.median(mhz), 1) if mhz else statistics.median(e[0] for e in self.edges),
+                "sm_max_mhz": max((e[1] for e in self.edges), default=None), "reasons": reasons,
+                "samples": len(mhz),
+                "edge_sm_mhz": [e[0] for e in self.edges],
+                "source": f"SM cycles / GPU timer on the GPU during the loop; {self.source} at its edges"}
 
 
 def build_workload(args, device_index=0, threads=0):
@@ -284,11 +272,12 @@ def run_ours(args):
     L.sync()
     L.reset_stats()
     L.set_timing(True)
-    barrier()
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
+    with ClockSampler(local) as clk:          # its first driver reading comes before the barrier
+        barrier()
         start.record(stream)
-        for _ in range(args.steps):
+        for i in range(args.steps):
+            clk.probe(i, args.steps)
             L.forward(x, out)
         stop.record(stream)
         torch.cuda.synchronize()
@@ -413,11 +402,12 @@ def run_ep(args):
     eng.sync()
     eng.reset_stats()
     eng.set_timing(True)
-    barrier()
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local if rank == 0 else None) as clk:
+    with ClockSampler(local if rank == 0 else None) as clk:   # first driver reading before the barrier
+        barrier()
         start.record(stream)
-        for _ in range(args.steps):
+        for i in range(args.steps):
+            clk.probe(i, args.steps)
             L(x)
         stop.record(stream)
         torch.cuda.synchronize()

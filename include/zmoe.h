@@ -43,6 +43,13 @@ enum {
 /* Version of this ABI. */
 int zmoe_abi_version(void);
 
+/* Average SM clock over a window, measured on the GPU by one thread: out is a
+ * device array of 2 uint64, receiving the SM cycles counted and the
+ * nanoseconds elapsed (MHz = out[0] * 1000 / out[1]).  Runs on `stream` next
+ * to other work, so a benchmark can record the clock under load without a
+ * driver query.  No counterpart in the reference. */
+zmoe_status zmoe_clock_probe(uint64_t* out, uint64_t window_ns, zmoe_stream_t stream);
+
 /* Human-readable text of the last error recorded on the calling thread. */
 const char* zmoe_last_error(void);
 

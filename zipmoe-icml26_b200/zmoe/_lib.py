@@ -73,6 +73,7 @@ class LayerStats(ctypes.Structure):
 SIGNATURES = {
     "zmoe_abi_version": (c_int, []),
     "zmoe_last_error": (ctypes.c_char_p, []),
+    "zmoe_clock_probe": (c_int, [c_void_p, ctypes.c_uint64, c_void_p]),
     "zmoe_tensor_recover": (c_int, [c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
     "zmoe_decode_chunks": (c_int, [c_void_p, c_int, c_void_p, c_void_p]),
     "zmoe_decode_scratch_bytes": (ctypes.c_uint64, [c_u32]),
