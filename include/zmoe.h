@@ -327,7 +327,8 @@ zmoe_status zmoe_layer_experts(zmoe_layer* layer, const uint16_t* x_rows, const 
 /* Same with host buffers (pinned for full speed); returns after out_host is written. */
 zmoe_status zmoe_layer_forward_host(zmoe_layer* layer, const uint16_t* x_host, int T, uint16_t* out_host,
                                     zmoe_stream_t stream);
-/* Pipelined form of zmoe_layer_forward_host: queues the input copy, the
+/* Pipelined form of zmoe_layer_forward_host (no counterpart in the
+ * reference, whose layer runs synchronously per call): queues the input copy, the
  * forward on `stream` and the output copy, and returns once the forward is
  * launched (it waits only for this step's expert counts, like
  * zmoe_layer_forward).  Copies run on the layer's own copy streams through two
