@@ -5,9 +5,11 @@ The port keeps the reference's arithmetic order, so results must be equal,
 not just close."""
 import json
 import os
+import tempfile
 
 import numpy as np
 import pytest
+import torch
 
 from zmoe import cache_planning as cp
 
@@ -52,6 +54,10 @@ def test_plan_cache_matches_reference(cases):
         assert cp.obtain_dist_from_trace(a["batch_size"], c["trace"]) == c["dist"]
         ratio, feasible = cp.plan_cache(c["trace"], total_memory=c["total_memory"], **a)
         assert (ratio, feasible) == (c["ratio"], c["feasible"])
+        # the reference's own call (runtime/model_offload.py:102-116) passes keywords and a file
+        with tempfile.NamedTemporaryFile(suffix=".pt") as f:
+            torch.save(c["trace"], f.name)
+            assert cp.PlanCache(trace_path=f.name, total_memory=c["total_memory"], **a) == (ratio, feasible)
 
 
 def test_coverage_to_weight_rejects_wrong_sum():

@@ -28,6 +28,7 @@ GPU 0, so the planner runs without a GPU.
 """
 from __future__ import annotations
 
+import os
 from collections import Counter
 from typing import List, Optional, Sequence, Tuple
 
@@ -143,14 +144,15 @@ def cache_pool_planning_simu(k, num_experts, num_sparse_layers, tensors_per_expe
     return ratios[int(np.argmin(smooth))], feasible
 
 
-def obtain_dist_from_trace(batch_size: int, trace) -> List[float]:
-    """Popularity curve from a routing trace: trace[prompt][layer][expert] =
-    invocation count (or a path torch.load reads it from).  Per batch of
+def obtain_dist_from_trace(batch_size: int, trace_path) -> List[float]:
+    """Popularity curve from a routing trace: trace_path is a file torch.load
+    reads, or the trace itself, trace[prompt][layer][expert] = invocation count.  Per batch of
     prompts and per layer the summed counts are sorted in decreasing order;
     the curves of all layers and batches are summed and normalised to 1
     (a trailing partial batch is dropped); sums run in the reference's order.
     ObtainDistFromTrace (runtime/cache_planning.py:142-162)."""
-    if isinstance(trace, str):
+    trace = trace_path
+    if isinstance(trace, (str, bytes, os.PathLike)):
         import torch
         trace = torch.load(trace, map_location="cpu")
     t = np.asarray(trace)
@@ -236,15 +238,15 @@ def weight_to_prob(weight: Sequence[float]) -> List[float]:
     return [w / (1 + w) for w in weight]
 
 
-def plan_cache(trace, batch_size, k, num_experts, num_sparse_layers, tensors_per_expert, num_elements_per_tensor,
+def plan_cache(trace_path, batch_size, k, num_experts, num_sparse_layers, tensors_per_expert, num_elements_per_tensor,
                compression_ratio, num_file_chunks, compute_pool_size, device_memory_ratio, decompression_delay,
                SM_IO_delay, step_size=0.05, synthetic=False, total_memory: Optional[int] = None
                ) -> Tuple[float, bool]:
-    """gpu_pool_ratio for zipmoe_prefetch_handle from a routing trace (a path
-    or a [prompts][layers][experts] count array), and whether the budget
+    """gpu_pool_ratio for zipmoe_prefetch_handle from a routing trace
+    (trace_path: a file, or the [prompts][layers][experts] count array itself), and whether the budget
     allows a split at all (0.99 when it does not).  PlanCache
     (runtime/cache_planning.py:264-303)."""
-    curve = obtain_dist_from_trace(batch_size, trace)
+    curve = obtain_dist_from_trace(batch_size, trace_path)
     target = scale_to_k(curve, k)
     probs = weight_to_prob(coverage_to_weight(target, k))
     avg_k = int(np.sum(probs))
