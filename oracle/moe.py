@@ -28,7 +28,7 @@ Defined orders (the reference's own order is whatever cuBLAS/MKL pick):
 from __future__ import annotations
 
 from dataclasses import dataclass, field
-from typing import List, Optional
+from typing import Optional
 
 import numpy as np
 import torch

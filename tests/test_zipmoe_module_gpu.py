@@ -2,7 +2,6 @@
 offload experts to the reference file format, register them with the
 expert_dispatcher, run experts/expert_executor.py's dispatch_local sequence and
 compare every expert output with the oracle FFN."""
-import numpy as np
 import pytest
 import torch
 
