@@ -202,13 +202,44 @@ def cpu_reference_layer(s, enc, extra, threads):
     return ReferenceCPULayer(shapes, enc, wr, bias, sg, sh, s.topk, warm, threads=threads)
 
 
+def cpu_model() -> str:
+    """Host CPU model name (lscpu "Model name", else /proc/cpuinfo)."""
+    try:
+        out = subprocess.run(["lscpu"], capture_output=True, text=True, timeout=10).stdout
+        for ln in out.splitlines():
+            if ln.strip().lower().startswith("model name"):
+                return ln.split(":", 1)[1].strip()
+    except Exception:
+        pass
+    try:
+        for ln in open("/proc/cpuinfo"):
+            if ln.lower().startswith("model name"):
+                return ln.split(":", 1)[1].strip()
+    except Exception:
+        pass
+    return "unknown"
+
+
+def bench_config(args, s, world):
+    """The workload as both arms print it (the same dict, so the lines compare)."""
+    return {"workload": "qwen1.5-moe-layer", "tokens_per_gpu": args.tokens, "hidden": s.hidden,
+            "experts": s.num_experts, "inter": s.inter, "topk": s.topk, "shared_inter": s.shared_inter,
+            "cached_experts": args.cache, "codec": f"{args.codec}-{args.level}",
+            "num_file_chunks": args.chunks, "zipf_s": s.zipf_s,
+            "parallelism": f"ep{world}" if world > 1 else "single", "store": args.store,
+            "l2": "inputs larger than L2 (decoded + compressed experts > 1 GB)"}
+
+
 def run_reference(args):
-    """CPU reference path (oracle port) on the host cores; prints the reference line."""
+    """The reference's CPU path (oracle port: liblz4 + torch CPU) on the host
+    cores; prints the reference line.  Nothing of this repository's library is
+    loaded in this process: the experts are encoded by the oracle's liblz4
+    bindings too."""
     world, rank, _ = dist_env()
     if rank != 0:
         return
-    from zmoe import synthetic as syn
-    from zmoe import codec as zc
+    from oracle import codec as oc
+    from zmoe import synthetic as syn      # pure Python: seeded tensors, no native code
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     s = syn.QWEN
@@ -216,7 +247,7 @@ def run_reference(args):
     wr, sg = syn.router_weights(s)
     sh = syn.shared_weights(s)
     bias = syn.zipf_bias(s, 0)
-    flat = zc.encode_tensors([t for e in w for t in e], args.chunks, args.codec, args.level, threads)
+    flat = oc.encode_tensors([t for e in w for t in e], args.chunks, args.codec, args.level, threads)
     enc = [flat[i * 3:(i + 1) * 3] for i in range(s.num_experts)]
     warm = syn.popularity_order(s, 0)[: args.cache]
     L = cpu_reference_layer(s, enc, (wr, bias, sg, sh, warm), threads)
@@ -232,11 +263,10 @@ def run_reference(args):
     v = args.tokens / dt
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "qwen1.5-moe-layer", "tokens": args.tokens, "hidden": s.hidden,
-                       "experts": s.num_experts, "topk": s.topk, "cached_experts": args.cache,
-                       "codec": f"{args.codec}-{args.level}", "num_file_chunks": args.chunks},
-            "cpu_baseline": {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations)",
+            "config": bench_config(args, s, world),
+            "cpu_baseline": {"value": v, "unit": UNIT, "cores": threads, "cpu_model": cpu_model(), "kind": "port",
                              "sample": f"{args.steps} full {args.tokens}-token layer steps: liblz4 decode of "
                                        f"{st['misses']} missed experts on {threads} threads + torch CPU BF16 layer"},
             "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -333,13 +363,7 @@ def run_ours(args):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations)",
-            "config": {"workload": "qwen1.5-moe-layer", "tokens_per_gpu": args.tokens, "hidden": s.hidden,
-                       "experts": s.num_experts, "inter": s.inter, "topk": s.topk, "shared_inter": s.shared_inter,
-                       "cached_experts": args.cache, "codec": f"{args.codec}-{args.level}",
-                       "num_file_chunks": args.chunks, "zipf_s": s.zipf_s,
-                       "parallelism": "replicas" if world > 1 else "single",
-                       "store": args.store,
-                       "l2": "inputs larger than L2 (decoded + compressed experts > 1 GB)"},
+            "config": bench_config(args, s, world),
             "e2e": {"value": world * args.tokens / (e2e_ms / 1e3), "unit": UNIT,
                     "h2d_bytes_per_step": x.numel() * 2, "d2h_bytes_per_step": x.numel() * 2},
             "roofline": {"bound": "hbm", "kernel": "map_kernel+resolve_kernel (fused LZ4 decode)", "achieved": achieved,
@@ -452,13 +476,9 @@ def run_ep(args):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations)",
-            "config": {"workload": "qwen1.5-moe-layer", "tokens_per_gpu": args.tokens, "hidden": s.hidden,
-                       "experts": s.num_experts, "inter": s.inter, "topk": s.topk, "shared_inter": s.shared_inter,
-                       "cached_experts": args.cache, "cached_experts_rank0": cache,
-                       "experts_rank0": len(mine), "codec": f"{args.codec}-{args.level}",
-                       "num_file_chunks": args.chunks, "zipf_s": s.zipf_s, "parallelism": f"ep{world}",
-                       "exchange": "NCCL all-to-all (counts, BF16 rows out, fp32 rows back)",
-                       "l2": "inputs larger than L2 (decoded + compressed experts > 1 GB)"},
+            "config": bench_config(args, s, world),
+            "ep": {"cached_experts_rank0": cache, "experts_rank0": len(mine),
+                   "exchange": "NCCL all-to-all (counts, BF16 rows out, fp32 rows back)"},
             "e2e": {"value": world * args.tokens / (e2e_ms / 1e3), "unit": UNIT,
                     "h2d_bytes_per_step": x.numel() * 2, "d2h_bytes_per_step": x.numel() * 2},
             "roofline": {"bound": "hbm", "kernel": "map_kernel+resolve_kernel (fused LZ4 decode)", "achieved": achieved,
@@ -492,7 +512,7 @@ def cpu_baseline(args, s, enc, extra):
         n += 1
     dt = (time.perf_counter() - t0) / n
     L.close()
-    return {"value": args.tokens / dt, "unit": UNIT, "cores": threads, "kind": "port",
+    return {"value": args.tokens / dt, "unit": UNIT, "cores": threads, "cpu_model": cpu_model(), "kind": "port",
             "sample": f"{n} full {args.tokens}-token layer steps ({st['misses']} misses decoded by liblz4 on "
                       f"{threads} threads, torch CPU BF16 experts)"}
 

@@ -28,7 +28,8 @@ typedef enum zmoe_status {
   ZMOE_ECUDA = 2,       /* a CUDA runtime call failed */
   ZMOE_EUNSUPPORTED = 3,/* shape outside what the kernels implement */
   ZMOE_ENOMEM = 4,
-  ZMOE_ENCCL = 5
+  ZMOE_ENCCL = 5,
+  ZMOE_EKERNEL = 6      /* a kernel gave up a bounded wait: that call's outputs are incomplete */
 } zmoe_status;
 
 /* Per-chunk decode status written by zmoe_decode_chunks. */
@@ -52,6 +53,20 @@ zmoe_status zmoe_clock_probe(uint64_t* out, uint64_t window_ns, zmoe_stream_t st
 
 /* Human-readable text of the last error recorded on the calling thread. */
 const char* zmoe_last_error(void);
+
+/* Device-wide error word of the tcgen05 expert-FFN kernels on the current
+ * device: 0, or 1 once a launch gave up one of its bounded mbarrier waits
+ * (it then drained its own copies, freed its TMEM and returned, leaving its
+ * outputs incomplete).  Synchronous; reset != 0 clears the word after reading.
+ * No counterpart in the reference, whose libtorch FFN has no device waits. */
+zmoe_status zmoe_kernel_error(int32_t* code, int reset);
+/* Test hook for the error path above (no counterpart in the reference): later
+ * expert-FFN launches from this process use wait_cycles (clock64 cycles; <= 0
+ * restores the default of about 2 s) as their wait limit, and with
+ * drop_loads != 0 their TMA producer issues no loads, so that the first MMA
+ * wait runs out and the launch returns through the error path.  Nothing
+ * faults or hangs: every wait stays bounded. */
+zmoe_status zmoe_debug_ffn_wait(long long wait_cycles, int drop_loads);
 
 /* --------------------------------------------------------------------------
  * Plane recombine.
@@ -178,7 +193,9 @@ zmoe_status zmoe_permute(const zmoe_permute_args* a, zmoe_stream_t stream);
  * ------------------------------------------------------------------------ */
 typedef struct zmoe_ffn_args {
   const uint16_t* x;          /* [rows, H] BF16 */
-  const uint16_t* const* w;   /* device array [G * 3] of weight pointers */
+  const uint16_t* const* w;   /* HOST array [G * 3] of device weight pointers (the launch builds one
+                                 TMA descriptor per matrix on the host); a group's pointers are all
+                                 set (w[1] may be NULL for kind 1) or all NULL (group skipped) */
   const int32_t* offsets;     /* [G + 1] device or NULL */
   int G, rows_total, H, I, kind;
   uint16_t* h;                /* [rows, I] BF16 scratch */
@@ -340,7 +357,10 @@ zmoe_status zmoe_layer_submit_host(zmoe_layer* layer, const uint16_t* x_host, in
 /* Makes `stream` wait (without blocking the host) until the output copies of
  * every submitted step have completed. */
 zmoe_status zmoe_layer_join_host(zmoe_layer* layer, zmoe_stream_t stream);
-/* Wait for the stream and report any decode error of earlier forwards. */
+/* Wait for the stream and report any decode error of earlier forwards
+ * (ZMOE_EINVAL) or an expert-FFN launch that gave up a wait (ZMOE_EKERNEL).
+ * zmoe_layer_forward and zmoe_layer_experts report both too, for earlier
+ * calls whose work has finished by then. */
 zmoe_status zmoe_layer_sync(zmoe_layer* layer, zmoe_stream_t stream);
 zmoe_status zmoe_layer_get_stats(const zmoe_layer* layer, zmoe_layer_stats* out);
 zmoe_status zmoe_layer_reset_stats(zmoe_layer* layer);

@@ -234,6 +234,48 @@ def encode_tensor(bits: np.ndarray, num_file_chunks: int = 3, codec: str = "LZ4H
     return blocks, [c.size for c in chunks], sm
 
 
+class Encoded:
+    """One tensor in the reference's storage form (blocks, original sizes, sm bytes)."""
+
+    def __init__(self, shape, blocks, original_sizes, sm: bytes):
+        self.shape = tuple(shape)
+        self.blocks = blocks
+        self.original_sizes = list(original_sizes)
+        self.sm = sm
+
+    @property
+    def numel(self) -> int:
+        return sum(self.original_sizes)
+
+
+def encode_tensors(tensors, num_file_chunks: int = 3, codec: str = "LZ4HC", level: int = 9,
+                   threads: int = 0) -> List[Encoded]:
+    """encode_tensor over many BF16 tensors, one chunk per task on a thread pool
+    (the reference compresses on its compute pool, tensor_engine.cpp:223-301);
+    ctypes releases the GIL inside each liblz4 call."""
+    from concurrent.futures import ThreadPoolExecutor
+    planes = []
+    for t in tensors:
+        exp, sm = split_planes(bf16_bits(t))
+        planes.append((tuple(t.shape), chunk_exponents(exp, num_file_chunks), sm))
+    jobs = [c for _, chunks, _ in planes for c in chunks]
+
+    def one(c):
+        if codec == "LZ4HC":
+            return lz4_compress_hc(c, level)
+        if codec == "LZ4":
+            return lz4_compress_fast(c, level)
+        raise ValueError(f"unsupported codec {codec}")
+
+    with ThreadPoolExecutor(max_workers=threads or (os.cpu_count() or 1)) as ex:
+        blocks = list(ex.map(one, jobs))
+    out, pos = [], 0
+    for shape, chunks, sm in planes:
+        out.append(Encoded(shape, blocks[pos:pos + len(chunks)], [c.size for c in chunks], sm.tobytes()))
+        pos += len(chunks)
+    return out
+
+
 def decode_tensor(blocks: Sequence[bytes], original_sizes: Sequence[int], sm: np.ndarray) -> np.ndarray:
     """Reference CPU miss path: decode every chunk, concatenate, recombine."""
     exp = np.concatenate([lz4_decompress(b, o) for b, o in zip(blocks, original_sizes)])

@@ -295,6 +295,31 @@ def qwen_layer(x, w_gate, experts, shared, w_shared_gate, k=4, bias=None):
     return out.to(torch.bfloat16), r
 
 
+def qwen_layer_bf16(x, w_gate, experts, shared, w_shared_gate, k=4, bias=None, topk_idx=None, topk_w=None):
+    """customized/qwen.py:56-102 with the reference's own roundings: every
+    torch op in BF16 (expert_module.cpp:39-50 via swiglu_bf16_ref), the routed
+    outputs scaled by BF16 weights and added into a BF16 buffer in ascending
+    expert order (qwen.py:89-93), the shared expert scaled by a BF16 sigmoid
+    gate and added last (qwen.py:98-100).  topk_idx / topk_w, when given,
+    replace this module's routing (to replay a selection made elsewhere, e.g.
+    where the reference broke an exact tie differently).  Returns BF16 [T, H]."""
+    xb = x.to(torch.bfloat16)
+    r = route_qwen(xb, w_gate, k, bias=bias)
+    idx = r.topk_idx if topk_idx is None else np.asarray(topk_idx)
+    tw = torch.from_numpy(r.topk_w if topk_w is None else np.asarray(topk_w, dtype=F32)).to(torch.bfloat16)
+    T, H = xb.shape
+    out = torch.zeros(T, H, dtype=torch.bfloat16)
+    for e in range(len(experts)):
+        tok = np.nonzero((idx == e).any(axis=1))[0]
+        if tok.size == 0:
+            continue
+        y = swiglu_bf16_ref(xb[tok], *experts[e])
+        wsel = torch.stack([tw[t][list(idx[t]).index(e)] for t in tok])
+        out[tok] += y * wsel[:, None]
+    sh = swiglu_bf16_ref(xb, *shared)
+    return out + torch.sigmoid(F.linear(xb, w_shared_gate.to(torch.bfloat16))) * sh
+
+
 def deepseek_layer(x, w_gate, experts, shared, k=6, routed_scaling_factor=1.0, bias=None):
     """customized/deepseek.py:67-116 (shared experts added without a gate)."""
     xb = x.to(torch.bfloat16)

@@ -3,7 +3,7 @@
 Run in a container that has the reference checkout (it is read, never
 modified):
 
-    python tests/golden/make_golden.py /root/reference
+    python tests/golden/make_golden.py <path of the reference checkout>
 
 Fixtures:
 
@@ -11,6 +11,8 @@ Fixtures:
   ragged sizes, tiny sizes, random bit patterns), their exponent / sign+mantissa
   planes, their LZ4HC-9 and LZ4-fast chunk blocks produced by liblz4 (the
   reference codec library), and the bytes liblz4 decodes them back to.
+* ``qwen_block_c2.npz`` — the same for the reference's Qwen block at the full
+  Qwen1.5-MoE-A2.7B layer shape with the benchmark's seeded weights (64 tokens).
 * ``qwen_block.npz`` / ``deepseek_block.npz`` — inputs are regenerated from
   seeds by the tests; the fixture holds the outputs of the reference's own
   ``customized/qwen.py`` Qwen2MoEBlock and ``customized/deepseek.py``
@@ -205,6 +207,49 @@ def qwen_block(ref, tokens=24):
     print("qwen block:", tuple(y.shape))
 
 
+def qwen_block_c2(ref, tokens=64):
+    """The reference's Qwen2MoEBlock at the full Qwen1.5-MoE-A2.7B layer shape
+    (hidden 2048, 60 experts of intermediate 1408, top-4, shared expert 5632
+    with its sigmoid gate), with the seeded synthetic weights of the benchmark
+    (zmoe.synthetic: experts seed 0, router seed 2, shared seed 4) and 64
+    tokens (seed 21).  The reference block has no router bias, so none is
+    used here.  The output is stored as BF16 bit patterns."""
+    from transformers import Qwen2MoeConfig
+    mod = _load_qwen(ref)
+    s = syn.QWEN
+    cfg = Qwen2MoeConfig(hidden_size=s.hidden, num_experts=s.num_experts, num_experts_per_tok=s.topk,
+                         moe_intermediate_size=s.inter, shared_expert_intermediate_size=s.shared_inter,
+                         norm_topk_prob=False, hidden_act="silu")
+    blk = mod.Qwen2MoEBlock(cfg).to(torch.bfloat16).eval()
+    w = syn.expert_weights(s, 1)[0]
+    wr, sg = syn.router_weights(s)
+    sh = syn.shared_weights(s)
+    x = syn.activations(tokens, s.hidden, seed=21)
+    with torch.no_grad():
+        blk.gate.weight.copy_(wr)
+        blk.shared_expert_gate.weight.copy_(sg)
+        for e in range(s.num_experts):
+            blk.experts[e].gate_proj.weight.copy_(w[e][0])
+            blk.experts[e].up_proj.weight.copy_(w[e][1])
+            blk.experts[e].down_proj.weight.copy_(w[e][2])
+        blk.shared_expert.gate_proj.weight.copy_(sh[0])
+        blk.shared_expert.up_proj.weight.copy_(sh[1])
+        blk.shared_expert.down_proj.weight.copy_(sh[2])
+        blk.expert_executor = _CPUExecutor(blk)
+        blk.layer_id = 0
+        y = blk(x.view(1, tokens, s.hidden)).view(tokens, s.hidden)
+        logits = blk.gate(x)
+        rw = torch.softmax(logits, dim=1, dtype=torch.float)
+        tw, ti = torch.topk(rw, s.topk, dim=-1)
+    np.savez_compressed(os.path.join(HERE, "qwen_block_c2.npz"),
+                        out_bits=y.contiguous().view(torch.int16).numpy(),
+                        logits_bits=logits.contiguous().view(torch.int16).numpy(),
+                        topk_idx=ti.numpy().astype(np.int32),
+                        topk_w=tw.numpy(), input_digest=np.array(digest(x, wr, sg, *w[0], *w[-1], *sh)),
+                        tokens=np.array(tokens))
+    print("qwen block (C2 shape):", tuple(y.shape))
+
+
 def deepseek_block(ref, tokens=24):
     mod = _load_deepseek(ref)
     s = DEEPSEEK_SMALL
@@ -340,9 +385,17 @@ def cache_planning_cases(ref):
 
 
 if __name__ == "__main__":
-    ref = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    if len(sys.argv) < 2:
+        sys.exit("usage: make_golden.py <path of the reference checkout>")
+    ref = sys.argv[1]
+    only = sys.argv[2:]
+    if only:
+        for name in only:
+            globals()[name](ref) if name != "codec_cases" else codec_cases()
+        sys.exit(0)
     codec_cases()
     qwen_block(ref)
+    qwen_block_c2(ref)
     deepseek_block(ref)
     predictor_cases(ref)
     cache_planning_cases(ref)

@@ -21,7 +21,7 @@ def test_library_exports_header_symbols():
     missing = [s for s in syms if not hasattr(lib, s)]
     assert not missing, missing
     assert set(_lib.SIGNATURES) <= syms | {"zmoe_last_error", "zmoe_abi_version"}
-    assert lib.zmoe_abi_version() == 2
+    assert lib.zmoe_abi_version() == 3
 
 
 def test_struct_layouts_match_header():

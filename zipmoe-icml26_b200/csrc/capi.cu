@@ -19,16 +19,25 @@ zmoe_status launch_decode_chunks(const zmoe_chunk*, int, int32_t*, cudaStream_t)
 zmoe_status launch_router(const zmoe_router_args*, cudaStream_t);
 zmoe_status launch_permute(const zmoe_permute_args*, cudaStream_t);
 zmoe_status launch_combine(const zmoe_combine_args*, cudaStream_t);
-zmoe_status launch_expert_ffn(const zmoe_ffn_args*, cudaStream_t);
 zmoe_status launch_gather_rows(const void*, const int32_t*, int, int, void*, cudaStream_t);
 
 }  // namespace zmoe
 
 extern "C" {
 
-int zmoe_abi_version(void) { return 2; }
+int zmoe_abi_version(void) { return 3; }
 
 const char* zmoe_last_error(void) { return zmoe::g_err; }
+
+zmoe_status zmoe_kernel_error(int32_t* code, int reset) {
+  ZMOE_CHECK_ARG(code, "kernel_error: null pointer");
+  return zmoe::read_kernel_error(code, reset);
+}
+
+zmoe_status zmoe_debug_ffn_wait(long long wait_cycles, int drop_loads) {
+  zmoe::set_ffn_wait(wait_cycles, drop_loads);
+  return ZMOE_OK;
+}
 
 zmoe_status zmoe_tensor_recover(uint16_t* out, const uint8_t* exp, const uint8_t* sm, size_t n,
                                 zmoe_stream_t stream) {

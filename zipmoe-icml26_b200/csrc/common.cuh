@@ -42,6 +42,15 @@ inline zmoe_status launch_status(const char* what) {
 
 constexpr int kNumSMs = 148;
 
+// Grouped expert FFN (ffn_tc.cu).  err: optional device word that a kernel
+// whose bounded wait ran out sets to 1.
+zmoe_status launch_expert_ffn(const zmoe_ffn_args* a, cudaStream_t stream, int32_t* err = nullptr);
+// Device-wide error word of the FFN kernels on the current device.
+zmoe_status read_kernel_error(int32_t* out, int reset);
+// Error-path test hook: wait limit (cycles, <= 0 restores the default) and
+// whether the FFN's TMA producer issues nothing.
+void set_ffn_wait(long long cycles, int drop_loads);
+
 // BF16 bit pattern from a sign+mantissa byte and an exponent byte
 // (csrc/kernels/tensor_recover.cu:25-30).
 __device__ __forceinline__ uint32_t recombine(uint32_t sm, uint32_t e) {

@@ -27,7 +27,6 @@ zmoe_status launch_decode_chunks(const zmoe_chunk*, int, int32_t*, cudaStream_t)
 zmoe_status launch_router(const zmoe_router_args*, cudaStream_t);
 zmoe_status launch_permute(const zmoe_permute_args*, cudaStream_t);
 zmoe_status launch_combine(const zmoe_combine_args*, cudaStream_t);
-zmoe_status launch_expert_ffn(const zmoe_ffn_args*, cudaStream_t);
 
 namespace {
 
@@ -114,6 +113,14 @@ struct Layer {
   uint64_t stage_cap = 0;
   uint64_t map_cap = 0;            // bytes of map_scratch
   int pending_status = 0;          // descriptors whose status is still to be checked
+  // error word of this layer's FFN launches (set when a bounded wait ran out),
+  // copied back after each call and checked at the next one
+  int32_t* kerr_dev = nullptr;
+  int32_t* kerr_host = nullptr;
+  cudaEvent_t kerr_ready = nullptr;
+  bool kerr_pending = false;
+  zmoe_status queue_kernel_error_copy(cudaStream_t s);
+  zmoe_status check_kernel_error(bool wait);
   // host-side pass-through buffers for forward_host
   uint16_t* x_stage = nullptr;
   uint16_t* out_stage = nullptr;
@@ -166,6 +173,8 @@ Layer::~Layer() {
   cudaFree(offsets_ext); cudaFreeHost(offsets_host);
   cudaFreeHost(counts_host); cudaFreeHost(desc_host); cudaFreeHost(wtab_host); cudaFreeHost(status_host);
   cudaFree(x_stage); cudaFree(out_stage); cudaFree(map_scratch);
+  cudaFree(kerr_dev); cudaFreeHost(kerr_host);
+  if (kerr_ready) cudaEventDestroy(kerr_ready);
   cudaFree(x_slot[1]); cudaFree(out_slot[1]);          // slot 0 is x_stage / out_stage
   for (int i = 0; i < 2; ++i)
     for (cudaEvent_t e : {in_done[i], fwd_done[i], out_done[i]})
@@ -268,7 +277,12 @@ zmoe_status Layer::init(const zmoe_layer_config& c) {
   out_slot[0] = out_stage;
   x_slot[1] = dmalloc<uint16_t>((size_t)T * H, &st);
   out_slot[1] = dmalloc<uint16_t>((size_t)T * H, &st);
+  kerr_dev = dmalloc<int32_t>(1, &st);
+  kerr_host = hmalloc<int32_t>(1, &st);
   if (st != ZMOE_OK) return st;
+  ZMOE_CUDA_RET(cudaMemset(kerr_dev, 0, sizeof(int32_t)));
+  *kerr_host = 0;
+  ZMOE_CUDA_RET(cudaEventCreateWithFlags(&kerr_ready, cudaEventDisableTiming));
   ZMOE_CUDA_RET(cudaStreamCreateWithFlags(&copy_in, cudaStreamNonBlocking));
   ZMOE_CUDA_RET(cudaStreamCreateWithFlags(&copy_out, cudaStreamNonBlocking));
   for (int i = 0; i < 2; ++i) {
@@ -312,6 +326,40 @@ zmoe_status Layer::check_status() {
       set_error("decode of chunk %d failed with status %d", i, status_host[i]);
       return ZMOE_EINVAL;
     }
+  }
+  return ZMOE_OK;
+}
+
+// After a call's FFN launches: copy the error word back (unless the previous
+// copy is still unread; the word stays set until it is reported, so that copy
+// or a later one sees it).
+zmoe_status Layer::queue_kernel_error_copy(cudaStream_t s) {
+  if (kerr_pending) return ZMOE_OK;
+  ZMOE_CUDA_RET(cudaMemcpyAsync(kerr_host, kerr_dev, sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+  ZMOE_CUDA_RET(cudaEventRecord(kerr_ready, s));
+  kerr_pending = true;
+  return ZMOE_OK;
+}
+
+// Reports (once) an FFN launch that gave up a bounded wait.  Without wait, a
+// copy that has not landed yet is left for the next check.
+zmoe_status Layer::check_kernel_error(bool wait) {
+  if (!kerr_pending) return ZMOE_OK;
+  if (wait) {
+    ZMOE_CUDA_RET(cudaEventSynchronize(kerr_ready));
+  } else {
+    const cudaError_t q = cudaEventQuery(kerr_ready);
+    if (q == cudaErrorNotReady) return ZMOE_OK;
+    ZMOE_CUDA_RET(q);
+  }
+  kerr_pending = false;
+  if (*kerr_host != 0) {
+    const int32_t code = *kerr_host;
+    *kerr_host = 0;
+    ZMOE_CUDA_RET(cudaMemset(kerr_dev, 0, sizeof(int32_t)));
+    set_error("an expert FFN launch of an earlier call gave up a bounded wait (code %d); its outputs are "
+              "incomplete", code);
+    return ZMOE_EKERNEL;
   }
   return ZMOE_OK;
 }
@@ -505,7 +553,7 @@ zmoe_status Layer::run_experts(const uint16_t* xrows, const int32_t* offsets_dev
         if (!a || !b) { set_error("cudaEventCreate failed"); return ZMOE_ECUDA; }
         ZMOE_CUDA_RET(cudaEventRecord(a, s));
       }
-      if ((st = launch_expert_ffn(&fa, s)) != ZMOE_OK) return st;
+      if ((st = launch_expert_ffn(&fa, s, kerr_dev)) != ZMOE_OK) return st;
       if (timing) {
         ZMOE_CUDA_RET(cudaEventRecord(ev_pool[ev + 1], s));
         ev_pending.push_back({ev, 1, 0});
@@ -546,6 +594,7 @@ zmoe_status Layer::experts(const uint16_t* xrows, const int32_t* counts_h, int r
     offsets_pending = false;
   }
   if ((st = check_status()) != ZMOE_OK) return st;
+  if ((st = check_kernel_error(false)) != ZMOE_OK) return st;
   desc_cursor = 0;
   if ((st = fold_timing()) != ZMOE_OK) return st;
   if (rows == 0) return ZMOE_OK;
@@ -558,6 +607,7 @@ zmoe_status Layer::experts(const uint16_t* xrows, const int32_t* counts_h, int r
   ZMOE_CUDA_RET(cudaEventRecord(offsets_ready, s));
   offsets_pending = true;
   if ((st = run_experts(xrows, offsets_ext, counts_host, rows, yrows, s)) != ZMOE_OK) return st;
+  if ((st = queue_kernel_error_copy(s)) != ZMOE_OK) return st;
   stats.forwards++;
   stats.tokens += rows;
   return ZMOE_OK;
@@ -601,13 +651,14 @@ zmoe_status Layer::forward(const uint16_t* x, int T, uint16_t* out, cudaStream_t
     const uint16_t* tab[3] = {w_shared[0], w_shared[1], w_shared[2]};   // host table
     fa.x = x; fa.w = tab; fa.offsets = nullptr; fa.G = 1; fa.rows_total = T; fa.H = H;
     fa.I = cfg.shared_inter; fa.kind = 0; fa.h = hsh; fa.y = ysh;
-    if ((st = launch_expert_ffn(&fa, s)) != ZMOE_OK) return st;
+    if ((st = launch_expert_ffn(&fa, s, kerr_dev)) != ZMOE_OK) return st;
     stats.launches += 2;
   }
   // everything before the counts copy is done, the previous forward's decode
   // and pinned-buffer copies included
   ZMOE_CUDA_RET(cudaEventSynchronize(counts_ready));
   if ((st = check_status()) != ZMOE_OK) return st;   // previous forward's decode
+  if ((st = check_kernel_error(true)) != ZMOE_OK) return st;   // its FFN launches (done by now)
   desc_cursor = 0;
   if ((st = fold_timing()) != ZMOE_OK) return st;
 
@@ -619,6 +670,7 @@ zmoe_status Layer::forward(const uint16_t* x, int T, uint16_t* out, cudaStream_t
   ca.shared_gate = w_sgate ? sg : nullptr; ca.row_of = row_of; ca.topk_w = tw; ca.x = x;
   ca.T = T; ca.H = H; ca.k = k; ca.mode = cfg.route_mode; ca.out = out;
   if ((st = launch_combine(&ca, s)) != ZMOE_OK) return st;
+  if ((st = queue_kernel_error_copy(s)) != ZMOE_OK) return st;
   stats.launches++;
   stats.forwards++;
   stats.tokens += T;
@@ -900,6 +952,7 @@ zmoe_status zmoe_layer_sync(zmoe_layer* layer, zmoe_stream_t stream) {
   ZMOE_CUDA_RET(cudaStreamSynchronize(reinterpret_cast<cudaStream_t>(stream)));
   zmoe_status st = L->check_status();
   if (st != ZMOE_OK) return st;
+  if ((st = L->check_kernel_error(true)) != ZMOE_OK) return st;
   return L->fold_timing();
 }
 

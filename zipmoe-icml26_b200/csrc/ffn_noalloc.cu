@@ -28,7 +28,6 @@
 
 namespace zmoe {
 
-zmoe_status launch_expert_ffn(const zmoe_ffn_args*, cudaStream_t);
 
 namespace {
 

@@ -23,8 +23,9 @@
 // ring keeps one CTA per SM, so the 512 columns are always free.
 //
 // Every mbarrier wait is bounded; on a timeout the CTA records an error code
-// in zmoe's device error word, waits (bounded) for the loads it issued,
-// releases its TMEM and returns.
+// in zmoe's device error word (g_kernel_error, read by zmoe_kernel_error) and
+// in the launch's own error word when the caller gave one, waits (bounded)
+// for the loads it issued, releases its TMEM and returns.
 #include <cuda.h>
 
 #include <mutex>
@@ -46,6 +47,12 @@ constexpr int kMaxGroups = 128;
 constexpr int kThreads = 192;
 constexpr long long kWaitCycles = 4000000000LL;   // about 2 s at 1.9 GHz
 
+// Error-path test hook (zmoe_debug_ffn_wait): the wait limit of the next
+// launches, and whether their TMA producer issues nothing, so that the MMA
+// warp's first wait runs out.  Host-side settings, copied into each launch.
+long long g_wait_limit = kWaitCycles;
+int g_drop_loads = 0;
+
 struct __align__(64) Params {
   CUtensorMap amap[kMaxMaps];         // weight (A) maps: MODE 0 uses 2 per group
   CUtensorMap bmap;                   // activation (B) map over [rows_total, K]
@@ -53,6 +60,9 @@ struct __align__(64) Params {
   void* out;                          // h (bf16) or y (fp32), row-major [rows_total, n_out]
   int g_begin, g_count;               // groups of this launch (offset into offsets)
   int rows_total, K, n_out;           // n_out = weight rows of one matrix (I or H)
+  int32_t* err;                       // caller's error word (device) or nullptr
+  long long wait_limit;               // clock64 cycles a wait may take
+  int drop_loads;                     // error-path test: the producer issues nothing
   uint8_t present[kMaxGroups];        // 0: group not in this launch (no weights)
 };
 
@@ -88,15 +98,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait; false on timeout (error recorded).
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int32_t* cta_err) {
+// Bounded wait; false on timeout (error recorded in the CTA, the device-wide
+// word and the caller's word) or when another warp of the CTA already failed.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int32_t* cta_err, int32_t* err_out,
+                                          long long limit) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   while (!mbar_try_wait(bar, parity)) {
     if (*(volatile int32_t*)cta_err) return false;
-    if (clock64() - t0 > kWaitCycles) {
+    if (clock64() - t0 > limit) {
       atomicCAS(cta_err, 0, 1);
       atomicCAS(&g_kernel_error, 0, 1);
+      if (err_out) atomicCAS(err_out, 0, 1);
       return false;
     }
   }
@@ -241,14 +254,14 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_tc_kernel(const __grid_consta
       uint32_t phase = 0;
       uint32_t armed[8] = {0, 0, 0, 0, 0, 0, 0, 0};   // bit: stage armed in phase
       bool ok = true;
-      for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
+      for (int u = p.drop_loads ? total : (int)blockIdx.x; u < total && ok; u += gridDim.x) {
         int g, mt, nt;
         unit_of(u, g, mt, nt);
         const int arow = mt * BM;
         const int brow = row0[g] + nt * BN;
         const int m0 = MODE == 0 ? 2 * g : g;
         for (int ks = 0; ks < KS; ++ks) {
-          if (!mbar_wait(&empty[stage], phase ^ 1u, cta_err)) { ok = false; break; }
+          if (!mbar_wait(&empty[stage], phase ^ 1u, cta_err, p.err, p.wait_limit)) { ok = false; break; }
           uint8_t* st = smem + stage * kStageBytes;
           mbar_expect_tx(&full[stage], kStageBytes);
           armed[stage] = phase + 1;
@@ -263,7 +276,7 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_tc_kernel(const __grid_consta
         for (int s = 0; s < STAGES; ++s)
           if (armed[s]) {
             const long long t0 = clock64();
-            while (!mbar_try_wait(&full[s], armed[s] - 1) && clock64() - t0 < kWaitCycles) {
+            while (!mbar_try_wait(&full[s], armed[s] - 1) && clock64() - t0 < p.wait_limit) {
             }
           }
       }
@@ -283,10 +296,10 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_tc_kernel(const __grid_consta
         const int ab = i & 1;                           // accumulator of this unit
         const uint32_t acc_phase = (uint32_t)(i >> 1) & 1u;
         const uint32_t tacc = tmem + (uint32_t)ab * kAccCols;
-        if (!mbar_wait(&tmem_empty[ab], acc_phase ^ 1u, cta_err)) break;
+        if (!mbar_wait(&tmem_empty[ab], acc_phase ^ 1u, cta_err, p.err, p.wait_limit)) break;
         tc_fence_after();
         for (int ks = 0; ks < KS; ++ks) {
-          if (!mbar_wait(&full[stage], phase, cta_err)) { ok = false; break; }
+          if (!mbar_wait(&full[stage], phase, cta_err, p.err, p.wait_limit)) { ok = false; break; }
           tc_fence_after();
           const uint32_t sa = smem_u32(smem + stage * kStageBytes);
           const uint64_t da0 = smem_desc(sa);
@@ -308,7 +321,7 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_tc_kernel(const __grid_consta
         // error path: wait (bounded) until every MMA issued here has finished
         tc_commit(drain);
         const long long t0 = clock64();
-        while (!mbar_try_wait(drain, 0) && clock64() - t0 < kWaitCycles) {
+        while (!mbar_try_wait(drain, 0) && clock64() - t0 < p.wait_limit) {
         }
       }
     }
@@ -321,7 +334,7 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_tc_kernel(const __grid_consta
       const int valid = min(BN, rows[g] - nt * BN);
       const int n = max(16, (valid + 15) & ~15);
       const int ab = i & 1;
-      if (!mbar_wait(&tmem_full[ab], (uint32_t)(i >> 1) & 1u, cta_err)) break;
+      if (!mbar_wait(&tmem_full[ab], (uint32_t)(i >> 1) & 1u, cta_err, p.err, p.wait_limit)) break;
       tc_fence_after();
       const int feat = mt * BM + q * 32 + lane;   // output feature of this thread
       const size_t rbase = (size_t)(row0[g] + nt * BN);
@@ -412,7 +425,7 @@ zmoe_status make_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t c
 
 template <int MODE>
 zmoe_status launch_mode(const zmoe_ffn_args* a, const uint16_t* act, int K, int n_out, void* out,
-                        cudaStream_t stream) {
+                        cudaStream_t stream, int32_t* err) {
   const int per = MODE == 0 ? 2 : 1;
   const int gmax = kMaxMaps / per < kMaxGroups ? kMaxMaps / per : kMaxGroups;
   static Params p;                            // 17 KB: too large for the stack frame of a host thread loop
@@ -448,6 +461,9 @@ zmoe_status launch_mode(const zmoe_ffn_args* a, const uint16_t* act, int K, int 
     p.rows_total = a->rows_total;
     p.K = K;
     p.n_out = n_out;
+    p.err = err;
+    p.wait_limit = g_wait_limit;
+    p.drop_loads = g_drop_loads;
     ffn_tc_kernel<MODE><<<sms, kThreads, smem, stream>>>(p);
     st = launch_status("ffn_tc_kernel");
     if (st != ZMOE_OK) return st;
@@ -457,19 +473,30 @@ zmoe_status launch_mode(const zmoe_ffn_args* a, const uint16_t* act, int K, int 
 
 }  // namespace tc
 
-// a->w is a host array of G*3 device pointers.
-zmoe_status launch_expert_ffn(const zmoe_ffn_args* a, cudaStream_t stream) {
+// a->w is a host array of G*3 device pointers.  err: device error word that
+// a timed-out wait sets to 1 (nullptr: only the device-wide word is set).
+zmoe_status launch_expert_ffn(const zmoe_ffn_args* a, cudaStream_t stream, int32_t* err) {
   ZMOE_CHECK_ARG(a && a->x && a->w && a->h && a->y, "expert_ffn: null pointer");
   ZMOE_CHECK_ARG(a->G >= 1, "expert_ffn: G must be >= 1");
   ZMOE_CHECK_ARG(a->kind == 0 || a->kind == 1, "expert_ffn: kind must be 0 (SwiGLU) or 1 (ReLU)");
   ZMOE_CHECK_ARG(a->H > 0 && a->H % 8 == 0 && a->I > 0 && a->I % 8 == 0,
                  "expert_ffn: H=%d and I=%d must be positive multiples of 8", a->H, a->I);
   ZMOE_CHECK_ARG(a->offsets || a->G == 1, "expert_ffn: offsets required for G > 1");
+  // A group takes part with all of its matrices or with none: the down pass
+  // must never read an intermediate that the up pass did not write.
+  for (int g = 0; g < a->G; ++g) {
+    const uint16_t* const* w = a->w + 3 * (size_t)g;
+    const bool up_set = w[0] && (a->kind == 1 || w[1]);
+    const bool none = !w[0] && !w[1] && !w[2];
+    ZMOE_CHECK_ARG(none || (up_set && w[2]),
+                   "expert_ffn: group %d has only some of its weight pointers set (w0=%p w1=%p w2=%p)", g,
+                   (const void*)w[0], (const void*)w[1], (const void*)w[2]);
+  }
   if (a->rows_total <= 0) return ZMOE_OK;
-  zmoe_status st = a->kind == 0 ? tc::launch_mode<0>(a, a->x, a->H, a->I, a->h, stream)
-                                : tc::launch_mode<1>(a, a->x, a->H, a->I, a->h, stream);
+  zmoe_status st = a->kind == 0 ? tc::launch_mode<0>(a, a->x, a->H, a->I, a->h, stream, err)
+                                : tc::launch_mode<1>(a, a->x, a->H, a->I, a->h, stream, err);
   if (st != ZMOE_OK) return st;
-  return tc::launch_mode<2>(a, a->h, a->I, a->H, a->y, stream);
+  return tc::launch_mode<2>(a, a->h, a->I, a->H, a->y, stream, err);
 }
 
 zmoe_status read_kernel_error(int32_t* out, int reset) {
@@ -479,6 +506,11 @@ zmoe_status read_kernel_error(int32_t* out, int reset) {
     ZMOE_CUDA_RET(cudaMemcpyToSymbol(g_kernel_error, &z, sizeof(int32_t)));
   }
   return ZMOE_OK;
+}
+
+void set_ffn_wait(long long cycles, int drop_loads) {
+  tc::g_wait_limit = cycles > 0 ? cycles : tc::kWaitCycles;
+  tc::g_drop_loads = drop_loads != 0;
 }
 
 }  // namespace zmoe

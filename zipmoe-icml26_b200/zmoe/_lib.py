@@ -73,6 +73,8 @@ class LayerStats(ctypes.Structure):
 SIGNATURES = {
     "zmoe_abi_version": (c_int, []),
     "zmoe_last_error": (ctypes.c_char_p, []),
+    "zmoe_kernel_error": (c_int, [ctypes.POINTER(ctypes.c_int32), c_int]),
+    "zmoe_debug_ffn_wait": (c_int, [ctypes.c_longlong, c_int]),
     "zmoe_clock_probe": (c_int, [c_void_p, ctypes.c_uint64, c_void_p]),
     "zmoe_tensor_recover": (c_int, [c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
     "zmoe_decode_chunks": (c_int, [c_void_p, c_int, c_void_p, c_void_p]),
