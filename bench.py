@@ -56,6 +56,9 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--store", default="device", choices=["device", "host"],
                     help="where the compressed experts live (host: pinned memory, copied in per miss)")
+    ap.add_argument("--timeline", default=None,
+                    help="write the GPU timeline of 3 more steps (kernels and copies per stream, "
+                         "torch.profiler over CUPTI) to this text file")
     return ap.parse_args()
 
 
@@ -273,6 +276,49 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def write_timeline(step, steps, path):
+    """Runs step() `steps` times under torch.profiler (CUDA activity only) and
+    writes every kernel and copy with its stream, start and duration (us,
+    relative to the first), then which kernels ran while a decode kernel ran
+    on another stream."""
+    import tempfile
+    from torch.profiler import ProfilerActivity, profile
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(steps):
+            step()
+        torch.cuda.synchronize()
+    with tempfile.TemporaryDirectory() as d:
+        tp = os.path.join(d, "trace.json")
+        prof.export_chrome_trace(tp)
+        tr = json.load(open(tp))
+    ev = [e for e in tr.get("traceEvents", []) if e.get("cat") in ("kernel", "gpu_memcpy", "gpu_memset")]
+    ev.sort(key=lambda e: e["ts"])
+    t0 = ev[0]["ts"] if ev else 0.0
+    short = lambda n: n.split("(")[0].replace("void ", "").replace("zmoe::", "").replace("(anonymous namespace)::", "")
+    lines = [f"# {len(ev)} GPU activities over {steps} steps (us from the first; stream = CUDA stream id)",
+             f"{'start':>10} {'dur':>8} {'stream':>6}  name"]
+    for e in ev:
+        lines.append(f"{e['ts'] - t0:10.1f} {e['dur']:8.1f} {e['args'].get('stream', -1):>6}  {short(e['name'])}")
+    dec = [e for e in ev if e.get("cat") == "kernel" and ("map_kernel" in e["name"] or "resolve_kernel" in e["name"])]
+    lines.append("")
+    lines.append("# kernels that overlapped a decode kernel of another stream (us of overlap)")
+    tot = {}
+    for e in ev:
+        if e.get("cat") != "kernel" or e in dec:
+            continue
+        a, b = e["ts"], e["ts"] + e["dur"]
+        ov = sum(max(0.0, min(b, d["ts"] + d["dur"]) - max(a, d["ts"])) for d in dec
+                 if d["args"].get("stream") != e["args"].get("stream"))
+        if ov > 0:
+            k = short(e["name"])
+            tot[k] = tot.get(k, 0.0) + ov
+    for k, v in sorted(tot.items(), key=lambda kv: -kv[1]):
+        lines.append(f"{v / steps:10.1f} per step  {k}")
+    with open(path, "w") as f:
+        f.write("\n".join(lines) + "\n")
+
+
 def run_ours(args):
     world, rank, local = dist_env()
     if world > 1:
@@ -315,6 +361,8 @@ def run_ours(args):
     ms = start.elapsed_time(stop) / args.steps
     st = L.stats()
     L.set_timing(False)
+    if args.timeline and rank == 0:
+        write_timeline(lambda: L.forward(x, out), 3, args.timeline)
 
     # end to end through the public API with pinned host buffers: every step
     # copies its input in and its output back (zmoe_layer_submit_host, copies

@@ -92,6 +92,49 @@ def test_engine_cache_hits_follow_warm_set():
     assert st["misses"] == 0 and st["hits"] > 0
 
 
+def test_prefetch_does_not_wait_for_the_stream():
+    # clock probes keep the current stream busy for 30 ms; prefetch must return
+    # before they end, and the next forward must see the prefetched experts
+    from zmoe._lib import lib
+    s = QWEN_SMALL
+    L, w, wr, sg, sh = _build(s, 4)
+    x = syn.activations(32, s.hidden, seed=61)
+    L(x.cuda())                                      # sizes the decoder scratch (a one-time synchronising allocation)
+    L.sync()
+    probe = torch.zeros(2, dtype=torch.int64, device="cuda")
+    stream = torch.cuda.current_stream()
+    for _ in range(3):
+        assert lib.zmoe_clock_probe(probe.data_ptr(), 10_000_000, stream.cuda_stream) == 0
+    cached = set(L.cached_experts())
+    want = [e for e in range(s.num_experts) if e not in cached][:2]
+    L.prefetch(want)
+    assert not stream.query()                        # the probe is still running: no host wait happened
+    out = L(x.cuda())
+    L.sync()
+    assert set(want) <= set(L.cached_experts())
+    ref, r = moe.qwen_layer(x, wr, w, sh, sg, k=s.topk)
+    mx, mr = _close(out.float().cpu().numpy(), ref.float().numpy())
+    assert mx < TOL_MAX_ABS and mr < TOL_MEAN_REL, (mx, mr)
+    st = L.stats()
+    used = set(np.unique(r.topk_idx).tolist())
+    assert st["hits"] >= len(used & set(want))
+
+
+def test_overlapped_waves_match_oracle_over_many_forwards():
+    # one transient slot: every miss beyond the cache is its own decode wave,
+    # with the hit FFN running beside the first wave's decode
+    s = QWEN_SMALL
+    L, w, wr, sg, sh = _build(s, 3, transient=1, T=48)
+    for step in range(6):
+        x = syn.activations(8 + 8 * step, s.hidden, seed=70 + step)
+        out = L(x.cuda())
+        ref, _ = moe.qwen_layer(x, wr, w, sh, sg, k=s.topk)
+        mx, mr = _close(out.float().cpu().numpy(), ref.float().numpy())
+        assert mx < TOL_MAX_ABS and mr < TOL_MEAN_REL, (step, mx, mr)
+    L.sync()
+    assert L.stats()["decode_errors"] == 0
+
+
 def test_engine_forward_host_matches_device():
     s = QWEN_SMALL
     L, *_ = _build(s, 2)

@@ -15,6 +15,7 @@
 //    the per-expert token counts (the reference's expert_count.cpu(),
 //    experts/expert_executor.py:45-49).
 #include <algorithm>
+#include <deque>
 #include <memory>
 #include <numeric>
 #include <vector>
@@ -106,13 +107,28 @@ struct Layer {
   const uint16_t** wtab_host = nullptr;
   int32_t* status_host = nullptr;
   int max_desc = 0, max_waves = 0;
-  int desc_cursor = 0;             // descriptors used by the current forward
+  // The pinned descriptor / status buffers (desc_host, status_host) and their
+  // device twins are used as a ring: each decode takes the next count entries
+  // and keeps them until the copy of its status words has landed.
+  int desc_cursor = 0;
+  struct PendingDecode { int base, count; cudaEvent_t done; };
+  std::deque<PendingDecode> pending;
+  std::vector<cudaEvent_t> free_events;
+  zmoe_status reclaim(bool wait_all);
+  zmoe_status alloc_desc(int count, int* base);
+  // Misses decode on the layer's own stream (the device's highest priority),
+  // while the caller's stream runs the FFN over cache hits and the shared
+  // expert; events order the two where slots are shared.
+  cudaStream_t ds = nullptr;
+  cudaEvent_t ev_caller = nullptr;      // caller's stream -> decode stream
+  cudaEvent_t ev_decoded = nullptr;     // decode stream -> caller's stream
+  cudaEvent_t ev_prefetch = nullptr;    // end of the last prefetch decode
+  bool prefetch_pending = false;
   uint32_t* map_scratch = nullptr; // decoder source-map scratch (zmoe_decode_scratch_bytes per chunk)
   bool host_store = false;         // compressed experts in pinned host memory, copied in per miss
   uint8_t* stage_buf = nullptr;    // host tier: device copies of the compressed tensors being decoded
   uint64_t stage_cap = 0;
   uint64_t map_cap = 0;            // bytes of map_scratch
-  int pending_status = 0;          // descriptors whose status is still to be checked
   // error word of this layer's FFN launches (set when a bounded wait ran out),
   // copied back after each call and checked at the next one
   int32_t* kerr_dev = nullptr;
@@ -131,7 +147,6 @@ struct Layer {
   cudaEvent_t in_done[2] = {nullptr, nullptr}, fwd_done[2] = {nullptr, nullptr}, out_done[2] = {nullptr, nullptr};
   uint64_t submitted = 0;
   zmoe_status submit_host(const uint16_t* x_host, int T, uint16_t* out_host, cudaStream_t s);
-  cudaEvent_t status_ready = nullptr;
   cudaEvent_t offsets_ready = nullptr;   // zmoe_layer_experts: the pinned offsets were copied
   cudaEvent_t counts_ready = nullptr;    // forward: the per-expert counts reached the host
   bool offsets_pending = false;
@@ -152,11 +167,13 @@ struct Layer {
   zmoe_status init(const zmoe_layer_config& c);
   zmoe_status forward(const uint16_t* x, int T, uint16_t* out, cudaStream_t s);
   zmoe_status run_experts(const uint16_t* xrows, const int32_t* offsets_dev, const int32_t* counts_h, int rows,
-                          float* yrows, cudaStream_t s);
+                          float* yrows, cudaStream_t s, bool caller_marked);
   zmoe_status experts(const uint16_t* xrows, const int32_t* counts_h, int rows, float* yrows, cudaStream_t s);
   zmoe_status check_status();
   int choose_victim(const std::vector<char>& active);
-  zmoe_status decode_into(const std::vector<std::pair<int, int>>& jobs, cudaStream_t s, int wave);
+  zmoe_status decode_into(const std::vector<std::pair<int, int>>& jobs, cudaStream_t s);
+  zmoe_status ffn_over(const std::vector<std::pair<int, int>>& groups, int table, const uint16_t* xrows,
+                       const int32_t* offsets_dev, int rows, float* yrows, cudaStream_t s);
   uint16_t* slot_ptr(int slot, int t) const { return slots + ((size_t)slot * tensors + t) * numel; }
 };
 
@@ -181,7 +198,11 @@ Layer::~Layer() {
       if (e) cudaEventDestroy(e);
   if (copy_in) cudaStreamDestroy(copy_in);
   if (copy_out) cudaStreamDestroy(copy_out);
-  if (status_ready) cudaEventDestroy(status_ready);
+  for (auto& p : pending) cudaEventDestroy(p.done);
+  for (auto e : free_events) cudaEventDestroy(e);
+  for (cudaEvent_t e : {ev_caller, ev_decoded, ev_prefetch})
+    if (e) cudaEventDestroy(e);
+  if (ds) cudaStreamDestroy(ds);
   if (offsets_ready) cudaEventDestroy(offsets_ready);
   if (counts_ready) cudaEventDestroy(counts_ready);
   for (auto e : ev_pool) cudaEventDestroy(e);
@@ -264,12 +285,12 @@ zmoe_status Layer::init(const zmoe_layer_config& c) {
   max_desc = E * tensors * 64;
   desc_dev = dmalloc<zmoe_chunk>(max_desc, &st);
   status_dev = dmalloc<int32_t>(max_desc, &st);
-  wtab_dev = dmalloc<const uint16_t*>((size_t)max_waves * E * 3, &st);
+  wtab_dev = dmalloc<const uint16_t*>((size_t)(max_waves + 1) * E * 3, &st);
   counts_host = hmalloc<int32_t>(E, &st);
   offsets_host = hmalloc<int32_t>(E + 1, &st);
   offsets_ext = dmalloc<int32_t>(E + 1, &st);
   desc_host = hmalloc<zmoe_chunk>(max_desc, &st);
-  wtab_host = hmalloc<const uint16_t*>((size_t)max_waves * E * 3, &st);
+  wtab_host = hmalloc<const uint16_t*>((size_t)(max_waves + 1) * E * 3, &st);
   status_host = hmalloc<int32_t>(max_desc, &st);
   x_stage = dmalloc<uint16_t>((size_t)T * H, &st);
   out_stage = dmalloc<uint16_t>((size_t)T * H, &st);
@@ -290,7 +311,12 @@ zmoe_status Layer::init(const zmoe_layer_config& c) {
     ZMOE_CUDA_RET(cudaEventCreateWithFlags(&fwd_done[i], cudaEventDisableTiming));
     ZMOE_CUDA_RET(cudaEventCreateWithFlags(&out_done[i], cudaEventDisableTiming));
   }
-  ZMOE_CUDA_RET(cudaEventCreateWithFlags(&status_ready, cudaEventDisableTiming));
+  int least = 0, greatest = 0;
+  ZMOE_CUDA_RET(cudaDeviceGetStreamPriorityRange(&least, &greatest));
+  ZMOE_CUDA_RET(cudaStreamCreateWithPriority(&ds, cudaStreamNonBlocking, greatest));
+  ZMOE_CUDA_RET(cudaEventCreateWithFlags(&ev_caller, cudaEventDisableTiming));
+  ZMOE_CUDA_RET(cudaEventCreateWithFlags(&ev_decoded, cudaEventDisableTiming));
+  ZMOE_CUDA_RET(cudaEventCreateWithFlags(&ev_prefetch, cudaEventDisableTiming));
   ZMOE_CUDA_RET(cudaEventCreateWithFlags(&offsets_ready, cudaEventDisableTiming));
   ZMOE_CUDA_RET(cudaEventCreateWithFlags(&counts_ready, cudaEventDisableTiming));
   return ZMOE_OK;
@@ -315,18 +341,43 @@ int Layer::choose_victim(const std::vector<char>& active) {
   return victim;
 }
 
-zmoe_status Layer::check_status() {
-  if (pending_status == 0) return ZMOE_OK;
-  ZMOE_CUDA_RET(cudaEventSynchronize(status_ready));
-  const int n = pending_status;
-  pending_status = 0;
-  for (int i = 0; i < n; ++i) {
-    if (status_host[i] != ZMOE_CHUNK_OK) {
-      stats.decode_errors++;
-      set_error("decode of chunk %d failed with status %d", i, status_host[i]);
-      return ZMOE_EINVAL;
+// Checks the status words of every decode whose status copy has landed (all
+// of them with wait_all) and frees their ring entries.  Returns the first
+// decode error found.
+zmoe_status Layer::reclaim(bool wait_all) {
+  zmoe_status bad = ZMOE_OK;
+  while (!pending.empty()) {
+    PendingDecode p = pending.front();
+    if (wait_all) {
+      ZMOE_CUDA_RET(cudaEventSynchronize(p.done));
+    } else {
+      const cudaError_t q = cudaEventQuery(p.done);
+      if (q == cudaErrorNotReady) break;
+      ZMOE_CUDA_RET(q);
     }
+    for (int i = 0; i < p.count && bad == ZMOE_OK; ++i) {
+      if (status_host[p.base + i] != ZMOE_CHUNK_OK) {
+        stats.decode_errors++;
+        set_error("decode of chunk %d failed with status %d", i, status_host[p.base + i]);
+        bad = ZMOE_EINVAL;
+      }
+    }
+    free_events.push_back(p.done);
+    pending.pop_front();
   }
+  if (pending.empty()) desc_cursor = 0;
+  return bad;
+}
+
+zmoe_status Layer::check_status() { return reclaim(false); }
+
+zmoe_status Layer::alloc_desc(int count, int* base) {
+  ZMOE_CHECK_ARG(count <= max_desc, "too many chunks in one decode (%d > %d)", count, max_desc);
+  zmoe_status st = reclaim(false);
+  if (st != ZMOE_OK) return st;
+  if (desc_cursor + count > max_desc && (st = reclaim(true)) != ZMOE_OK) return st;
+  *base = desc_cursor;
+  desc_cursor += count;
   return ZMOE_OK;
 }
 
@@ -364,10 +415,15 @@ zmoe_status Layer::check_kernel_error(bool wait) {
   return ZMOE_OK;
 }
 
-// Decode (expert, slot) jobs in one fused launch.
-zmoe_status Layer::decode_into(const std::vector<std::pair<int, int>>& jobs, cudaStream_t s, int wave) {
-  const int base = desc_cursor;
-  int nd = base;
+// Decode (expert, slot) jobs in one fused launch on stream s (the decode stream).
+zmoe_status Layer::decode_into(const std::vector<std::pair<int, int>>& jobs, cudaStream_t s) {
+  int cnt = 0;
+  for (auto [e, slot] : jobs)
+    for (int t = 0; t < tensors; ++t) cnt += (int)store[e][t].block_off.size();
+  if (cnt == 0) return ZMOE_OK;
+  int base = 0;
+  zmoe_status st = alloc_desc(cnt, &base);
+  if (st != ZMOE_OK) return st;
   // host tier: each tensor's packed buffer is copied into the staging area
   // ahead of the decode (stream order keeps the previous decode's reads of the
   // area before these copies)
@@ -385,6 +441,7 @@ zmoe_status Layer::decode_into(const std::vector<std::pair<int, int>>& jobs, cud
     }
   }
   uint64_t stage_off = 0;
+  int nd = base;
   for (auto [e, slot] : jobs) {
     for (int t = 0; t < tensors; ++t) {
       const TensorStore& ts = store[e][t];
@@ -399,10 +456,6 @@ zmoe_status Layer::decode_into(const std::vector<std::pair<int, int>>& jobs, cud
       uint64_t e0 = 0;
       uint16_t* dst = slot_ptr(slot, t);
       for (size_t c = 0; c < ts.block_off.size(); ++c) {
-        if (nd >= max_desc) {
-          set_error("too many chunks in one decode (%d)", nd);
-          return ZMOE_EUNSUPPORTED;
-        }
         zmoe_chunk& d = desc_host[nd++];
         d.src = buf + ts.block_off[c];
         d.sm = buf + ts.sm_off + e0;
@@ -419,12 +472,11 @@ zmoe_status Layer::decode_into(const std::vector<std::pair<int, int>>& jobs, cud
     }
     stats.decoded_experts++;
   }
-  const int cnt = nd - base;
   uint64_t need = 0;
   for (int i = 0; i < cnt; ++i) need += zmoe_decode_scratch_bytes(desc_host[base + i].out_size);
   if (need > map_cap) {
     // grows to the largest decode seen (a synchronising allocation, only
-    // before the working set is known)
+    // before the working set is known); every decode runs on this stream
     ZMOE_CUDA_RET(cudaStreamSynchronize(s));
     cudaFree(map_scratch);
     map_scratch = nullptr;
@@ -437,11 +489,6 @@ zmoe_status Layer::decode_into(const std::vector<std::pair<int, int>>& jobs, cud
     desc_host[base + i].map = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(map_scratch) + moff);
     moff += zmoe_decode_scratch_bytes(desc_host[base + i].out_size);
   }
-  if (cnt == 0) return ZMOE_OK;
-  (void)wave;
-  // Descriptors and status words of every wave of one forward live side by
-  // side, so no pinned buffer is rewritten before its copy has run.
-  desc_cursor = nd;
   ZMOE_CUDA_RET(cudaMemcpyAsync(desc_dev + base, desc_host + base, sizeof(zmoe_chunk) * cnt,
                                 cudaMemcpyHostToDevice, s));
   uint64_t bytes = 0;
@@ -453,7 +500,7 @@ zmoe_status Layer::decode_into(const std::vector<std::pair<int, int>>& jobs, cud
     if (!a || !b) { set_error("cudaEventCreate failed"); return ZMOE_ECUDA; }
     ZMOE_CUDA_RET(cudaEventRecord(a, s));
   }
-  zmoe_status st = launch_decode_chunks(desc_dev + base, cnt, status_dev + base, s);
+  st = launch_decode_chunks(desc_dev + base, cnt, status_dev + base, s);
   if (st != ZMOE_OK) return st;
   if (timing) {
     ZMOE_CUDA_RET(cudaEventRecord(ev_pool[ev + 1], s));
@@ -464,16 +511,59 @@ zmoe_status Layer::decode_into(const std::vector<std::pair<int, int>>& jobs, cud
   stats.decoded_chunks += cnt;
   ZMOE_CUDA_RET(cudaMemcpyAsync(status_host + base, status_dev + base, sizeof(int32_t) * cnt,
                                 cudaMemcpyDeviceToHost, s));
-  ZMOE_CUDA_RET(cudaEventRecord(status_ready, s));
-  pending_status = nd;
+  cudaEvent_t done = nullptr;
+  if (!free_events.empty()) {
+    done = free_events.back();
+    free_events.pop_back();
+  } else {
+    ZMOE_CUDA_RET(cudaEventCreateWithFlags(&done, cudaEventDisableTiming));
+  }
+  ZMOE_CUDA_RET(cudaEventRecord(done, s));
+  pending.push_back({base, cnt, done});
+  return ZMOE_OK;
+}
+
+// Grouped FFN over the given (expert, slot) groups on stream s; the other
+// groups of the launch are skipped.  table: which host weight table to fill.
+zmoe_status Layer::ffn_over(const std::vector<std::pair<int, int>>& groups, int table, const uint16_t* xrows,
+                            const int32_t* offsets_dev, int rows, float* yrows, cudaStream_t s) {
+  if (groups.empty()) return ZMOE_OK;
+  const int E = cfg.num_experts;
+  if (table > max_waves) { set_error("too many decode waves"); return ZMOE_EUNSUPPORTED; }
+  const uint16_t** tab = wtab_host + (size_t)table * E * 3;
+  std::fill(tab, tab + (size_t)E * 3, nullptr);
+  for (auto [e, slot] : groups) {
+    tab[e * 3 + 0] = slot_ptr(slot, 0);
+    tab[e * 3 + 1] = tensors == 3 ? slot_ptr(slot, 1) : nullptr;
+    tab[e * 3 + 2] = slot_ptr(slot, tensors - 1);
+  }
+  zmoe_ffn_args fa{};
+  fa.x = xrows; fa.w = tab; fa.offsets = offsets_dev; fa.G = E; fa.rows_total = rows; fa.H = cfg.hidden;
+  fa.I = cfg.inter; fa.kind = cfg.kind; fa.h = h; fa.y = yrows;
+  int ev = -1;
+  if (timing) {
+    ev = ev_used;
+    cudaEvent_t a = next_event(), b = next_event();
+    if (!a || !b) { set_error("cudaEventCreate failed"); return ZMOE_ECUDA; }
+    ZMOE_CUDA_RET(cudaEventRecord(a, s));
+  }
+  zmoe_status st = launch_expert_ffn(&fa, s, kerr_dev);
+  if (st != ZMOE_OK) return st;
+  if (timing) {
+    ZMOE_CUDA_RET(cudaEventRecord(ev_pool[ev + 1], s));
+    ev_pending.push_back({ev, 1, 0});
+  }
+  stats.launches += 2;
   return ZMOE_OK;
 }
 
 // Cache decisions (ProactiveDecision), miss decode waves and the grouped FFN
 // over rows already grouped by expert: group e is rows [offsets[e], offsets[e+1]).
+// caller_marked: ev_caller was recorded on s before any work of this call
+// (otherwise it is recorded here).
 zmoe_status Layer::run_experts(const uint16_t* xrows, const int32_t* offsets_dev, const int32_t* counts_h, int rows,
-                               float* yrows, cudaStream_t s) {
-  const int E = cfg.num_experts, H = cfg.hidden;
+                               float* yrows, cudaStream_t s, bool caller_marked) {
+  const int E = cfg.num_experts;
   zmoe_status st;
   // 3. cache decisions (ProactiveDecision)
   std::vector<char> active(E, 0);
@@ -519,53 +609,44 @@ zmoe_status Layer::run_experts(const uint16_t* xrows, const int32_t* offsets_dev
     to_transient.push_back({e, -1});
   }
 
-  // 4. waves: decode misses, run the grouped FFN over experts whose weights are ready
+  // 4. Misses decode on the decode stream, in waves of the transient slots;
+  //    the FFN over the cache hits runs on the caller's stream meanwhile, and
+  //    the FFN over each decoded wave follows its decode.  Every slot a decode
+  //    overwrites was last read by FFN work queued on s before ev_caller.
+  if (!caller_marked) ZMOE_CUDA_RET(cudaEventRecord(ev_caller, s));
+  ZMOE_CUDA_RET(cudaStreamWaitEvent(ds, ev_caller, 0));
   size_t tpos = 0;
-  int wave = 0;
-  std::vector<std::pair<int, int>> ready(hits_slots);
+  int table = 0;
   std::vector<std::pair<int, int>> jobs(to_cache);
-  while (true) {
+  auto next_wave = [&]() {
     int used = 0;
     while (tpos < to_transient.size() && used < n_transient) {
-      const int slot = n_cache + used;
-      jobs.push_back({to_transient[tpos].first, slot});
+      jobs.push_back({to_transient[tpos].first, n_cache + used});
       ++tpos;
       ++used;
     }
-    if ((st = decode_into(jobs, s, wave)) != ZMOE_OK) return st;
-    ready.insert(ready.end(), jobs.begin(), jobs.end());
-    if (!ready.empty()) {
-      if (wave >= max_waves - 1) { set_error("too many decode waves"); return ZMOE_EUNSUPPORTED; }
-      const uint16_t** tab = wtab_host + (size_t)wave * E * 3;
-      std::fill(tab, tab + (size_t)E * 3, nullptr);
-      for (auto [e, slot] : ready) {
-        tab[e * 3 + 0] = slot_ptr(slot, 0);
-        tab[e * 3 + 1] = tensors == 3 ? slot_ptr(slot, 1) : nullptr;
-        tab[e * 3 + 2] = slot_ptr(slot, tensors - 1);
-      }
-      zmoe_ffn_args fa{};
-      fa.x = xrows; fa.w = tab; fa.offsets = offsets_dev; fa.G = E; fa.rows_total = rows; fa.H = H;
-      fa.I = cfg.inter; fa.kind = cfg.kind; fa.h = h; fa.y = yrows;
-      int ev = -1;
-      if (timing) {
-        ev = ev_used;
-        cudaEvent_t a = next_event(), b = next_event();
-        if (!a || !b) { set_error("cudaEventCreate failed"); return ZMOE_ECUDA; }
-        ZMOE_CUDA_RET(cudaEventRecord(a, s));
-      }
-      if ((st = launch_expert_ffn(&fa, s, kerr_dev)) != ZMOE_OK) return st;
-      if (timing) {
-        ZMOE_CUDA_RET(cudaEventRecord(ev_pool[ev + 1], s));
-        ev_pending.push_back({ev, 1, 0});
-      }
-      stats.launches += 2;
+  };
+  next_wave();
+  if ((st = decode_into(jobs, ds)) != ZMOE_OK) return st;       // the critical path goes first
+  if (!hits_slots.empty()) {
+    if (prefetch_pending) {                                      // hits may sit in slots a prefetch filled
+      ZMOE_CUDA_RET(cudaStreamWaitEvent(s, ev_prefetch, 0));
+      prefetch_pending = false;
     }
-    ++wave;
-    ready.clear();
-    jobs.clear();
-    if (tpos >= to_transient.size()) break;
+    if ((st = ffn_over(hits_slots, table++, xrows, offsets_dev, rows, yrows, s)) != ZMOE_OK) return st;
   }
-
+  while (!jobs.empty()) {
+    ZMOE_CUDA_RET(cudaEventRecord(ev_decoded, ds));
+    ZMOE_CUDA_RET(cudaStreamWaitEvent(s, ev_decoded, 0));
+    if ((st = ffn_over(jobs, table++, xrows, offsets_dev, rows, yrows, s)) != ZMOE_OK) return st;
+    jobs.clear();
+    next_wave();
+    if (jobs.empty()) break;
+    // the next wave reuses the transient slots that this wave's FFN reads
+    ZMOE_CUDA_RET(cudaEventRecord(ev_caller, s));
+    ZMOE_CUDA_RET(cudaStreamWaitEvent(ds, ev_caller, 0));
+    if ((st = decode_into(jobs, ds)) != ZMOE_OK) return st;
+  }
   return ZMOE_OK;
 }
 
@@ -585,17 +666,16 @@ zmoe_status Layer::experts(const uint16_t* xrows, const int32_t* counts_h, int r
     for (int t = 0; t < tensors; ++t)
       ZMOE_CHECK_ARG(store[e][t].loaded(), "experts: expert %d tensor %d not loaded", e, t);
   zmoe_status st;
-  // Host buffers of the previous call: its pinned offsets copy, its decode
-  // descriptors and status (status_ready comes after both on the stream).
-  // Waiting on these events, not on the stream, lets the caller's queued work
-  // (an exchange, a gather) run on while this call plans and launches.
+  // The pinned offsets buffer of the previous call is rewritten below: wait
+  // for its copy (an event, not the stream, so that the caller's queued work,
+  // an exchange or a gather, runs on while this call plans and launches).
+  // Decode statuses that have landed are checked without waiting.
   if (offsets_pending) {
     ZMOE_CUDA_RET(cudaEventSynchronize(offsets_ready));
     offsets_pending = false;
   }
   if ((st = check_status()) != ZMOE_OK) return st;
   if ((st = check_kernel_error(false)) != ZMOE_OK) return st;
-  desc_cursor = 0;
   if ((st = fold_timing()) != ZMOE_OK) return st;
   if (rows == 0) return ZMOE_OK;
   offsets_host[0] = 0;
@@ -606,7 +686,7 @@ zmoe_status Layer::experts(const uint16_t* xrows, const int32_t* counts_h, int r
   ZMOE_CUDA_RET(cudaMemcpyAsync(offsets_ext, offsets_host, sizeof(int32_t) * (E + 1), cudaMemcpyHostToDevice, s));
   ZMOE_CUDA_RET(cudaEventRecord(offsets_ready, s));
   offsets_pending = true;
-  if ((st = run_experts(xrows, offsets_ext, counts_host, rows, yrows, s)) != ZMOE_OK) return st;
+  if ((st = run_experts(xrows, offsets_ext, counts_host, rows, yrows, s, false)) != ZMOE_OK) return st;
   if ((st = queue_kernel_error_copy(s)) != ZMOE_OK) return st;
   stats.forwards++;
   stats.tokens += rows;
@@ -623,6 +703,9 @@ zmoe_status Layer::forward(const uint16_t* x, int T, uint16_t* out, cudaStream_t
       ZMOE_CHECK_ARG(store[e][t].loaded(), "forward: expert %d tensor %d not loaded", e, t);
   if (T == 0) return ZMOE_OK;
   zmoe_status st;
+  // everything queued so far (the previous forward's FFN reads of the slots)
+  // comes before this forward's decodes; the shared expert below does not
+  ZMOE_CUDA_RET(cudaEventRecord(ev_caller, s));
 
   // 1. router
   zmoe_router_args ra{};
@@ -659,10 +742,9 @@ zmoe_status Layer::forward(const uint16_t* x, int T, uint16_t* out, cudaStream_t
   ZMOE_CUDA_RET(cudaEventSynchronize(counts_ready));
   if ((st = check_status()) != ZMOE_OK) return st;   // previous forward's decode
   if ((st = check_kernel_error(true)) != ZMOE_OK) return st;   // its FFN launches (done by now)
-  desc_cursor = 0;
   if ((st = fold_timing()) != ZMOE_OK) return st;
 
-  if ((st = run_experts(xp, offsets, counts_host, T * k, y, s)) != ZMOE_OK) return st;
+  if ((st = run_experts(xp, offsets, counts_host, T * k, y, s, true)) != ZMOE_OK) return st;
 
   // 5. combine
   zmoe_combine_args ca{};
@@ -856,14 +938,13 @@ zmoe_status zmoe_layer_warm_cache(zmoe_layer* layer, const int* experts, int n, 
     jobs.push_back({e, slot});
   }
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  ZMOE_CUDA_RET(cudaStreamSynchronize(s));
-  zmoe_status st = L->check_status();
+  ZMOE_CUDA_RET(cudaEventRecord(L->ev_caller, s));       // free slots: nothing queued reads them, but keep order
+  ZMOE_CUDA_RET(cudaStreamWaitEvent(L->ds, L->ev_caller, 0));
+  zmoe_status st = L->decode_into(jobs, L->ds);
   if (st != ZMOE_OK) return st;
-  L->desc_cursor = 0;
-  st = L->decode_into(jobs, s, 0);
-  if (st != ZMOE_OK) return st;
-  ZMOE_CUDA_RET(cudaStreamSynchronize(s));
-  return L->check_status();
+  ZMOE_CUDA_RET(cudaEventRecord(L->ev_decoded, L->ds));
+  ZMOE_CUDA_RET(cudaStreamWaitEvent(s, L->ev_decoded, 0));
+  return L->reclaim(true);                               // the cache is warm when this returns
 }
 
 zmoe_status zmoe_layer_prefetch(zmoe_layer* layer, const int* experts, int n, zmoe_stream_t stream) {
@@ -878,10 +959,8 @@ zmoe_status zmoe_layer_prefetch(zmoe_layer* layer, const int* experts, int n, zm
     keep[experts[i]] = 1;
   }
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  ZMOE_CUDA_RET(cudaStreamSynchronize(s));
   zmoe_status st = L->check_status();
   if (st != ZMOE_OK) return st;
-  L->desc_cursor = 0;
   std::vector<std::pair<int, int>> jobs;
   for (int i = 0; i < n && L->n_cache > 0; ++i) {
     const int e = experts[i];
@@ -896,7 +975,16 @@ zmoe_status zmoe_layer_prefetch(zmoe_layer* layer, const int* experts, int n, zm
     L->slot_admit[slot] = L->clock;
     jobs.push_back({e, slot});
   }
-  return L->decode_into(jobs, s, 0);
+  if (jobs.empty()) return ZMOE_OK;
+  // the victims were last read by FFN work already queued on the caller's
+  // stream; the decode runs after it on the decode stream, and the next FFN
+  // over cache hits waits for the decode (ev_prefetch).  No host wait.
+  ZMOE_CUDA_RET(cudaEventRecord(L->ev_caller, s));
+  ZMOE_CUDA_RET(cudaStreamWaitEvent(L->ds, L->ev_caller, 0));
+  if ((st = L->decode_into(jobs, L->ds)) != ZMOE_OK) return st;
+  ZMOE_CUDA_RET(cudaEventRecord(L->ev_prefetch, L->ds));
+  L->prefetch_pending = true;
+  return ZMOE_OK;
 }
 
 zmoe_status zmoe_layer_forward(zmoe_layer* layer, const uint16_t* x, int T, uint16_t* out, zmoe_stream_t stream) {
@@ -950,7 +1038,7 @@ zmoe_status zmoe_layer_sync(zmoe_layer* layer, zmoe_stream_t stream) {
   Layer* L = reinterpret_cast<Layer*>(layer);
   ZMOE_CHECK_ARG(L, "sync: null layer");
   ZMOE_CUDA_RET(cudaStreamSynchronize(reinterpret_cast<cudaStream_t>(stream)));
-  zmoe_status st = L->check_status();
+  zmoe_status st = L->reclaim(true);                     // decodes on the decode stream too (prefetches)
   if (st != ZMOE_OK) return st;
   if ((st = L->check_kernel_error(true)) != ZMOE_OK) return st;
   return L->fold_timing();

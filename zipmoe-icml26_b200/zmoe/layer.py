@@ -102,6 +102,15 @@ class MoELayer:
         check(lib.zmoe_layer_warm_cache(self._h, arr, len(ex), torch.cuda.current_stream(self.device).cuda_stream),
               "zmoe_layer_warm_cache")
 
+    def prefetch(self, experts: Iterable[int]):
+        """Decode experts into cache slots ahead of use (zmoe_layer_prefetch),
+        on the layer's decode stream after the work already queued on the
+        current stream; returns without waiting."""
+        ex = list(experts)
+        arr = (ctypes.c_int * max(len(ex), 1))(*ex)
+        check(lib.zmoe_layer_prefetch(self._h, arr, len(ex), torch.cuda.current_stream(self.device).cuda_stream),
+              "zmoe_layer_prefetch")
+
     def forward(self, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         if not x.is_cuda or x.dtype != torch.bfloat16 or not x.is_contiguous():
             raise ValueError("x must be a contiguous CUDA BF16 tensor")
