@@ -185,11 +185,13 @@ zmoe_status zmoe_permute(const zmoe_permute_args* a, zmoe_stream_t stream);
  * Replaces DeepSeekMoEDenseActDense::forward (csrc/dispatcher/expert_module.cpp:39-50)
  * and SwitchTransformersDenseActDense::forward (:67-78) run one expert at a
  * time by ExpertDispatcher::GPUExecFunc (expert_dispatcher.cpp:354-427).
- * kind 0: y = bf16(silu(x Wg^T) * (x Wu^T)) Wd^T ; kind 1: y = bf16(relu(x Wi^T)) Wo^T.
+ * kind 0: y = bf16(bf16(silu(x Wg^T) * (x Wu^T)) Wd^T) ; kind 1: y = bf16(bf16(relu(x Wi^T)) Wo^T):
+ * fp32 accumulation, the intermediate and the output each rounded to BF16
+ * once (the reference's libtorch FFN returns BF16 rows).
  * w[g*3 + {0,1,2}] are the device pointers of group g's matrices (row-major
  * [I, H], [I, H], [H, I]; for kind 1 w[g*3+0] = wi [I, H], w[g*3+2] = wo [H, I]).
  * Rows of group g are offsets[g] .. offsets[g+1] of x; NULL offsets means one
- * group of rows_total rows.  y is fp32 [rows, H]; h is BF16 scratch [rows, I].
+ * group of rows_total rows.  y is BF16 [rows, H]; h is BF16 scratch [rows, I].
  * ------------------------------------------------------------------------ */
 typedef struct zmoe_ffn_args {
   const uint16_t* x;          /* [rows, H] BF16 */
@@ -199,7 +201,7 @@ typedef struct zmoe_ffn_args {
   const int32_t* offsets;     /* [G + 1] device or NULL */
   int G, rows_total, H, I, kind;
   uint16_t* h;                /* [rows, I] BF16 scratch */
-  float* y;                   /* [rows, H] fp32 out */
+  uint16_t* y;                /* [rows, H] BF16 out */
 } zmoe_ffn_args;
 
 zmoe_status zmoe_expert_ffn(const zmoe_ffn_args* a, zmoe_stream_t stream);
@@ -227,8 +229,8 @@ zmoe_status zmoe_expert_ffn_noalloc(const zmoe_ffn_args* a, zmoe_stream_t stream
  * fp32 accumulation, one BF16 rounding.
  * ------------------------------------------------------------------------ */
 typedef struct zmoe_combine_args {
-  const float* y;             /* [rows, H] */
-  const float* y_shared;      /* [T, H] or NULL */
+  const uint16_t* y;          /* [rows, H] BF16 expert rows */
+  const uint16_t* y_shared;   /* [T, H] BF16 shared-expert rows, or NULL */
   const float* shared_gate;   /* [T] or NULL */
   const int32_t* row_of;      /* [T, k] */
   const float* topk_w;        /* [T, k] */
@@ -334,13 +336,13 @@ zmoe_status zmoe_layer_forward(zmoe_layer* layer, const uint16_t* x, int T, uint
  * exchanges rows): x_rows device [rows, H] BF16 grouped by this layer's
  * experts, counts_host[e] rows of expert e (host array, summing to rows <=
  * max_tokens * topk); applies the cache decision, decodes misses and runs the
- * grouped FFN into y, device [rows, H] fp32.  Router and shared-expert weights
+ * grouped FFN into y, device [rows, H] BF16.  Router and shared-expert weights
  * are not used.  Replaces, for the experts one rank owns,
  * ExpertDispatcher::EnqueueExpert .. Wait (csrc/dispatcher/expert_dispatcher.cpp:149-217,285-515).
  * Does not wait for the stream: it waits only for this layer's own earlier
  * copies and decodes (events). */
 zmoe_status zmoe_layer_experts(zmoe_layer* layer, const uint16_t* x_rows, const int32_t* counts_host, int rows,
-                               float* y, zmoe_stream_t stream);
+                               uint16_t* y, zmoe_stream_t stream);
 /* Same with host buffers (pinned for full speed); returns after out_host is written. */
 zmoe_status zmoe_layer_forward_host(zmoe_layer* layer, const uint16_t* x_host, int T, uint16_t* out_host,
                                     zmoe_stream_t stream);
@@ -376,6 +378,40 @@ zmoe_status zmoe_layer_prefetch(zmoe_layer* layer, const int* experts, int n, zm
  * rank and the LFU/ZipMoE victim keys); replaces
  * ZipMoECacheHandle::reset_global_access_counts (csrc/memory/cache.cpp). */
 zmoe_status zmoe_layer_reset_access_counts(zmoe_layer* layer);
+
+/* --------------------------------------------------------------------------
+ * Expert-parallel layer over NCCL (one process per GPU).
+ * Rank r owns experts [r*E/P, (r+1)*E/P) in its own zmoe_layer (created with
+ * those E_r experts and max_tokens >= P * the per-rank max_tokens below);
+ * router, shared expert and tokens are data-parallel.  A forward routes and
+ * permutes the rank's tokens, sends per-expert counts and then the BF16 rows
+ * to the experts' ranks (grouped ncclSend/ncclRecv), runs the local experts
+ * (zmoe_layer_experts: cache decision, miss decode, grouped FFN), returns the
+ * BF16 rows and combines them with the shared expert, which runs on a side
+ * stream during the exchange.  The host waits once per forward, for the
+ * counts.  Replaces, for the ranks of an expert-parallel deployment, the
+ * reference's per-rank ExpertExecutor.dispatch_local (experts/expert_executor.py:40-84)
+ * and the exchange around it.  nccl_comm is an ncclComm_t of the world ranks
+ * created by the NCCL library already loaded in the process (for example
+ * torch's ProcessGroupNCCL._comm_ptr()); every rank calls zmoe_ep_forward in
+ * the same order.  A world of 1 needs no communicator.
+ * ------------------------------------------------------------------------ */
+typedef struct zmoe_ep zmoe_ep;
+
+typedef struct zmoe_ep_config {
+  zmoe_layer_config layer;    /* the whole layer: all E experts; max_tokens per rank; cache fields unused */
+  int rank, world;
+  void* nccl_comm;            /* ncclComm_t */
+} zmoe_ep_config;
+
+zmoe_status zmoe_ep_create(const zmoe_ep_config* cfg, zmoe_layer* local, zmoe_ep** out);
+zmoe_status zmoe_ep_destroy(zmoe_ep* ep);
+/* Host pointers, copied to HBM.  bias ([E] fp32) and w_shared_gate ([H] BF16) may be NULL. */
+zmoe_status zmoe_ep_set_router(zmoe_ep* ep, const uint16_t* w_router, const float* bias,
+                               const uint16_t* w_shared_gate);
+zmoe_status zmoe_ep_set_shared(zmoe_ep* ep, const uint16_t* gate, const uint16_t* up, const uint16_t* down);
+/* x, out: device [T, H] BF16, T <= max_tokens (T = 0 still takes part in the exchanges). */
+zmoe_status zmoe_ep_forward(zmoe_ep* ep, const uint16_t* x, int T, uint16_t* out, zmoe_stream_t stream);
 
 #ifdef __cplusplus
 }

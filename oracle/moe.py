@@ -22,8 +22,9 @@ Defined orders (the reference's own order is whatever cuBLAS/MKL pick):
   polynomial, fp32, no fused multiply-add), the 32-lane strided sum + butterfly,
   and an IEEE division.  Everything is reproduced bit for bit by the kernel.
 * Top-k: larger value first, ties to the lower expert index.
-* Expert FFN accumulates in fp32; the SwiGLU intermediate is rounded to BF16
-  once; the combine accumulates in fp32 and rounds the layer output once.
+* Expert FFN accumulates in fp32; the SwiGLU intermediate and the expert
+  output are each rounded to BF16 once (the reference's libtorch FFN returns
+  BF16); the combine accumulates in fp32 and rounds the layer output once.
 """
 from __future__ import annotations
 
@@ -247,19 +248,20 @@ def permute(topk_idx: np.ndarray, E: int):
 # experts
 # --------------------------------------------------------------------------
 def swiglu_fp32(x: torch.Tensor, wg: torch.Tensor, wu: torch.Tensor, wd: torch.Tensor) -> torch.Tensor:
-    """expert_module.cpp:39-50 with fp32 accumulation and one BF16 rounding of
-    the intermediate: y = bf16(silu(x Wg^T) * (x Wu^T)) Wd^T (fp32 result)."""
+    """expert_module.cpp:39-50 with fp32 accumulation: the intermediate and the
+    output are each rounded to BF16 once, as the reference's libtorch matmuls
+    return them: y = bf16(bf16(silu(x Wg^T) * (x Wu^T)) Wd^T) (BF16 values, fp32 tensor)."""
     xf = x.float()
     g = xf @ wg.float().t()
     u = xf @ wu.float().t()
     h = (F.silu(g) * u).to(torch.bfloat16).float()
-    return h @ wd.float().t()
+    return (h @ wd.float().t()).to(torch.bfloat16).float()
 
 
 def relu_ffn_fp32(x: torch.Tensor, wi: torch.Tensor, wo: torch.Tensor) -> torch.Tensor:
-    """expert_module.cpp:67-78: y = bf16(relu(x wi^T)) wo^T (fp32 result)."""
+    """expert_module.cpp:67-78: y = bf16(bf16(relu(x wi^T)) wo^T) (BF16 values, fp32 tensor)."""
     h = F.relu(x.float() @ wi.float().t()).to(torch.bfloat16).float()
-    return h @ wo.float().t()
+    return (h @ wo.float().t()).to(torch.bfloat16).float()
 
 
 def swiglu_bf16_ref(x, wg, wu, wd):

@@ -178,7 +178,7 @@ def test_grouped_ffn_large_groups_and_split_launches(kind, G, H, I):
     wtab = ops.weight_table([dev[g % 6] for g in range(G)], "cuda")
     y, _ = ops.expert_ffn(x.cuda(), wtab, torch.from_numpy(offs).cuda(), G, I, kind)
     torch.cuda.synchronize()
-    got = y.cpu()
+    got = y.float().cpu()
     for g in range(G):
         a, b = int(offs[g]), int(offs[g + 1])
         if a == b:
@@ -199,5 +199,5 @@ def test_shared_expert_shape_one_group_512_rows():
     y, _ = ops.expert_ffn(x.cuda(), ops.weight_table([dev], "cuda"), None, 1, s.shared_inter, 0)
     torch.cuda.synchronize()
     ref = moe.swiglu_fp32(x, *sh)
-    mx, mr = _close(y.cpu().numpy(), ref.numpy())
+    mx, mr = _close(y.float().cpu().numpy(), ref.numpy())
     assert mx <= TOL_MAX_ABS and mr <= TOL_MEAN_REL, (mx, mr)

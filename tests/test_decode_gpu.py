@@ -193,3 +193,26 @@ def test_decode_small_offsets_across_segments():
         torch.cuda.synchronize()
         assert (st.cpu().numpy() == 0).all()
         assert np.array_equal(_bits(out), bits)
+
+
+def test_decode_index_of_another_block_is_reported_not_trapped():
+    """An index that does not belong to the block (the host builds it at load
+    time, so this is a caller error) must end in a status word or in the right
+    bytes, never in a fault; the context stays usable."""
+    ops = _ops()
+    gen = torch.Generator().manual_seed(31)
+    a = codec.bf16_bits((torch.randn(300, 700, generator=gen) * 0.02).to(torch.bfloat16))
+    b = codec.bf16_bits((torch.randn(300, 700, generator=gen) * 0.07).to(torch.bfloat16))
+    ba, oa, sma = codec.encode_tensor(a, 1)
+    bb, ob, smb = codec.encode_tensor(b, 1)
+    assert oa == ob
+    ct = ops.CompressedTensor(bb, ob, smb.tobytes())
+    ct.indexes = ops.CompressedTensor(ba, oa, sma.tobytes()).indexes.clone()
+    ct.index_rows = [int(ct.indexes.shape[0])]
+    out, st = ct.decode()
+    torch.cuda.synchronize()
+    code = int(st.cpu()[0])
+    assert code != 0 or np.array_equal(_bits(out), b)
+    out, st = ops.CompressedTensor(ba, oa, sma.tobytes()).decode()
+    torch.cuda.synchronize()
+    assert int(st.cpu()[0]) == 0 and np.array_equal(_bits(out), a)

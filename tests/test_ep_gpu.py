@@ -43,15 +43,17 @@ def _single(s, wr, sg, sh, bias, enc, T, device=0):
     return L
 
 
+@pytest.mark.parametrize("native", [True, False])
 @pytest.mark.parametrize("name", ["qwen", "deepseek", "switch"])
-def test_ep_one_rank_equals_layer_engine(name):
+def test_ep_one_rank_equals_layer_engine(name, native):
     from zmoe import ep
     s = SHAPES[name]
     w, wr, sg, sh, bias, enc = _inputs(s)
     T = 48
     x = syn.activations(T, s.hidden, seed=21).cuda()
     ref = _single(s, wr, sg, sh, bias, enc, T)(x)
-    layer = ep.build_gpu_layer(s, enc, wr, bias, sg, sh, max_tokens=T, cache_slots=2, device=0, warm=[0, 1])
+    layer = ep.build_gpu_layer(s, enc, wr, bias, sg, sh, max_tokens=T, cache_slots=2, device=0, warm=[0, 1],
+                               native=native)
     for _ in range(2):                                   # cold, then with cache state
         out = layer(x)
         torch.cuda.synchronize()

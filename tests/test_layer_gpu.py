@@ -124,7 +124,7 @@ def test_grouped_ffn_matches_oracle(kind):
             ref[a:b] = moe.swiglu_fp32(x[a:b], *mats[g])
         else:
             ref[a:b] = moe.relu_ffn_fp32(x[a:b], mats[g][0], mats[g][2])
-    mx, mr = _close(y[:R].cpu().numpy(), ref.numpy())
+    mx, mr = _close(y[:R].float().cpu().numpy(), ref.numpy())
     assert mx < TOL_MAX_ABS and mr < TOL_MEAN_REL, (mx, mr)
 
 

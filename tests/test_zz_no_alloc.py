@@ -35,7 +35,7 @@ def _case(seed, kind, rows, H=512, I=320):
 
 def _call(fn, x, wtab, offsets, G, R, H, I, kind, h):
     from zmoe._lib import FfnArgs, check
-    y = torch.full((R, H), float("nan"), dtype=torch.float32, device="cuda")
+    y = torch.full((R, H), float("nan"), dtype=torch.bfloat16, device="cuda")
     a = FfnArgs(x.data_ptr(), wtab.data_ptr(), offsets.data_ptr(), G, R, H, I, kind,
                 h.data_ptr() if h is not None else None, y.data_ptr())
     check(fn(ctypes.byref(a), torch.cuda.current_stream().cuda_stream), fn.__name__)

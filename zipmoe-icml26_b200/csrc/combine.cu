@@ -3,15 +3,20 @@
 // Replaces the per-expert Python loops of customized/qwen.py:89-100,
 // customized/deepseek.py:103-115 and customized/switch_transformers.py:83-87,
 // which accumulate into a BF16 buffer in completion order.  Here each thread
-// owns 4 consecutive hidden elements of one token, sums the k expert rows in
-// slot order in fp32, adds the (optionally gated) shared-expert row and rounds
-// once to BF16.
+// owns 4 consecutive hidden elements of one token, sums the k BF16 expert rows
+// in slot order in fp32, adds the (optionally gated) shared-expert row and
+// rounds once to BF16.
 #include "common.cuh"
 
 namespace zmoe {
 namespace {
 
 constexpr int kThreads = 256;
+
+__device__ __forceinline__ float4 bf16x4(uint2 b) {
+  return make_float4(__uint_as_float(b.x << 16), __uint_as_float(b.x & 0xffff0000u), __uint_as_float(b.y << 16),
+                     __uint_as_float(b.y & 0xffff0000u));
+}
 
 __global__ void __launch_bounds__(kThreads)
 combine_kernel(const zmoe_combine_args a) {
@@ -23,21 +28,15 @@ combine_kernel(const zmoe_combine_args a) {
   if (a.mode == ZMOE_ROUTE_SWITCH) {
     const int r = a.row_of[(size_t)t * k];
     const float w = a.topk_w[(size_t)t * k];
-    float4 v;
-    if (r >= 0) {
-      v = __ldg(reinterpret_cast<const float4*>(a.y + (size_t)r * H + h));
-    } else {
-      const uint2 xb = __ldg(reinterpret_cast<const uint2*>(a.x + (size_t)t * H + h));
-      v = make_float4(__uint_as_float(xb.x << 16), __uint_as_float(xb.x & 0xffff0000u),
-                      __uint_as_float(xb.y << 16), __uint_as_float(xb.y & 0xffff0000u));
-    }
+    const uint16_t* src = r >= 0 ? a.y + (size_t)r * H + h : a.x + (size_t)t * H + h;
+    const float4 v = bf16x4(__ldg(reinterpret_cast<const uint2*>(src)));
     acc = make_float4(w * v.x, w * v.y, w * v.z, w * v.w);
   } else {
     for (int j = 0; j < k; ++j) {
       const int r = a.row_of[(size_t)t * k + j];
       if (r < 0) continue;
       const float w = a.topk_w[(size_t)t * k + j];
-      const float4 v = __ldg(reinterpret_cast<const float4*>(a.y + (size_t)r * H + h));
+      const float4 v = bf16x4(__ldg(reinterpret_cast<const uint2*>(a.y + (size_t)r * H + h)));
       acc.x = fmaf(w, v.x, acc.x);
       acc.y = fmaf(w, v.y, acc.y);
       acc.z = fmaf(w, v.z, acc.z);
@@ -45,7 +44,7 @@ combine_kernel(const zmoe_combine_args a) {
     }
     if (a.y_shared) {
       const float g = a.shared_gate ? a.shared_gate[t] : 1.0f;
-      const float4 v = __ldg(reinterpret_cast<const float4*>(a.y_shared + (size_t)t * H + h));
+      const float4 v = bf16x4(__ldg(reinterpret_cast<const uint2*>(a.y_shared + (size_t)t * H + h)));
       acc.x = fmaf(g, v.x, acc.x);
       acc.y = fmaf(g, v.y, acc.y);
       acc.z = fmaf(g, v.z, acc.z);

@@ -95,7 +95,8 @@ struct Layer {
   // workspace
   int max_rows = 0;
   int32_t *idx = nullptr, *counts = nullptr, *offsets = nullptr, *row_of = nullptr, *tor = nullptr;
-  float *tw = nullptr, *sg = nullptr, *y = nullptr, *ysh = nullptr;
+  float *tw = nullptr, *sg = nullptr;
+  uint16_t *y = nullptr, *ysh = nullptr;              // BF16 expert rows
   uint16_t *xp = nullptr, *h = nullptr, *hsh = nullptr;
   zmoe_chunk* desc_dev = nullptr;
   int32_t* status_dev = nullptr;
@@ -167,13 +168,13 @@ struct Layer {
   zmoe_status init(const zmoe_layer_config& c);
   zmoe_status forward(const uint16_t* x, int T, uint16_t* out, cudaStream_t s);
   zmoe_status run_experts(const uint16_t* xrows, const int32_t* offsets_dev, const int32_t* counts_h, int rows,
-                          float* yrows, cudaStream_t s, bool caller_marked);
-  zmoe_status experts(const uint16_t* xrows, const int32_t* counts_h, int rows, float* yrows, cudaStream_t s);
+                          uint16_t* yrows, cudaStream_t s, bool caller_marked);
+  zmoe_status experts(const uint16_t* xrows, const int32_t* counts_h, int rows, uint16_t* yrows, cudaStream_t s);
   zmoe_status check_status();
   int choose_victim(const std::vector<char>& active);
   zmoe_status decode_into(const std::vector<std::pair<int, int>>& jobs, cudaStream_t s);
   zmoe_status ffn_over(const std::vector<std::pair<int, int>>& groups, int table, const uint16_t* xrows,
-                       const int32_t* offsets_dev, int rows, float* yrows, cudaStream_t s);
+                       const int32_t* offsets_dev, int rows, uint16_t* yrows, cudaStream_t s);
   uint16_t* slot_ptr(int slot, int t) const { return slots + ((size_t)slot * tensors + t) * numel; }
 };
 
@@ -276,9 +277,9 @@ zmoe_status Layer::init(const zmoe_layer_config& c) {
   tor = dmalloc<int32_t>((size_t)T * k, &st);
   xp = dmalloc<uint16_t>((size_t)max_rows * H, &st);
   h = dmalloc<uint16_t>((size_t)max_rows * c.inter, &st);
-  y = dmalloc<float>((size_t)max_rows * H, &st);
+  y = dmalloc<uint16_t>((size_t)max_rows * H, &st);
   if (c.shared_inter > 0) {
-    ysh = dmalloc<float>((size_t)T * H, &st);
+    ysh = dmalloc<uint16_t>((size_t)T * H, &st);
     hsh = dmalloc<uint16_t>((size_t)T * c.shared_inter, &st);
   }
   max_waves = (E + n_transient - 1) / n_transient + 1;
@@ -526,7 +527,7 @@ zmoe_status Layer::decode_into(const std::vector<std::pair<int, int>>& jobs, cud
 // Grouped FFN over the given (expert, slot) groups on stream s; the other
 // groups of the launch are skipped.  table: which host weight table to fill.
 zmoe_status Layer::ffn_over(const std::vector<std::pair<int, int>>& groups, int table, const uint16_t* xrows,
-                            const int32_t* offsets_dev, int rows, float* yrows, cudaStream_t s) {
+                            const int32_t* offsets_dev, int rows, uint16_t* yrows, cudaStream_t s) {
   if (groups.empty()) return ZMOE_OK;
   const int E = cfg.num_experts;
   if (table > max_waves) { set_error("too many decode waves"); return ZMOE_EUNSUPPORTED; }
@@ -562,7 +563,7 @@ zmoe_status Layer::ffn_over(const std::vector<std::pair<int, int>>& groups, int 
 // caller_marked: ev_caller was recorded on s before any work of this call
 // (otherwise it is recorded here).
 zmoe_status Layer::run_experts(const uint16_t* xrows, const int32_t* offsets_dev, const int32_t* counts_h, int rows,
-                               float* yrows, cudaStream_t s, bool caller_marked) {
+                               uint16_t* yrows, cudaStream_t s, bool caller_marked) {
   const int E = cfg.num_experts;
   zmoe_status st;
   // 3. cache decisions (ProactiveDecision)
@@ -652,7 +653,8 @@ zmoe_status Layer::run_experts(const uint16_t* xrows, const int32_t* offsets_dev
 
 // Expert stage alone, for callers that route and exchange rows themselves
 // (expert parallelism): counts_h[e] rows of local expert e, grouped in order.
-zmoe_status Layer::experts(const uint16_t* xrows, const int32_t* counts_h, int rows, float* yrows, cudaStream_t s) {
+zmoe_status Layer::experts(const uint16_t* xrows, const int32_t* counts_h, int rows, uint16_t* yrows,
+                           cudaStream_t s) {
   const int E = cfg.num_experts;
   ZMOE_CHECK_ARG(counts_h && (rows == 0 || (xrows && yrows)), "experts: null pointer");
   ZMOE_CHECK_ARG(rows >= 0 && rows <= max_rows, "experts: rows=%d outside [0, max_tokens*topk=%d]", rows, max_rows);
@@ -994,7 +996,7 @@ zmoe_status zmoe_layer_forward(zmoe_layer* layer, const uint16_t* x, int T, uint
 }
 
 zmoe_status zmoe_layer_experts(zmoe_layer* layer, const uint16_t* x_rows, const int32_t* counts_host, int rows,
-                               float* y, zmoe_stream_t stream) {
+                               uint16_t* y, zmoe_stream_t stream) {
   Layer* L = reinterpret_cast<Layer*>(layer);
   ZMOE_CHECK_ARG(L, "experts: null layer");
   return L->experts(x_rows, counts_host, rows, y, reinterpret_cast<cudaStream_t>(stream));

@@ -7,7 +7,7 @@
 //
 // Two persistent launches per layer:
 //   up:   h[t, i] = bf16( silu(sum_k Wg[i,k] x[t,k]) * sum_k Wu[i,k] x[t,k] )   (or relu(Wi x))
-//   down: y[t, j] = sum_i Wd[j,i] h[t,i]                                        (fp32)
+//   down: y[t, j] = bf16( sum_i Wd[j,i] h[t,i] )
 // Both are "swap-AB" GEMMs: the weight rows are the MMA M dimension (128 per
 // tile), the group's tokens are the N dimension (up to 128 per tile), so a
 // group with a handful of tokens still streams its weights at full width.
@@ -57,7 +57,7 @@ struct __align__(64) Params {
   CUtensorMap amap[kMaxMaps];         // weight (A) maps: MODE 0 uses 2 per group
   CUtensorMap bmap;                   // activation (B) map over [rows_total, K]
   const int32_t* offsets;             // [G_all + 1] device, or nullptr: one group of rows_total
-  void* out;                          // h (bf16) or y (fp32), row-major [rows_total, n_out]
+  void* out;                          // h or y (BF16), row-major [rows_total, n_out]
   int g_begin, g_count;               // groups of this launch (offset into offsets)
   int rows_total, K, n_out;           // n_out = weight rows of one matrix (I or H)
   int32_t* err;                       // caller's error word (device) or nullptr
@@ -168,7 +168,7 @@ __device__ __forceinline__ float silu(float g) { return g / (1.0f + __expf(-g));
 // ---------------------------------------------------------------------------
 // kernel
 // ---------------------------------------------------------------------------
-template <int MODE>  // 0: SwiGLU up (gate+up maps), 1: ReLU up, 2: down (fp32 out)
+template <int MODE>  // 0: SwiGLU up (gate+up maps), 1: ReLU up, 2: down (BF16 out)
 __global__ void __launch_bounds__(kThreads, 1) ffn_tc_kernel(const __grid_constant__ Params p) {
   constexpr int NA = MODE == 0 ? 2 : 1;
   constexpr int STAGES = MODE == 0 ? 4 : 6;
@@ -355,7 +355,7 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_tc_kernel(const __grid_consta
           } else if (MODE == 1) {
             static_cast<uint16_t*>(p.out)[o] = f32_to_bf16_bits(fmaxf(v, 0.0f));
           } else {
-            static_cast<float*>(p.out)[o] = v;
+            static_cast<uint16_t*>(p.out)[o] = f32_to_bf16_bits(v);
           }
         }
       }

@@ -766,11 +766,11 @@ class Dispatcher {
         check(zmoe_gather_rows(x.data_ptr(), idx.data_ptr<int32_t>(), rows, (int)(H * 2), xg.data_ptr(),
                                current_stream()),
               "zmoe_gather_rows");
-        auto yf = torch::empty({rows, H}, x.options().dtype(torch::kFloat32));
+        auto yf = torch::empty({rows, H}, x.options().dtype(torch::kBFloat16));
         check(zmoe_layer_experts(eng.L, reinterpret_cast<const uint16_t*>(xg.data_ptr()), counts.data(), rows,
-                                 yf.data_ptr<float>(), current_stream()),
+                                 reinterpret_cast<uint16_t*>(yf.data_ptr()), current_stream()),
               "zmoe_layer_experts");
-        y = yf.to(torch::kBFloat16);                 // the reference's experts return BF16
+        y = yf;                                      // BF16, as the reference's experts return it
       }
       std::vector<int64_t> start(E_ + 1, 0);
       for (int e = 0; e < E_; ++e) start[e + 1] = start[e] + counts[e];

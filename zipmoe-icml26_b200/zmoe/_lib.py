@@ -68,6 +68,10 @@ class LayerStats(ctypes.Structure):
         "host_copy_bytes")]
 
 
+class EPConfig(ctypes.Structure):
+    _fields_ = [("layer", LayerConfig), ("rank", c_int), ("world", c_int), ("nccl_comm", c_void_p)]
+
+
 # (name, restype, argtypes) of every exported symbol; tests check the header
 # declares exactly these.
 SIGNATURES = {
@@ -111,6 +115,11 @@ SIGNATURES = {
     "zmoe_layer_prefetch": (c_int, [c_void_p, ctypes.POINTER(c_int), c_int, c_void_p]),
     "zmoe_layer_cached_experts": (c_int, [c_void_p, ctypes.POINTER(ctypes.c_int32), c_int,
                                           ctypes.POINTER(c_int)]),
+    "zmoe_ep_create": (c_int, [ctypes.POINTER(EPConfig), c_void_p, ctypes.POINTER(c_void_p)]),
+    "zmoe_ep_destroy": (c_int, [c_void_p]),
+    "zmoe_ep_set_router": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p]),
+    "zmoe_ep_set_shared": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p]),
+    "zmoe_ep_forward": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p]),
 }
 
 

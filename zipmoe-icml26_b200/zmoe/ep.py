@@ -12,16 +12,19 @@ One forward on every rank:
 3. all-to-all of the permuted BF16 rows (sizes from the counts);
 4. regroup the received rows by local expert (a row gather);
 5. the expert stage of the local engine (cache decision, miss decode on the
-   GPU, tcgen05 grouped FFN) -> fp32 rows;
-6. inverse regroup, all-to-all of the fp32 rows back to their token's rank;
+   GPU, tcgen05 grouped FFN) -> BF16 rows;
+6. inverse regroup, all-to-all of the BF16 rows back to their token's rank;
 7. shared expert and gate-weighted combine on the local tokens.
 
 This is the exchange the reference's vendored DeepSeek expert parallelism and
 its dispatcher imply (``experts/expert_executor.py:40-84`` drives one rank's
 experts; ``csrc/dispatcher/expert_dispatcher.cpp:326-330`` gathers an expert's
-rows).  The collectives go through ``torch.distributed`` (NCCL on GPUs); the
-arithmetic goes through the C ABI of libzmoe.so (``EPKernels``).  A kernel set
-with the same methods can be passed in place of ``EPKernels``.
+rows).  Two implementations: :class:`NativeEPLayer` runs the whole forward in
+libzmoe.so (zmoe_ep_forward, NCCL point-to-point calls on the group's own
+communicator, one host wait per forward); :class:`EPMoELayer` runs the same
+steps in Python over ``torch.distributed`` with the arithmetic behind an
+object (``EPKernels`` on a GPU, or the oracle's kernels on the CPU for gloo
+tests).
 """
 from __future__ import annotations
 
@@ -187,18 +190,84 @@ class EPMoELayer:
             if y_sh is not None:
                 y_sh.record_stream(torch.cuda.current_stream(x.device))
         if n_send == 0:                                   # every token dropped (Switch capacity)
-            y_back = torch.zeros(1, H, dtype=torch.float32, device=x.device)
+            y_back = torch.zeros(1, H, dtype=y_src.dtype, device=x.device)
         return self.K.combine(y_back, row_of, tw, sg, y_sh, x)
 
     __call__ = forward
 
 
+def nccl_comm_ptr(device: int, group=None) -> int:
+    """The ncclComm_t (as an integer) of a torch.distributed NCCL group on
+    this rank's GPU; a barrier first makes sure the communicator exists."""
+    pg = group if group is not None else dist.distributed_c10d._get_default_group()
+    dist.barrier(group=pg)
+    return int(pg._get_backend(torch.device("cuda", device))._comm_ptr())
+
+
+class NativeEPLayer:
+    """One rank's share of an expert-parallel MoE layer, run by libzmoe.so
+    (zmoe_ep_forward): routing, NCCL exchanges of counts and BF16 rows, the
+    local engine's expert stage and the combine, in C++ with one host wait per
+    forward.  ``local`` is the :class:`MoELayer` holding this rank's experts."""
+
+    def __init__(self, shape: LayerShape, local, w_router, bias, w_shared_gate, shared, max_tokens: int,
+                 device: int, group=None):
+        import ctypes
+        from ._lib import EPConfig, LayerConfig, check, lib
+        from .layer import route_mode
+        self.s, self.local, self.engine = shape, local, local
+        self.P = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.device = torch.device("cuda", device)
+        comm = nccl_comm_ptr(device, group) if self.P > 1 else None
+        lc = LayerConfig(shape.hidden, shape.num_experts, shape.inter, shape.topk, shape.kind, route_mode(shape), 0,
+                         shape.scaling, shape.shared_inter, shape.capacity, shape.seq_len, max_tokens, 0, 0, 0, 0.0)
+        cfg = EPConfig(lc, self.rank, self.P, comm)
+        h = ctypes.c_void_p()
+        check(lib.zmoe_ep_create(ctypes.byref(cfg), local._h, ctypes.byref(h)), "zmoe_ep_create")
+        self._h, self._lib, self._check = h, lib, check
+        host = lambda t: None if t is None else t.detach().contiguous().cpu()
+        self._keep = [host(w_router.to(torch.bfloat16)), host(bias.to(torch.float32)) if bias is not None else None,
+                      host(w_shared_gate.to(torch.bfloat16)) if w_shared_gate is not None else None]
+        ptr = lambda t: None if t is None else t.data_ptr()
+        check(lib.zmoe_ep_set_router(h, *[ptr(t) for t in self._keep]), "zmoe_ep_set_router")
+        if shared is not None:
+            sh = [host(t.to(torch.bfloat16)) for t in shared]
+            check(lib.zmoe_ep_set_shared(h, *[t.data_ptr() for t in sh]), "zmoe_ep_set_shared")
+        self.max_tokens = max_tokens
+
+    def forward(self, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if not x.is_cuda or x.dtype != torch.bfloat16 or not x.is_contiguous():
+            raise ValueError("x must be a contiguous CUDA BF16 tensor")
+        if out is None:
+            out = torch.empty_like(x)
+        self._check(self._lib.zmoe_ep_forward(self._h, x.data_ptr(), x.shape[0], out.data_ptr(),
+                                              torch.cuda.current_stream(self.device).cuda_stream), "zmoe_ep_forward")
+        return out
+
+    __call__ = forward
+
+    def close(self):
+        if getattr(self, "_h", None):
+            self._lib.zmoe_ep_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 def build_gpu_layer(shape: LayerShape, experts_encoded, w_router, bias, w_shared_gate, shared, max_tokens: int,
-                    cache_slots: int, device: int, group=None, warm: Sequence[int] = ()):
-    """EPMoELayer on this rank's GPU.  experts_encoded[e] = encoded tensors of
-    global expert e (zmoe.codec.EncodedTensor; None for experts other ranks
-    own); only the owned experts are loaded.  max_tokens bounds the tokens of one rank; warm = global expert ids
-    to decode into the cache up front (those this rank owns)."""
+                    cache_slots: int, device: int, group=None, warm: Sequence[int] = (), native: bool = True):
+    """This rank's share of an expert-parallel layer on its GPU.
+    experts_encoded[e] = encoded tensors of global expert e (EncodedTensor;
+    None for experts other ranks own); only the owned experts are loaded.
+    max_tokens bounds the tokens of one rank; warm = global expert ids to
+    decode into the cache up front (those this rank owns).  native: the C++
+    layer (NativeEPLayer, NCCL from libzmoe.so); otherwise the Python
+    exchange (EPMoELayer over torch.distributed)."""
     from .layer import MoELayer
     P = dist.get_world_size(group) if dist.is_initialized() else 1
     rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -212,6 +281,8 @@ def build_gpu_layer(shape: LayerShape, experts_encoded, w_router, bias, w_shared
     w = [e - mine.start for e in warm if e in mine]
     if w:
         local.warm_cache(w[:local_cache_cap(cache_slots, len(mine))])
+    if native:
+        return NativeEPLayer(shape, local, w_router, bias, w_shared_gate, shared, max_tokens, device, group)
     kern = EPKernels(shape, w_router, bias, w_shared_gate, shared, torch.device("cuda", device))
     layer = EPMoELayer(shape, kern, local, group)
     layer.engine = local

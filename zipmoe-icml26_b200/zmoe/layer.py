@@ -146,7 +146,7 @@ class MoELayer:
 
     def experts(self, x_rows: torch.Tensor, counts, y: Optional[torch.Tensor] = None) -> torch.Tensor:
         """Expert stage alone (zmoe_layer_experts): x_rows [rows, H] BF16 grouped
-        by this layer's experts, counts[e] rows of expert e; returns fp32 [rows, H]."""
+        by this layer's experts, counts[e] rows of expert e; returns BF16 [rows, H]."""
         import numpy as np
         c = np.ascontiguousarray(np.asarray(counts, dtype=np.int32))
         if c.size != self.shape.num_experts:
@@ -156,7 +156,7 @@ class MoELayer:
                      or x_rows.shape[0] < rows):
             raise ValueError("x_rows must be a contiguous CUDA BF16 tensor with sum(counts) rows")
         if y is None:
-            y = torch.empty(rows, self.shape.hidden, dtype=torch.float32, device=self.device)
+            y = torch.empty(rows, self.shape.hidden, dtype=torch.bfloat16, device=self.device)
         check(lib.zmoe_layer_experts(self._h, x_rows.data_ptr() if rows else None,
                                      c.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), rows,
                                      y.data_ptr() if rows else None,

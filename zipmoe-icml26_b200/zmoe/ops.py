@@ -208,7 +208,7 @@ def expert_ffn(x: torch.Tensor, wtab: torch.Tensor, offsets: Optional[torch.Tens
     rows = x.shape[0] if rows_total is None else rows_total
     H = x.shape[1]
     h = torch.empty(max(rows, 1), I, dtype=torch.bfloat16, device=x.device)
-    y = torch.empty(max(rows, 1), H, dtype=torch.float32, device=x.device)
+    y = torch.empty(max(rows, 1), H, dtype=torch.bfloat16, device=x.device)
     a = FfnArgs(x.data_ptr(), wtab.data_ptr(), _ptr(offsets), G, rows, H, I, kind, h.data_ptr(), y.data_ptr())
     check(lib.zmoe_expert_ffn(ctypes.byref(a), _stream()), "zmoe_expert_ffn")
     return y, h
