@@ -499,18 +499,24 @@ def run_ep(args):
 
     for _ in range(2):
         host_step()
-    barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(args.steps):
-        host_step()
-    e1.record(stream)
-    torch.cuda.synchronize()
+    with ClockSampler(local if rank == 0 else None) as clk2:   # its driver reading comes before the barrier
+        barrier()
+        e0.record(stream)
+        for i in range(args.steps):
+            clk2.probe(i, args.steps)                 # the same side-stream probes as the device-timed loop
+            host_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
     barrier()
     e2e_ms = e0.elapsed_time(e1) / args.steps
-    t = torch.tensor([ms, e2e_ms], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, e2e_ms = float(t[0]), float(t[1])
+    # every rank's own step times, then the max over ranks
+    per = torch.tensor([ms, e2e_ms], dtype=torch.float64, device="cuda")
+    gathered = [torch.zeros_like(per) for _ in range(world)]
+    dist.all_gather(gathered, per)
+    per_rank = [[round(float(g[0]), 4), round(float(g[1]), 4)] for g in gathered]
+    ms = max(p[0] for p in per_rank)
+    e2e_ms = max(p[1] for p in per_rank)
     clocks = clk.summary()
     if rank == 0:
         hbm, tfl, src = peaks()
@@ -518,6 +524,7 @@ def run_ep(args):
         launches = max(st["decode_timed_launches"], 1)
         achieved = (st["decode_timed_bytes"] / launches) / (dec_s / launches) / 1e9 if dec_s > 0 else 0.0
         # per step: router 1, permute 3, gathers 2, shared FFN 2, combine 1 + the engine's own
+        # (NCCL's own kernels are not counted)
         ep_launches = 9 * args.steps
         line = {
             "metric": METRIC, "value": world * args.tokens / (ms / 1e3), "unit": UNIT, "n_gpus": world,
@@ -526,7 +533,9 @@ def run_ep(args):
             "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations)",
             "config": bench_config(args, s, world),
             "ep": {"cached_experts_rank0": cache, "experts_rank0": len(mine),
-                   "exchange": "NCCL all-to-all (counts, BF16 rows out, fp32 rows back)"},
+                   "exchange": "libzmoe.so zmoe_ep_forward: grouped ncclSend/ncclRecv of counts, BF16 rows out "
+                               "and BF16 rows back on torch's NCCL communicator; one host wait per step",
+                   "per_rank_ms_value_e2e": per_rank},
             "e2e": {"value": world * args.tokens / (e2e_ms / 1e3), "unit": UNIT,
                     "h2d_bytes_per_step": x.numel() * 2, "d2h_bytes_per_step": x.numel() * 2},
             "roofline": {"bound": "hbm", "kernel": "map_kernel+resolve_kernel (fused LZ4 decode)", "achieved": achieved,
@@ -540,6 +549,9 @@ def run_ep(args):
             "clocks": clocks,
         }
         print(json.dumps(line), flush=True)
+    torch.cuda.synchronize()
+    if hasattr(L, "close"):
+        L.close()                                      # the native layer before its engine and the communicator
     eng.close()
     dist.barrier()
     dist.destroy_process_group()
