@@ -36,6 +36,7 @@ for _p in (ROOT, PKG):
     if _p not in sys.path:
         sys.path.insert(0, _p)
 
+import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
 METRIC = "MoE-layer tokens/s"
@@ -56,6 +57,10 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--store", default="device", choices=["device", "host"],
                     help="where the compressed experts live (host: pinned memory, copied in per miss)")
+    ap.add_argument("--config", default="qwen", choices=["qwen", "decode-sweep", "switch"],
+                    help="qwen: the Qwen1.5-MoE layer (default; the headline line, with a token-count sweep); "
+                         "decode-sweep: decode+recombine GB/s over sizes and weight distributions; "
+                         "switch: the Switch-large-128 layer at 4096 tokens")
     ap.add_argument("--timeline", default=None,
                     help="write the GPU timeline of 3 more steps (kernels and copies per stream, "
                          "torch.profiler over CUPTI) to this text file")
@@ -363,6 +368,7 @@ def run_ours(args):
     L.set_timing(False)
     if args.timeline and rank == 0:
         write_timeline(lambda: L.forward(x, out), 3, args.timeline)
+    sweep = token_sweep(L, s, args) if args.config == "qwen" else None
 
     # end to end through the public API with pinned host buffers: every step
     # copies its input in and its output back (zmoe_layer_submit_host, copies
@@ -425,6 +431,8 @@ def run_ours(args):
             "gpu_launches": st["launches"],
             "clocks": clocks,
         }
+        if sweep is not None:
+            line["tokens_sweep"] = sweep
         if cpu is not None:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
@@ -557,6 +565,315 @@ def run_ep(args):
     dist.destroy_process_group()
 
 
+def token_sweep(L, s, args):
+    """The same layer (same cache state going in) at the other batch sizes of
+    the Qwen config: tokens/s, step time and experts decoded per step."""
+    from zmoe import synthetic as syn
+    out = {}
+    for T in (1, 16, 128):
+        xs = syn.activations(T, s.hidden, seed=50 + T).cuda()
+        os_ = torch.empty_like(xs)
+        for _ in range(3):
+            L.forward(xs, os_)
+        L.sync()
+        before = L.stats()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(args.steps):
+            L.forward(xs, os_)
+        b.record()
+        torch.cuda.synchronize()
+        L.sync()
+        ms = a.elapsed_time(b) / args.steps
+        st = L.stats()
+        dec = (st["decoded_experts"] - before["decoded_experts"]) / args.steps
+        touched = (st["hits"] + st["misses"] - before["hits"] - before["misses"]) / args.steps
+        out[str(T)] = {"tokens_per_s": T / (ms * 1e-3), "ms_per_step": ms, "experts_touched_per_step": touched,
+                       "experts_decoded_per_step": dec}
+    return out
+
+
+def weight_family(name: str, scale: float, shape, seed: int):
+    """BF16 matrices whose exponent planes compress differently: normal(sd),
+    laplace(b) and uniform(+-a) draws, seeded."""
+    gen = torch.Generator().manual_seed(seed)
+    if name == "normal":
+        w = torch.randn(*shape, generator=gen) * scale
+    elif name == "laplace":
+        u = torch.rand(*shape, generator=gen) - 0.5
+        w = -scale * torch.sign(u) * torch.log1p(-2 * u.abs())
+    else:
+        w = (torch.rand(*shape, generator=gen) * 2 - 1) * scale
+    return w.to(torch.bfloat16)
+
+
+def run_decode_sweep(args):
+    """Decode+recombine throughput over total sizes and weight distributions
+    (the decompression-bandwidth sweep): for each family a pool of 8 distinct
+    Qwen-shaped matrices is encoded (LZ4HC-9, 3 chunks), copied on the device
+    until the requested size is reached (every copy has its own source bytes,
+    so nothing is served from L2), and decoded in launches of up to 1 GiB of
+    output.  Each rank decodes its own copies (weak scaling); value is the
+    sum over ranks at the largest size for normal(0.02)."""
+    import datetime
+    from zmoe import codec as zc
+    from zmoe import ops
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+    families = [("normal", 0.005), ("normal", 0.02), ("normal", 0.08), ("normal", 0.0283), ("laplace", 0.02),
+                ("uniform", 0.05)]
+    sizes_mb = [1, 16, 256, 1024, 4096, 8192]
+    shape = (1408, 2048)
+    n_el = shape[0] * shape[1]
+    results = []
+    hbm, _, src = peaks()
+    threads = max(1, (os.cpu_count() or 1) // world)
+    for fi, (fam, scale) in enumerate(families):
+        pool = [weight_family(fam, scale, shape, 1000 * fi + i) for i in range(8)]
+        enc = zc.encode_tensors(pool, args.chunks, args.codec, args.level, threads)
+        ratio = sum(e.compressed_bytes for e in enc) / sum(e.numel for e in enc)
+        base = [ops.CompressedTensor(e.blocks, e.original_sizes, e.sm) for e in enc]
+        for mb in sizes_mb:
+            n_mat = max(1, int(round(mb * 2 ** 20 / (2 * n_el))))
+            small = mb * 2 ** 20 < 2 * n_el
+            if small:                                   # 1 MB: the leading rows of one matrix
+                rows = max(1, mb * 2 ** 20 // (2 * shape[1]))
+                e = zc.encode_tensors([pool[0][:rows]], args.chunks, args.codec, args.level, threads)[0]
+                cts = [ops.CompressedTensor(e.blocks, e.original_sizes, e.sm)]
+                n_out = [e.numel]
+            else:
+                cts = []
+                for i in range(n_mat):
+                    b = base[i % len(base)]
+                    c = object.__new__(ops.CompressedTensor)
+                    c.__dict__.update(b.__dict__)
+                    if i >= len(base):                  # its own device copy of the source bytes
+                        c.blocks, c.sm = b.blocks.clone(), b.sm.clone()
+                        c.indexes = b.indexes.clone()
+                    cts.append(c)
+                n_out = [n_el] * n_mat
+            total = sum(n_out)
+            dst = torch.empty(total, dtype=torch.bfloat16, device="cuda")
+            launches, pos, cur = [], 0, []
+            cap = 2 ** 29                               # elements (1 GiB of BF16) per launch
+            for c, n in zip(cts, n_out):
+                if cur and sum(d[4] for d in cur) + n > cap:
+                    launches.append(cur)
+                    cur = []
+                cur.extend(c.descs(dst[pos:pos + n]))
+                pos += n
+            launches.append(cur)
+            tables = []
+            for d in launches:
+                scratch = ops.map_scratch([x[4] for x in d], "cuda")
+                tables.append((ops.chunk_table(d, "cuda", scratch), len(d), scratch,
+                               torch.zeros(len(d), dtype=torch.int32, device="cuda")))
+            alg = sum(x[3] + 3 * x[4] for d in launches for x in d)
+
+            def once():
+                for tab, n, _, st in tables:
+                    ops.check(ops.lib.zmoe_decode_chunks(tab.data_ptr(), n, st.data_ptr(),
+                                                         torch.cuda.current_stream().cuda_stream), "decode")
+            for _ in range(2):
+                once()
+            torch.cuda.synchronize()
+            if dist is not None:
+                dist.barrier()
+            reps = max(1, min(args.steps, int(2e9 // max(alg, 1)) + 1))
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            for _ in range(reps):
+                once()
+            b.record()
+            torch.cuda.synchronize()
+            ms = a.elapsed_time(b) / reps
+            ok = all(bool((t[3] == 0).all()) for t in tables)
+            if mb == sizes_mb[-1] or small:             # bit-exact check of the first matrix
+                want = codec_bits(pool[0][:rows] if small else pool[0])
+                ok = ok and torch.equal(dst[:want.numel()].view(torch.int16).cpu(), want)
+            t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+            if dist is not None:
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t[0])
+            gbs = world * alg / (ms * 1e-3) / 1e9
+            results.append({"family": f"{fam}({scale})", "exp_ratio": round(ratio, 4), "size_mb": mb,
+                            "chunks": sum(len(d) for d in launches), "ms": round(ms, 4), "gb_per_s": round(gbs, 1),
+                            "frac_of_hbm": round(gbs / world / hbm, 4), "status_ok": ok})
+            del tables, dst, cts
+            torch.cuda.empty_cache()
+    head = [r for r in results if r["family"] == "normal(0.02)" and r["size_mb"] == sizes_mb[-1]][0]
+    if rank == 0:
+        cpu = cpu_decode_baseline(args) if not args.no_cpu_baseline and world == 1 else None
+        line = {"metric": "expert decode+recombine GB/s (algorithmic bytes)", "value": head["gb_per_s"],
+                "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": 2,
+                "ms_per_step": head["ms"], "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "u8", "data": "synthetic (seeded weight families, see results)",
+                "config": {"workload": "decode-sweep", "codec": f"{args.codec}-{args.level}",
+                           "num_file_chunks": args.chunks, "sizes_mb_per_gpu": sizes_mb,
+                           "l2": "inputs larger than L2 from 256 MB up"},
+                "roofline": {"bound": "hbm", "achieved": head["gb_per_s"] / world, "peak": hbm, "unit": "GB/s",
+                             "frac": head["gb_per_s"] / world / hbm, "peak_source": src, "traffic": None},
+                "results": results}
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_switch(args):
+    """Switch-large-128 layer (d_model 1024, 128 ReLU experts of 2816, top-1,
+    capacity factor 1.25, overflow tokens passed through) over 4096 tokens:
+    one GPU holds all 128 experts (16 decoded in the cache, the rest
+    compressed); under torchrun the experts are sharded (16 per GPU at 8 GPUs)
+    and each rank routes 4096 / N tokens as its own sequence, so the capacity
+    is floor(1.25 * (4096 / N) / 128) per rank."""
+    import dataclasses
+    import datetime
+    from zmoe import ep
+    from zmoe import synthetic as syn
+    from zmoe.layer import MoELayer
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+    T = 4096 // world
+    s = dataclasses.replace(syn.SWITCH, capacity=(125 * T) // (100 * syn.SWITCH.num_experts), seq_len=T)
+    w = syn.expert_weights(s, 1)[0]
+    wr, _ = syn.router_weights(s)
+    threads = max(1, (os.cpu_count() or 1) // world)
+    cache = max(1, 16 // world)
+    if world == 1:
+        L = MoELayer(s, max_tokens=T, cache_slots=cache, device=local)
+        L.set_router(wr, None, None)
+        L.load_experts(w, num_file_chunks=args.chunks, codec=args.codec, level=args.level, threads=threads)
+        eng = L
+    else:
+        from zmoe import codec as zc
+        part = ep.ExpertPartition(s.num_experts, world)
+        mine = part.owned(rank)
+        flat = zc.encode_tensors([t for e in mine for t in w[e]], args.chunks, args.codec, args.level, threads)
+        enc = [None] * s.num_experts
+        for j, e in enumerate(mine):
+            enc[e] = flat[j * 2:(j + 1) * 2]
+        L = ep.build_gpu_layer(s, enc, wr, None, None, None, max_tokens=T, cache_slots=cache, device=local)
+        eng = L.engine
+    x = syn.activations(T, s.hidden, seed=1 + rank).cuda()
+    out = torch.empty_like(x)
+    stream = torch.cuda.current_stream()
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        L(x, out) if world == 1 else L(x)
+    eng.sync()
+    eng.reset_stats()
+    eng.set_timing(True)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local if rank == 0 else None) as clk:
+        barrier()
+        a.record(stream)
+        for i in range(args.steps):
+            clk.probe(i, args.steps)
+            L(x, out) if world == 1 else L(x)
+        b.record(stream)
+        torch.cuda.synchronize()
+    eng.sync()
+    ms = a.elapsed_time(b) / args.steps
+    st = eng.stats()
+    eng.set_timing(False)
+    xh = x.cpu().pin_memory()
+    oh = torch.empty_like(xh).pin_memory()
+    xd = torch.empty_like(x)
+
+    def host_step():
+        xd.copy_(xh, non_blocking=True)
+        oh.copy_(L(xd), non_blocking=True)
+
+    for _ in range(2):
+        host_step()
+    a2, b2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local if rank == 0 else None) as clk2:
+        barrier()
+        a2.record(stream)
+        for i in range(args.steps):
+            clk2.probe(i, args.steps)
+            host_step()
+        b2.record(stream)
+        torch.cuda.synchronize()
+    e2e_ms = a2.elapsed_time(b2) / args.steps
+    t = torch.tensor([ms, e2e_ms], dtype=torch.float64, device="cuda")
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, e2e_ms = float(t[0]), float(t[1])
+    if rank == 0:
+        hbm, _, src = peaks()
+        dec_s = st["decode_ns"] * 1e-9
+        launches = max(st["decode_timed_launches"], 1)
+        achieved = (st["decode_timed_bytes"] / launches) / (dec_s / launches) / 1e9 if dec_s > 0 else 0.0
+        line = {"metric": "MoE-layer tokens/s", "value": world * T / (ms / 1e3), "unit": "tokens/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations, uniform router)",
+                "config": {"workload": "switch-large-128-layer", "tokens_total": 4096, "tokens_per_gpu": T,
+                           "hidden": s.hidden, "experts": s.num_experts, "inter": s.inter, "topk": 1,
+                           "capacity_per_rank": s.capacity, "cached_experts_per_gpu": cache,
+                           "codec": f"{args.codec}-{args.level}", "num_file_chunks": args.chunks,
+                           "parallelism": f"ep{world}" if world > 1 else "single"},
+                "e2e": {"value": world * T / (e2e_ms / 1e3), "unit": "tokens/s",
+                        "h2d_bytes_per_step": x.numel() * 2, "d2h_bytes_per_step": x.numel() * 2},
+                "roofline": {"bound": "hbm", "kernel": "map_kernel+resolve_kernel (fused LZ4 decode)",
+                             "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                             "peak_source": src, "traffic": None},
+                "decode": {"experts_per_step_rank0": st["decoded_experts"] / args.steps},
+                "cache": {"hits": st["hits"], "misses": st["misses"]},
+                "gpu_launches": st["launches"], "clocks": clk.summary()}
+        print(json.dumps(line), flush=True)
+    torch.cuda.synchronize()
+    if world > 1 and hasattr(L, "close"):
+        L.close()
+    eng.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def codec_bits(t):
+    return t.contiguous().view(torch.int16).cpu()
+
+
+def cpu_decode_baseline(args):
+    """liblz4 decode (LZ4_decompress_safe_partial, one chunk per task) plus the
+    numpy recombine on every host thread, over 32 Qwen chunks of normal(0.02)."""
+    from concurrent.futures import ThreadPoolExecutor
+    from oracle import codec as oc
+    threads = os.cpu_count() or 1
+    mats = [weight_family("normal", 0.02, (1408, 2048), 7000 + i) for i in range(11)]
+    enc = oc.encode_tensors(mats, args.chunks, args.codec, args.level, threads)
+    chunks = [(b, o) for e in enc for b, o in zip(e.blocks, e.original_sizes)][:32]
+    sms = [np.frombuffer(e.sm, np.uint8) for e in enc]
+    t0 = time.perf_counter()
+    with ThreadPoolExecutor(max_workers=threads) as ex:
+        outs = list(ex.map(lambda c: oc.lz4_decompress(c[0], c[1]), chunks))
+        rec = list(ex.map(lambda i: oc.recombine(outs[i], sms[i // 3][(i % 3) * outs[0].size:][:outs[i].size]),
+                          range(len(outs))))
+    dt = time.perf_counter() - t0
+    alg = sum(len(b) + 3 * o for b, o in chunks)
+    del rec
+    return {"value": alg / dt / 1e9, "unit": "GB/s", "cores": threads, "cpu_model": cpu_model(), "kind": "port",
+            "sample": f"{len(chunks)} LZ4 chunks of 961,195 B decoded and recombined on {threads} threads"}
+
+
 def cpu_baseline(args, s, enc, extra):
     from zmoe import synthetic as syn
     threads = os.cpu_count() or 1
@@ -581,6 +898,10 @@ def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+    elif args.config == "decode-sweep":
+        run_decode_sweep(args)
+    elif args.config == "switch":
+        run_switch(args)
     else:
         run_ours(args)
 

@@ -293,6 +293,8 @@ typedef struct zmoe_layer_config {
   int transient_slots;        /* decode slots for misses; 0 = num_experts - cache_slots */
   int cache_policy;           /* ZMOE_CACHE_* victim selection */
   double state_margin;        /* hyperparam_state_margin of the NORMAL threshold */
+  int sm_slots;               /* host store: experts whose sign+mantissa planes stay in HBM (the SMCACHE
+                                 pool of ZipMoECacheHandle, csrc/memory/cache.cpp:122-123, 369-401) */
 } zmoe_layer_config;
 
 typedef struct zmoe_layer_stats {
@@ -302,6 +304,7 @@ typedef struct zmoe_layer_stats {
   /* filled when timing is on: CUDA-event durations on the launch stream */
   uint64_t decode_ns, decode_timed_bytes, decode_timed_launches, ffn_ns, ffn_timed_launches;
   uint64_t host_copy_bytes;   /* host tier: compressed bytes copied to the GPU for decodes */
+  uint64_t sm_resident_tensors; /* host tier: tensors decoded with their sign+mantissa plane resident in HBM */
 } zmoe_layer_stats;
 
 zmoe_status zmoe_layer_create(const zmoe_layer_config* cfg, zmoe_layer** out);
@@ -324,7 +327,12 @@ zmoe_status zmoe_layer_load_expert(zmoe_layer* layer, int expert, int tensor, co
  * on the stream).  The host tier is for models whose compressed experts do not
  * fit the GPU; a miss then costs a PCIe copy of the compressed tensor.  It
  * replaces the reference's per-miss reads of the stored planes
- * (tensor_engine.cpp:380-417, pread into pinned docks). */
+ * (tensor_engine.cpp:380-417, pread into pinned docks).  With sm_slots > 0 the
+ * host tier keeps a pool of sign+mantissa planes in HBM (the reference's
+ * SMCACHE state): a miss ranked, by the layer's token counts, below
+ * cache_slots + sm_slots + margin * E but not admitted to a decoded slot gets
+ * (or keeps) its planes in the pool, and its later misses copy only the
+ * exponent blocks and index (about a third of the bytes). */
 enum { ZMOE_STORE_DEVICE = 0, ZMOE_STORE_HOST = 1 };
 zmoe_status zmoe_layer_set_store(zmoe_layer* layer, int where);
 /* Decode the given experts into free cache slots now. */

@@ -167,6 +167,36 @@ def test_engine_host_store_matches_device_store():
         check(lib.zmoe_layer_set_store(Lh._h, 0), "zmoe_layer_set_store")   # experts already loaded
 
 
+def test_host_store_sm_tier_bit_identical_and_copies_a_third():
+    # SMCACHE: misses outside the decoded cache keep their sign+mantissa planes
+    # in HBM, so later misses copy only exponent blocks and indexes
+    from zmoe.layer import MoELayer
+    s = QWEN_SMALL
+    L, w, wr, sg, sh = _build(s, 2, transient=2)
+    layers = {}
+    for sm in (0, 8):
+        Lh = MoELayer(s, max_tokens=64, cache_slots=2, transient_slots=2, store="host", sm_slots=sm)
+        Lh.set_router(wr, None, sg)
+        Lh.set_shared(*sh)
+        Lh.load_experts(w, num_file_chunks=3)
+        layers[sm] = Lh
+    per_miss = {}
+    for i in range(5):
+        x = syn.activations(24, s.hidden, seed=80 + i).cuda()
+        want = L(x)
+        for sm, Lh in layers.items():
+            if i == 1:
+                Lh.reset_stats()                        # planes admitted on the first forward; count from here
+            assert torch.equal(want, Lh(x)), (i, sm)
+    for sm, Lh in layers.items():
+        Lh.sync()
+        st = Lh.stats()
+        assert st["decode_errors"] == 0 and st["misses"] > 0
+        per_miss[sm] = st["host_copy_bytes"] / st["misses"]
+    assert layers[8].stats()["sm_resident_tensors"] > 0 and layers[0].stats()["sm_resident_tensors"] == 0
+    assert per_miss[8] < 0.45 * per_miss[0], per_miss
+
+
 def test_engine_submit_host_pipeline_matches_device():
     # five steps with different inputs through the two staging slots; each
     # step's output lands in its own pinned buffer

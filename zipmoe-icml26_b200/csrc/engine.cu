@@ -127,6 +127,14 @@ struct Layer {
   bool prefetch_pending = false;
   uint32_t* map_scratch = nullptr; // decoder source-map scratch (zmoe_decode_scratch_bytes per chunk)
   bool host_store = false;         // compressed experts in pinned host memory, copied in per miss
+  // host tier: pool of sign+mantissa planes kept in HBM (SMCACHE experts)
+  int n_sm = 0;
+  uint8_t* sm_pool = nullptr;      // n_sm * tensors * numel bytes
+  std::vector<int> sm_owner, expert_sm;
+  std::vector<uint64_t> sm_stamp;
+  std::vector<char> sm_fill;       // this forward: planes to copy into the pool before decoding
+  uint8_t* sm_plane(int e, int t) const { return sm_pool + ((size_t)expert_sm[e] * tensors + t) * numel; }
+  int choose_sm_victim(const std::vector<char>& active);
   uint8_t* stage_buf = nullptr;    // host tier: device copies of the compressed tensors being decoded
   uint64_t stage_cap = 0;
   uint64_t map_cap = 0;            // bytes of map_scratch
@@ -182,6 +190,7 @@ Layer::~Layer() {
   for (auto& e : store)
     for (auto& t : e) { cudaFree(t.dev); cudaFreeHost(t.host); }
   cudaFree(stage_buf);
+  cudaFree(sm_pool);
   cudaFree(slots);
   cudaFree(w_router); cudaFree(bias); cudaFree(w_sgate);
   for (auto* p : w_shared) cudaFree(p);
@@ -250,6 +259,7 @@ zmoe_status Layer::init(const zmoe_layer_config& c) {
   ZMOE_CHECK_ARG(c.cache_slots >= 0 && c.cache_slots <= c.num_experts, "layer: cache_slots outside [0, E]");
   ZMOE_CHECK_ARG(c.shared_inter == 0 || c.shared_inter % 8 == 0, "layer: shared_inter must be a multiple of 8");
   ZMOE_CHECK_ARG(c.route_mode != ZMOE_ROUTE_SWITCH || c.kind == 1, "layer: Switch routing needs ReLU experts");
+  ZMOE_CHECK_ARG(c.sm_slots >= 0 && c.sm_slots <= c.num_experts, "layer: sm_slots outside [0, E]");
   tensors = c.kind == 0 ? 3 : 2;
   numel = (uint64_t)c.hidden * c.inter;
   const int E = c.num_experts;
@@ -264,6 +274,8 @@ zmoe_status Layer::init(const zmoe_layer_config& c) {
   slot_stamp.assign(n_slots, 0);
   slot_admit.assign(n_slots, 0);
   global_count.assign(E, 0);
+  expert_sm.assign(E, -1);
+  sm_fill.assign(E, 0);
   zmoe_status st = ZMOE_OK;
   slots = dmalloc<uint16_t>((size_t)n_slots * tensors * numel, &st);
   const int T = c.max_tokens, k = c.topk, H = c.hidden;
@@ -321,6 +333,20 @@ zmoe_status Layer::init(const zmoe_layer_config& c) {
   ZMOE_CUDA_RET(cudaEventCreateWithFlags(&offsets_ready, cudaEventDisableTiming));
   ZMOE_CUDA_RET(cudaEventCreateWithFlags(&counts_ready, cudaEventDisableTiming));
   return ZMOE_OK;
+}
+
+// A pool slot for a sign+mantissa plane: a free one, else the least recently
+// used plane of an expert this forward does not use.
+int Layer::choose_sm_victim(const std::vector<char>& active) {
+  int victim = -1;
+  uint64_t best = UINT64_MAX;
+  for (int s = 0; s < n_sm; ++s) {
+    const int e = sm_owner[s];
+    if (e < 0) return s;
+    if (active[e] || sm_fill[e]) continue;
+    if (sm_stamp[s] < best) { best = sm_stamp[s]; victim = s; }
+  }
+  return victim;
 }
 
 int Layer::choose_victim(const std::vector<char>& active) {
@@ -431,7 +457,7 @@ zmoe_status Layer::decode_into(const std::vector<std::pair<int, int>>& jobs, cud
   if (host_store) {
     uint64_t need = 0;
     for (auto [e, slot] : jobs)
-      for (int t = 0; t < tensors; ++t) need += store[e][t].bytes;
+      for (int t = 0; t < tensors; ++t) need += store[e][t].bytes;    // an upper bound with resident planes
     if (need > stage_cap) {
       ZMOE_CUDA_RET(cudaStreamSynchronize(s));
       cudaFree(stage_buf);
@@ -447,11 +473,31 @@ zmoe_status Layer::decode_into(const std::vector<std::pair<int, int>>& jobs, cud
     for (int t = 0; t < tensors; ++t) {
       const TensorStore& ts = store[e][t];
       const uint8_t* buf = ts.dev;
+      const uint8_t* smbase = nullptr;                 // the plane, when not in buf at sm_off
+      uint64_t idx_shift = 0;                          // the indexes sit this much lower in the staged copy
       if (host_store) {
         uint8_t* at = stage_buf + stage_off;           // offsets stay 16-byte aligned (bytes is)
-        ZMOE_CUDA_RET(cudaMemcpyAsync(at, ts.host, ts.bytes, cudaMemcpyHostToDevice, s));
-        stats.host_copy_bytes += ts.bytes;
-        stage_off += ts.bytes;
+        const bool resident = n_sm > 0 && expert_sm[e] >= 0;
+        if (resident) {
+          // blocks, then indexes; the plane comes from the pool (copied in first when new)
+          if (sm_fill[e]) {
+            ZMOE_CUDA_RET(cudaMemcpyAsync(sm_plane(e, t), ts.host + ts.sm_off, ts.numel, cudaMemcpyHostToDevice,
+                                          s));
+            stats.host_copy_bytes += ts.numel;
+          }
+          const uint64_t idx0 = ts.idx_off.empty() ? ts.bytes : ts.idx_off[0];
+          ZMOE_CUDA_RET(cudaMemcpyAsync(at, ts.host, ts.sm_off, cudaMemcpyHostToDevice, s));
+          ZMOE_CUDA_RET(cudaMemcpyAsync(at + ts.sm_off, ts.host + idx0, ts.bytes - idx0, cudaMemcpyHostToDevice, s));
+          stats.host_copy_bytes += ts.sm_off + (ts.bytes - idx0);
+          stats.sm_resident_tensors++;
+          stage_off += ts.sm_off + (ts.bytes - idx0);
+          smbase = sm_plane(e, t);
+          idx_shift = idx0 - ts.sm_off;
+        } else {
+          ZMOE_CUDA_RET(cudaMemcpyAsync(at, ts.host, ts.bytes, cudaMemcpyHostToDevice, s));
+          stats.host_copy_bytes += ts.bytes;
+          stage_off += ts.bytes;
+        }
         buf = at;
       }
       uint64_t e0 = 0;
@@ -459,11 +505,11 @@ zmoe_status Layer::decode_into(const std::vector<std::pair<int, int>>& jobs, cud
       for (size_t c = 0; c < ts.block_off.size(); ++c) {
         zmoe_chunk& d = desc_host[nd++];
         d.src = buf + ts.block_off[c];
-        d.sm = buf + ts.sm_off + e0;
+        d.sm = (smbase ? smbase : buf + ts.sm_off) + e0;
         d.dst = dst + e0;
         d.src_size = ts.block_size[c];
         d.out_size = ts.orig_size[c];
-        d.index = reinterpret_cast<const uint32_t*>(buf + ts.idx_off[c]);
+        d.index = reinterpret_cast<const uint32_t*>(buf + ts.idx_off[c] - idx_shift);
         d.n_index = ts.idx_n[c];
         d.seg_bytes = kSegBytes;
         d.map = nullptr;                     // assigned below, one scratch area per chunk
@@ -590,6 +636,8 @@ zmoe_status Layer::run_experts(const uint16_t* xrows, const int32_t* offsets_dev
   // rank of each miss by global count (count_up of cache.cpp:230-238)
   std::vector<std::pair<int, int>> to_cache, to_transient;
   const double thr_normal = n_cache + cfg.state_margin * E;
+  const double thr_sm = n_cache + n_sm + cfg.state_margin * E;   // Threshold_SMCACHE (cache.cpp:122-123)
+  std::fill(sm_fill.begin(), sm_fill.end(), 0);
   for (int e : misses) {
     int up = 0;
     for (int q = 0; q < E; ++q) up += global_count[q] > global_count[e];
@@ -608,6 +656,19 @@ zmoe_status Layer::run_experts(const uint16_t* xrows, const int32_t* offsets_dev
       }
     }
     to_transient.push_back({e, -1});
+    // SMCACHE: not decoded-cached, but ranked high enough to keep its planes in HBM
+    if (n_sm > 0 && up < thr_sm) {
+      if (expert_sm[e] < 0) {
+        const int ps = choose_sm_victim(active);
+        if (ps >= 0) {
+          if (sm_owner[ps] >= 0) expert_sm[sm_owner[ps]] = -1;
+          sm_owner[ps] = e;
+          expert_sm[e] = ps;
+          sm_fill[e] = 1;
+        }
+      }
+      if (expert_sm[e] >= 0) sm_stamp[expert_sm[e]] = clock;
+    }
   }
 
   // 4. Misses decode on the decode stream, in waves of the transient slots;
@@ -916,6 +977,12 @@ zmoe_status zmoe_layer_set_store(zmoe_layer* layer, int where) {
   for (auto& e : L->store)
     for (auto& t : e) ZMOE_CHECK_ARG(!t.loaded(), "set_store: experts are already loaded");
   L->host_store = where == ZMOE_STORE_HOST;
+  if (L->host_store && L->cfg.sm_slots > 0 && !L->sm_pool) {
+    L->n_sm = L->cfg.sm_slots;
+    ZMOE_CUDA_RET(cudaMalloc(&L->sm_pool, (size_t)L->n_sm * L->tensors * L->numel));
+    L->sm_owner.assign(L->n_sm, -1);
+    L->sm_stamp.assign(L->n_sm, 0);
+  }
   return ZMOE_OK;
 }
 

@@ -860,6 +860,12 @@ class Dispatcher {
     const double pool = (double)prop.totalGlobalMem * c.device_memory_ratio * c.gpu_pool_ratio;
     int cache = (int)(pool / expert_bytes / c.num_expert_layers);
     cache = std::max(0, std::min(cache, E_));
+    // the rest of the budget holds sign+mantissa planes (1 byte per element),
+    // the reference's SM pool (runtime/cache_planning.py:71-88); the engine
+    // uses it when its experts are stored in host memory
+    const double sm_pool = (double)prop.totalGlobalMem * c.device_memory_ratio * (1.0 - c.gpu_pool_ratio);
+    int sm = (int)(sm_pool / (expert_bytes / 2.0) / c.num_expert_layers);
+    sm = std::max(0, std::min(sm, E_ - cache));
     zmoe_layer_config cfg{};
     cfg.hidden = eng->H;
     cfg.num_experts = E_;
@@ -873,6 +879,7 @@ class Dispatcher {
     cfg.transient_slots = std::max(1, std::min(E_ - cache, 32));
     cfg.cache_policy = cache_policy_of(c.caching_algorithm);
     cfg.state_margin = c.state_margin;
+    cfg.sm_slots = sm;
     check(zmoe_layer_create(&cfg, &eng->L), "zmoe_layer_create");
     for (int e = 0; e < E_; ++e)
       for (size_t t = 0; t < metas[e].size(); ++t) {

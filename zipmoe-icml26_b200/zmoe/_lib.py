@@ -57,7 +57,7 @@ class LayerConfig(ctypes.Structure):
                 ("kind", c_int), ("route_mode", c_int), ("norm_topk_prob", c_int), ("scaling", c_float),
                 ("shared_inter", c_int), ("capacity", c_int), ("seq_len", c_int), ("max_tokens", c_int),
                 ("cache_slots", c_int), ("transient_slots", c_int), ("cache_policy", c_int),
-                ("state_margin", ctypes.c_double)]
+                ("state_margin", ctypes.c_double), ("sm_slots", c_int)]
 
 
 class LayerStats(ctypes.Structure):
@@ -65,7 +65,7 @@ class LayerStats(ctypes.Structure):
         "forwards", "tokens", "hits", "misses", "evictions", "decoded_experts", "decoded_chunks",
         "decoded_bytes", "decode_launches", "launches", "decode_errors", "store_bytes",
         "decode_ns", "decode_timed_bytes", "decode_timed_launches", "ffn_ns", "ffn_timed_launches",
-        "host_copy_bytes")]
+        "host_copy_bytes", "sm_resident_tensors")]
 
 
 class EPConfig(ctypes.Structure):

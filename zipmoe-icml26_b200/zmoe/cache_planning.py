@@ -267,6 +267,19 @@ def decoded_slots(gpu_pool_ratio: float, total_memory: int, device_memory_ratio:
     return max(0, min(num_experts, int(gpu_pool_ratio * budget / (2 * tensors_per_expert * num_elements_per_tensor))))
 
 
+def sm_slots(gpu_pool_ratio: float, total_memory: int, device_memory_ratio: float, num_sparse_layers: int,
+             tensors_per_expert: int, num_elements_per_tensor: int, num_experts: int) -> int:
+    """Experts per layer whose sign+mantissa planes (1 byte per element) the
+    rest of the budget holds: the reference's SM pool,
+    int((1 - ratio_full) * total_mem / sm_slot_size) (runtime/cache_planning.py:71-88).
+    MoELayer(store="host", sm_slots=...) keeps that many planes in HBM."""
+    budget = device_memory_ratio * total_memory / num_sparse_layers
+    full = decoded_slots(gpu_pool_ratio, total_memory, device_memory_ratio, num_sparse_layers, tensors_per_expert,
+                         num_elements_per_tensor, num_experts)
+    n = int((1.0 - gpu_pool_ratio) * budget / (tensors_per_expert * num_elements_per_tensor))
+    return max(0, min(num_experts - full, n))
+
+
 # the reference's names
 CalculateProb = calculate_prob
 DelaySimu = delay_simu

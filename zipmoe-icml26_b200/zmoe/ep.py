@@ -221,7 +221,7 @@ class NativeEPLayer:
         self.device = torch.device("cuda", device)
         comm = nccl_comm_ptr(device, group) if self.P > 1 else None
         lc = LayerConfig(shape.hidden, shape.num_experts, shape.inter, shape.topk, shape.kind, route_mode(shape), 0,
-                         shape.scaling, shape.shared_inter, shape.capacity, shape.seq_len, max_tokens, 0, 0, 0, 0.0)
+                         shape.scaling, shape.shared_inter, shape.capacity, shape.seq_len, max_tokens, 0, 0, 0, 0.0, 0)
         cfg = EPConfig(lc, self.rank, self.P, comm)
         h = ctypes.c_void_p()
         check(lib.zmoe_ep_create(ctypes.byref(cfg), local._h, ctypes.byref(h)), "zmoe_ep_create")

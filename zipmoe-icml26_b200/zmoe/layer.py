@@ -28,19 +28,21 @@ def route_mode(s: LayerShape) -> int:
 
 class MoELayer:
     def __init__(self, shape: LayerShape, max_tokens: int, cache_slots: int, transient_slots: int = 0,
-                 policy: str = "ZipMoE", state_margin: float = 0.1, device: int = 0, store: str = "device"):
+                 policy: str = "ZipMoE", state_margin: float = 0.1, device: int = 0, store: str = "device",
+                 sm_slots: int = 0):
         self.shape = shape
         self.device = torch.device("cuda", device)
         torch.cuda.set_device(self.device)
         cfg = LayerConfig(shape.hidden, shape.num_experts, shape.inter, shape.topk, shape.kind, route_mode(shape),
                           0, shape.scaling, shape.shared_inter, shape.capacity, shape.seq_len, max_tokens,
-                          cache_slots, transient_slots, POLICIES[policy], state_margin)
+                          cache_slots, transient_slots, POLICIES[policy], state_margin, sm_slots)
         h = ctypes.c_void_p()
         check(lib.zmoe_layer_create(ctypes.byref(cfg), ctypes.byref(h)), "zmoe_layer_create")
         self._h = h
         if store not in STORES:
             raise ValueError(f"store must be one of {sorted(STORES)}")
-        # "host": compressed experts in pinned host memory, copied in per miss
+        # "host": compressed experts in pinned host memory, copied in per miss;
+        # sm_slots: how many experts' sign+mantissa planes the host tier keeps in HBM
         check(lib.zmoe_layer_set_store(h, STORES[store]), "zmoe_layer_set_store")
         self.max_tokens = max_tokens
 
