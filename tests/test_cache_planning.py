@@ -75,11 +75,11 @@ def test_decoded_slots_follow_the_pool():
 
 def test_sm_slots_split_the_budget_with_decoded_slots():
     from zmoe import cache_planning as cp
-    kw = dict(total_memory=180 * 2 ** 30, device_memory_ratio=0.5, num_sparse_layers=24, tensors_per_expert=3,
+    kw = dict(total_memory=180 * 2 ** 30, device_memory_ratio=0.5, num_sparse_layers=240, tensors_per_expert=3,
               num_elements_per_tensor=2048 * 1408, num_experts=60)
     full = cp.decoded_slots(0.5, **kw)
     sm = cp.sm_slots(0.5, **kw)
-    budget = 0.5 * 180 * 2 ** 30 / 24
+    budget = 0.5 * 180 * 2 ** 30 / 240
     assert full == int(0.5 * budget / (2 * 3 * 2048 * 1408))
     assert sm == min(60 - full, int(0.5 * budget / (3 * 2048 * 1408)))
     assert cp.sm_slots(1.0, **kw) == 0
