@@ -57,10 +57,13 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--store", default="device", choices=["device", "host"],
                     help="where the compressed experts live (host: pinned memory, copied in per miss)")
-    ap.add_argument("--config", default="qwen", choices=["qwen", "decode-sweep", "switch"],
+    ap.add_argument("--sm-slots", type=int, default=0,
+                    help="host store: experts whose sign+mantissa planes stay in HBM (the SMCACHE pool)")
+    ap.add_argument("--config", default="qwen", choices=["qwen", "decode-sweep", "switch", "deepseek-stack"],
                     help="qwen: the Qwen1.5-MoE layer (default; the headline line, with a token-count sweep); "
                          "decode-sweep: decode+recombine GB/s over sizes and weight distributions; "
-                         "switch: the Switch-large-128 layer at 4096 tokens")
+                         "switch: the Switch-large-128 layer at 4096 tokens; deepseek-stack: 26 "
+                         "DeepSeek-V2-Lite MoE layers at decode batch sizes, with and without next-layer prefetch")
     ap.add_argument("--timeline", default=None,
                     help="write the GPU timeline of 3 more steps (kernels and copies per stream, "
                          "torch.profiler over CUPTI) to this text file")
@@ -194,7 +197,7 @@ def build_workload(args, device_index=0, threads=0):
     sh = syn.shared_weights(s)
     bias = syn.zipf_bias(s, 0)
     L = MoELayer(s, max_tokens=args.tokens, cache_slots=args.cache, device=device_index,
-                 store=getattr(args, "store", "device"))
+                 store=getattr(args, "store", "device"), sm_slots=getattr(args, "sm_slots", 0))
     L.set_router(wr, bias, sg)
     L.set_shared(*sh)
     enc = L.load_experts(w, num_file_chunks=args.chunks, codec=args.codec, level=args.level, threads=threads)
@@ -235,6 +238,7 @@ def bench_config(args, s, world):
             "cached_experts": args.cache, "codec": f"{args.codec}-{args.level}",
             "num_file_chunks": args.chunks, "zipf_s": s.zipf_s,
             "parallelism": f"ep{world}" if world > 1 else "single", "store": args.store,
+            "sm_slots": args.sm_slots,
             "l2": "inputs larger than L2 (decoded + compressed experts > 1 GB)"}
 
 
@@ -693,7 +697,7 @@ def run_decode_sweep(args):
             ms = a.elapsed_time(b) / reps
             ok = all(bool((t[3] == 0).all()) for t in tables)
             if mb == sizes_mb[-1] or small:             # bit-exact check of the first matrix
-                want = codec_bits(pool[0][:rows] if small else pool[0])
+                want = codec_bits(pool[0][:rows] if small else pool[0]).reshape(-1)
                 ok = ok and torch.equal(dst[:want.numel()].view(torch.int16).cpu(), want)
             t = torch.tensor([ms], dtype=torch.float64, device="cuda")
             if dist is not None:
@@ -848,6 +852,100 @@ def run_switch(args):
         dist.destroy_process_group()
 
 
+def run_deepseek_stack(args):
+    """26 DeepSeek-V2-Lite-shaped MoE layers (64 SwiGLU experts of 1408, top-6
+    softmax, routed_scaling 1.0, 2 shared experts of combined 2816, Zipf(1.2)
+    popularity with a per-layer seeded permutation), one GPU, decode batches
+    of 1 and 64 tokens, 16 decoded experts cached per layer.  The stack's
+    input is the layer-to-layer chain: layer l + 1 takes layer l's output.
+    Each batch size runs twice: without prefetch, and with the next-layer
+    predictor (ExpertPredictor: 0.8 * count + 0.2 * last-5 visits, top-6)
+    asking layer l + 1 to decode its predicted experts into its cache before
+    layer l runs, so those decodes overlap layer l.  Expert weights: a seeded
+    pool of 64 experts, each layer taking them in its own seeded order (every
+    layer holds and decodes its own copy of the compressed bytes)."""
+    from zmoe import codec as zc
+    from zmoe import synthetic as syn
+    from zmoe.layer import MoELayer
+    from zmoe.predictor import ExpertPredictor
+    world, rank, local = dist_env()
+    if rank != 0:
+        return
+    torch.cuda.set_device(local)
+    s = syn.DEEPSEEK
+    n_layers, cache, Tmax = 26, 16, 64
+    threads = os.cpu_count() or 1
+    pool = syn.expert_weights(s, 1)[0]
+    enc = zc.encode_tensors([t for e in pool for t in e], args.chunks, args.codec, args.level, threads)
+    enc = [enc[3 * e:3 * e + 3] for e in range(s.num_experts)]
+    layers = []
+    for li in range(n_layers):
+        perm = torch.randperm(s.num_experts, generator=torch.Generator().manual_seed(100 + li)).tolist()
+        wr, _ = syn.router_weights(s, seed=2 + 1000 * li)
+        sh = syn.shared_weights(s, seed=4 + 1000 * li)
+        L = MoELayer(s, max_tokens=Tmax, cache_slots=cache, device=local)
+        L.set_router(wr, syn.zipf_bias(s, li), None)
+        L.set_shared(*sh)
+        for e in range(s.num_experts):
+            for t, et in enumerate(enc[perm[e]]):
+                L.load_encoded(e, t, et)
+        L.warm_cache(syn.popularity_order(s, li)[:cache])
+        layers.append(L)
+    stream = torch.cuda.current_stream()
+    results = {}
+    for T in (1, 64):
+        for prefetch in (False, True):
+            pred = ExpertPredictor(n_layers, s.topk)
+            x0 = syn.activations(T, s.hidden, seed=1).cuda()
+            outs = [torch.empty_like(x0) for _ in range(n_layers)]
+
+            def stack():
+                x = x0
+                for li, L in enumerate(layers):
+                    if prefetch and li + 1 < n_layers:
+                        _, want = pred.predict_next_layer(li)
+                        if want:
+                            layers[li + 1].prefetch(want[:cache])
+                    L.forward(x, outs[li])
+                    pred.update(li, [e for e, c in enumerate(L.last_counts()) if c > 0])
+                    x = outs[li]
+                return x
+
+            for _ in range(max(args.warmup, 3)):
+                stack()
+            torch.cuda.synchronize()
+            before = [L.stats() for L in layers]
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            for _ in range(args.steps):
+                stack()
+            b.record(stream)
+            torch.cuda.synchronize()
+            for L in layers:
+                L.sync()
+            ms = a.elapsed_time(b) / args.steps
+            after = [L.stats() for L in layers]
+            hits = sum(y["hits"] - x["hits"] for x, y in zip(before, after))
+            misses = sum(y["misses"] - x["misses"] for x, y in zip(before, after))
+            dec = sum(y["decoded_experts"] - x["decoded_experts"] for x, y in zip(before, after))
+            results[f"T{T}_{'prefetch' if prefetch else 'no_prefetch'}"] = {
+                "tokens_per_s": T / (ms * 1e-3), "ms_per_stack": ms, "hit_rate": hits / max(hits + misses, 1),
+                "experts_decoded_per_stack": dec / args.steps}
+    head = results["T64_prefetch"]
+    line = {"metric": "MoE-stack tokens/s (26 layers)", "value": head["tokens_per_s"], "unit": "tokens/s",
+            "n_gpus": 1, "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": head["ms_per_stack"],
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,0.02) expert pool, per-layer routers, N(0,1) input)",
+            "config": {"workload": "deepseek-v2-lite-moe-stack", "layers": n_layers, "experts": s.num_experts,
+                       "inter": s.inter, "topk": s.topk, "shared_inter": s.shared_inter, "zipf_s": s.zipf_s,
+                       "cached_experts_per_layer": cache, "codec": f"{args.codec}-{args.level}",
+                       "num_file_chunks": args.chunks, "parallelism": "single"},
+            "results": results}
+    print(json.dumps(line), flush=True)
+    for L in layers:
+        L.close()
+
+
 def codec_bits(t):
     return t.contiguous().view(torch.int16).cpu()
 
@@ -902,6 +1000,8 @@ def main():
         run_decode_sweep(args)
     elif args.config == "switch":
         run_switch(args)
+    elif args.config == "deepseek-stack":
+        run_deepseek_stack(args)
     else:
         run_ours(args)
 

@@ -382,6 +382,11 @@ zmoe_status zmoe_layer_cached_experts(const zmoe_layer* layer, int32_t* experts,
  * ExpertDispatcher::SubmitPrefetch / EnqueuePrefetch
  * (csrc/dispatcher/expert_dispatcher.cpp:220-277). */
 zmoe_status zmoe_layer_prefetch(zmoe_layer* layer, const int* experts, int n, zmoe_stream_t stream);
+/* Per-expert token counts of the layer's last forward or expert stage
+ * (counts[e], e < cap; n receives the number of experts).  The input of a
+ * next-layer predictor: the reference's ExpertExecutor records each layer's
+ * activated experts for ExpertPredictor (experts/expert_executor.py:68-83). */
+zmoe_status zmoe_layer_last_counts(const zmoe_layer* layer, int32_t* counts, int cap, int* n);
 /* Zero the per-expert token counts behind the cache decision (the admission
  * rank and the LFU/ZipMoE victim keys); replaces
  * ZipMoECacheHandle::reset_global_access_counts (csrc/memory/cache.cpp). */

@@ -316,6 +316,7 @@ zmoe_status Layer::init(const zmoe_layer_config& c) {
   if (st != ZMOE_OK) return st;
   ZMOE_CUDA_RET(cudaMemset(kerr_dev, 0, sizeof(int32_t)));
   *kerr_host = 0;
+  memset(counts_host, 0, sizeof(int32_t) * E);
   ZMOE_CUDA_RET(cudaEventCreateWithFlags(&kerr_ready, cudaEventDisableTiming));
   ZMOE_CUDA_RET(cudaStreamCreateWithFlags(&copy_in, cudaStreamNonBlocking));
   ZMOE_CUDA_RET(cudaStreamCreateWithFlags(&copy_out, cudaStreamNonBlocking));
@@ -1133,6 +1134,16 @@ zmoe_status zmoe_layer_get_stats(const zmoe_layer* layer, zmoe_layer_stats* out)
   const Layer* L = reinterpret_cast<const Layer*>(layer);
   ZMOE_CHECK_ARG(L && out, "get_stats: null pointer");
   *out = L->stats;
+  return ZMOE_OK;
+}
+
+zmoe_status zmoe_layer_last_counts(const zmoe_layer* layer, int32_t* counts, int cap, int* n) {
+  const Layer* L = reinterpret_cast<const Layer*>(layer);
+  ZMOE_CHECK_ARG(L && n, "last_counts: null pointer");
+  const int E = L->cfg.num_experts;
+  *n = E;
+  if (counts)
+    for (int e = 0; e < E && e < cap; ++e) counts[e] = L->counts_host[e];
   return ZMOE_OK;
 }
 

@@ -113,6 +113,7 @@ SIGNATURES = {
     "zmoe_layer_set_timing": (c_int, [c_void_p, c_int]),
     "zmoe_layer_reset_access_counts": (c_int, [c_void_p]),
     "zmoe_layer_prefetch": (c_int, [c_void_p, ctypes.POINTER(c_int), c_int, c_void_p]),
+    "zmoe_layer_last_counts": (c_int, [c_void_p, ctypes.POINTER(ctypes.c_int32), c_int, ctypes.POINTER(c_int)]),
     "zmoe_layer_cached_experts": (c_int, [c_void_p, ctypes.POINTER(ctypes.c_int32), c_int,
                                           ctypes.POINTER(c_int)]),
     "zmoe_ep_create": (c_int, [ctypes.POINTER(EPConfig), c_void_p, ctypes.POINTER(c_void_p)]),

@@ -179,6 +179,14 @@ class MoELayer:
     def set_timing(self, on: bool = True):
         check(lib.zmoe_layer_set_timing(self._h, int(on)), "zmoe_layer_set_timing")
 
+    def last_counts(self) -> List[int]:
+        """Tokens per expert in the last forward (zmoe_layer_last_counts)."""
+        n = ctypes.c_int()
+        buf = (ctypes.c_int32 * self.shape.num_experts)()
+        check(lib.zmoe_layer_last_counts(self._h, buf, self.shape.num_experts, ctypes.byref(n)),
+              "zmoe_layer_last_counts")
+        return [int(buf[i]) for i in range(n.value)]
+
     def cached_experts(self) -> List[int]:
         n = ctypes.c_int()
         buf = (ctypes.c_int32 * self.shape.num_experts)()
