@@ -857,7 +857,8 @@ def run_deepseek_stack(args):
     softmax, routed_scaling 1.0, 2 shared experts of combined 2816, Zipf(1.2)
     popularity with a per-layer seeded permutation), one GPU, decode batches
     of 1 and 64 tokens, 16 decoded experts cached per layer.  The stack's
-    input is the layer-to-layer chain: layer l + 1 takes layer l's output.
+    input is the layer-to-layer chain: layer l + 1 takes layer l's output,
+    and every step feeds new tokens, as decoding does.
     Each batch size runs twice: without prefetch, and with the next-layer
     predictor (ExpertPredictor: 0.8 * count + 0.2 * last-5 visits, top-6)
     asking layer l + 1 to decode its predicted experts into its cache before
@@ -896,11 +897,14 @@ def run_deepseek_stack(args):
     for T in (1, 64):
         for prefetch in (False, True):
             pred = ExpertPredictor(n_layers, s.topk)
-            x0 = syn.activations(T, s.hidden, seed=1).cuda()
-            outs = [torch.empty_like(x0) for _ in range(n_layers)]
+            n_in = max(args.warmup, 3) + args.steps
+            xs = syn.activations(n_in * T, s.hidden, seed=1).view(n_in, T, s.hidden).cuda()   # new tokens every step
+            outs = [torch.empty_like(xs[0]) for _ in range(n_layers)]
+            step_no = [0]
 
             def stack():
-                x = x0
+                x = xs[step_no[0] % n_in]
+                step_no[0] += 1
                 for li, L in enumerate(layers):
                     if prefetch and li + 1 < n_layers:
                         _, want = pred.predict_next_layer(li)
