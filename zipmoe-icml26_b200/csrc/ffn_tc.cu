@@ -39,7 +39,8 @@ __device__ int32_t g_kernel_error = 0;
 namespace tc {
 
 constexpr int BM = 128;               // weight rows per tile (MMA M)
-constexpr int BN = 128;               // tokens per tile (max MMA N)
+constexpr int BN = 128;               // tokens per tile of grouped launches (the narrow kernel's maximum)
+constexpr int BNW = 256;              // tokens per tile at most in the wide kernel (max MMA N)
 constexpr int BK = 64;                // bf16 per 128-byte swizzle row
 constexpr int kTileBytes = BM * BK * 2;   // 16 KiB (A tile; B tile has the same size)
 constexpr int kMaxMaps = 128;
@@ -60,6 +61,7 @@ struct __align__(64) Params {
   void* out;                          // h or y (BF16), row-major [rows_total, n_out]
   int g_begin, g_count;               // groups of this launch (offset into offsets)
   int rows_total, K, n_out;           // n_out = weight rows of one matrix (I or H)
+  int bn;                             // tokens per tile (multiple of 16, at most the kernel's BNT)
   int32_t* err;                       // caller's error word (device) or nullptr
   long long wait_limit;               // clock64 cycles a wait may take
   int drop_loads;                     // error-path test: the producer issues nothing
@@ -168,13 +170,19 @@ __device__ __forceinline__ float silu(float g) { return g / (1.0f + __expf(-g));
 // ---------------------------------------------------------------------------
 // kernel
 // ---------------------------------------------------------------------------
-template <int MODE>  // 0: SwiGLU up (gate+up maps), 1: ReLU up, 2: down (BF16 out)
+// MODE 0: SwiGLU up (gate+up maps), 1: ReLU up, 2: down (BF16 out).  BNT: the
+// largest token tile (the B region of a stage and the accumulator width); the
+// launch's tile p.bn is at most BNT.
+template <int MODE, int BNT>
 __global__ void __launch_bounds__(kThreads, 1) ffn_tc_kernel(const __grid_constant__ Params p) {
   constexpr int NA = MODE == 0 ? 2 : 1;
-  constexpr int STAGES = MODE == 0 ? 4 : 6;
-  constexpr int kStageBytes = (NA + 1) * kTileBytes;
-  constexpr uint32_t kAccCols = MODE == 0 ? 256 : 128;   // TMEM columns of one accumulator
-  constexpr uint32_t kTmemCols = 2 * kAccCols;            // two accumulators: MMA and epilogue overlap
+  constexpr int kBTileBytes = BNT * BK * 2;
+  constexpr int kStageBytes = NA * kTileBytes + kBTileBytes;
+  constexpr int STAGES = (192 * 1024) / kStageBytes;     // 4 / 6 stages at BNT 128, 3 / 4 at 256
+  constexpr uint32_t kAccCols = NA * BNT;                // TMEM columns of one accumulator
+  constexpr uint32_t NACC = 2 * kAccCols <= 512 ? 2 : 1; // two accumulators (MMA and epilogue overlap) when they fit
+  constexpr uint32_t kTmemCols = NACC * kAccCols;
+  static_assert(STAGES >= 3 && STAGES <= 8, "operand ring depth");
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -213,7 +221,7 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_tc_kernel(const __grid_consta
         r0 = p.offsets[p.g_begin + g];
         rn = p.offsets[p.g_begin + g + 1] - r0;
       }
-      const int nt = (p.present[g] && rn > 0) ? (rn + BN - 1) / BN : 0;
+      const int nt = (p.present[g] && rn > 0) ? (rn + p.bn - 1) / p.bn : 0;
       prefix[g] = acc;
       ntiles[g] = nt;
       row0[g] = r0;
@@ -258,12 +266,12 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_tc_kernel(const __grid_consta
         int g, mt, nt;
         unit_of(u, g, mt, nt);
         const int arow = mt * BM;
-        const int brow = row0[g] + nt * BN;
+        const int brow = row0[g] + nt * p.bn;
         const int m0 = MODE == 0 ? 2 * g : g;
         for (int ks = 0; ks < KS; ++ks) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, cta_err, p.err, p.wait_limit)) { ok = false; break; }
           uint8_t* st = smem + stage * kStageBytes;
-          mbar_expect_tx(&full[stage], kStageBytes);
+          mbar_expect_tx(&full[stage], NA * kTileBytes + p.bn * BK * 2);
           armed[stage] = phase + 1;
           tma_load_2d(st, &p.amap[m0], ks * BK, arow, &full[stage]);
           if (NA == 2) tma_load_2d(st + kTileBytes, &p.amap[m0 + 1], ks * BK, arow, &full[stage]);
@@ -290,11 +298,11 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_tc_kernel(const __grid_consta
       for (int u = blockIdx.x, i = 0; u < total && ok; u += gridDim.x, ++i) {
         int g, mt, nt;
         unit_of(u, g, mt, nt);
-        const int valid = min(BN, rows[g] - nt * BN);
+        const int valid = min(p.bn, rows[g] - nt * p.bn);
         const int n = max(16, (valid + 15) & ~15);
         const uint32_t idesc = instr_desc(n);
-        const int ab = i & 1;                           // accumulator of this unit
-        const uint32_t acc_phase = (uint32_t)(i >> 1) & 1u;
+        const int ab = (int)((uint32_t)i % NACC);       // accumulator of this unit
+        const uint32_t acc_phase = ((uint32_t)i / NACC) & 1u;
         const uint32_t tacc = tmem + (uint32_t)ab * kAccCols;
         if (!mbar_wait(&tmem_empty[ab], acc_phase ^ 1u, cta_err, p.err, p.wait_limit)) break;
         tc_fence_after();
@@ -309,7 +317,7 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_tc_kernel(const __grid_consta
           for (int kk = 0; kk < BK / 16; ++kk) {
             const uint32_t accf = (ks | kk) != 0;
             tc_mma(tacc, da0 + 2 * kk, db + 2 * kk, idesc, accf);
-            if (NA == 2) tc_mma(tacc + 128, da1 + 2 * kk, db + 2 * kk, idesc, accf);
+            if (NA == 2) tc_mma(tacc + BNT, da1 + 2 * kk, db + 2 * kk, idesc, accf);
           }
           tc_commit(&empty[stage]);
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
@@ -331,18 +339,18 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_tc_kernel(const __grid_consta
     for (int u = blockIdx.x, i = 0; u < total; u += gridDim.x, ++i) {
       int g, mt, nt;
       unit_of(u, g, mt, nt);
-      const int valid = min(BN, rows[g] - nt * BN);
+      const int valid = min(p.bn, rows[g] - nt * p.bn);
       const int n = max(16, (valid + 15) & ~15);
-      const int ab = i & 1;
-      if (!mbar_wait(&tmem_full[ab], (uint32_t)(i >> 1) & 1u, cta_err, p.err, p.wait_limit)) break;
+      const int ab = (int)((uint32_t)i % NACC);
+      if (!mbar_wait(&tmem_full[ab], ((uint32_t)i / NACC) & 1u, cta_err, p.err, p.wait_limit)) break;
       tc_fence_after();
       const int feat = mt * BM + q * 32 + lane;   // output feature of this thread
-      const size_t rbase = (size_t)(row0[g] + nt * BN);
+      const size_t rbase = (size_t)(row0[g] + nt * p.bn);
       const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)ab * kAccCols;
       for (int c0 = 0; c0 < n; c0 += 16) {
         uint32_t a[16], b[16];
         tmem_ld16(taddr + c0, a);
-        if (MODE == 0) tmem_ld16(taddr + 128 + c0, b);
+        if (MODE == 0) tmem_ld16(taddr + BNT + c0, b);
         tmem_wait_ld();
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
@@ -372,11 +380,34 @@ __global__ void __launch_bounds__(kThreads, 1) ffn_tc_kernel(const __grid_consta
   }
 }
 
-template <int MODE>
+template <int MODE, int BNT>
 constexpr int smem_bytes() {
   constexpr int NA = MODE == 0 ? 2 : 1;
-  constexpr int STAGES = MODE == 0 ? 4 : 6;
-  return 1024 + STAGES * (NA + 1) * kTileBytes + 2 * STAGES * 8 + 40 + 8 + 4 * (4 * kMaxGroups + 2);
+  constexpr int kStageBytes = NA * kTileBytes + BNT * BK * 2;
+  constexpr int STAGES = (192 * 1024) / kStageBytes;
+  return 1024 + STAGES * kStageBytes + 2 * STAGES * 8 + 40 + 8 + 4 * (4 * kMaxGroups + 2);
+}
+
+// Token tile of a launch with one dense group of R rows (the shared expert):
+// the units (MT weight tiles x token tiles) should fill the SMs in whole
+// waves.  A unit streams (NA * 128 + bn) * K * 2 bytes at about 100 GB/s per SM
+// and runs 2 * NA * 128 * bn * K FLOP at about 10.7 TFLOP/s per SM; the tile
+// with the least estimated waves x unit time wins.  Grouped launches keep BN.
+inline int dense_tile(int MT, int R, int K, int NA, int sms) {
+  int best = BN;
+  double best_t = 1e30;
+  for (int bn = 16; bn <= BNW; bn += 16) {
+    const long long units = (long long)MT * ((R + bn - 1) / bn);
+    const long long waves = (units + sms - 1) / sms;
+    const double load = (double)(NA * BM + bn) * K * 2 / 100e9;
+    const double mma = 2.0 * NA * BM * bn * (double)K / 10.7e12;
+    const double t = (double)waves * (load > mma ? load : mma);
+    if (t < best_t * 0.999) {
+      best_t = t;
+      best = bn;
+    }
+  }
+  return best;
 }
 
 // ---------------------------------------------------------------------------
@@ -431,11 +462,16 @@ zmoe_status launch_mode(const zmoe_ffn_args* a, const uint16_t* act, int K, int 
   static Params p;                            // 17 KB: too large for the stack frame of a host thread loop
   static std::mutex mu;
   std::lock_guard<std::mutex> lock(mu);
-  const int smem = smem_bytes<MODE>();
-  ZMOE_CUDA_RET(cudaFuncSetAttribute(ffn_tc_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   int dev = 0, sms = kNumSMs;
   ZMOE_CUDA_RET(cudaGetDevice(&dev));
   ZMOE_CUDA_RET(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  const int bn = a->offsets ? BN : dense_tile((n_out + BM - 1) / BM, a->rows_total, K, per, sms);
+  const bool wide = bn > BN;
+  const int smem = wide ? smem_bytes<MODE, BNW>() : smem_bytes<MODE, BN>();
+  if (wide)
+    ZMOE_CUDA_RET(cudaFuncSetAttribute(ffn_tc_kernel<MODE, BNW>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  else
+    ZMOE_CUDA_RET(cudaFuncSetAttribute(ffn_tc_kernel<MODE, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   for (int g0 = 0; g0 < a->G; g0 += gmax) {
     const int gc = a->G - g0 < gmax ? a->G - g0 : gmax;
     memset(&p, 0, sizeof(p));
@@ -452,7 +488,7 @@ zmoe_status launch_mode(const zmoe_ffn_args* a, const uint16_t* act, int K, int 
       any = 1;
     }
     if (!any) continue;
-    zmoe_status st = make_map(&p.bmap, act, (uint64_t)a->rows_total, (uint64_t)K, BN);
+    zmoe_status st = make_map(&p.bmap, act, (uint64_t)a->rows_total, (uint64_t)K, (uint32_t)bn);
     if (st != ZMOE_OK) return st;
     p.offsets = a->offsets;
     p.out = out;
@@ -461,10 +497,12 @@ zmoe_status launch_mode(const zmoe_ffn_args* a, const uint16_t* act, int K, int 
     p.rows_total = a->rows_total;
     p.K = K;
     p.n_out = n_out;
+    p.bn = bn;
     p.err = err;
     p.wait_limit = g_wait_limit;
     p.drop_loads = g_drop_loads;
-    ffn_tc_kernel<MODE><<<sms, kThreads, smem, stream>>>(p);
+    if (wide) ffn_tc_kernel<MODE, BNW><<<sms, kThreads, smem, stream>>>(p);
+    else ffn_tc_kernel<MODE, BN><<<sms, kThreads, smem, stream>>>(p);
     st = launch_status("ffn_tc_kernel");
     if (st != ZMOE_OK) return st;
   }
