@@ -868,8 +868,14 @@ zmoe_status launch_decode_chunks(const zmoe_chunk* chunks, int n_chunks, int32_t
   ZMOE_CHECK_ARG(n_chunks <= 65535, "decode_chunks: %d chunks in one launch (at most 65535)", n_chunks);
   constexpr int kMapColumns = 16;                     // map CTAs per chunk (each loops over regions)
   const int msmem = (int)sizeof(MapSmem), rsmem = (int)sizeof(Smem);
-  ZMOE_CUDA_RET(cudaFuncSetAttribute(map_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, msmem));
-  ZMOE_CUDA_RET(cudaFuncSetAttribute(resolve_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, rsmem));
+  static uint64_t attr_set = 0;                        // devices whose kernel attributes are set
+  int dev = 0;
+  ZMOE_CUDA_RET(cudaGetDevice(&dev));
+  if (!(attr_set & (1ull << (dev & 63)))) {
+    ZMOE_CUDA_RET(cudaFuncSetAttribute(map_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, msmem));
+    ZMOE_CUDA_RET(cudaFuncSetAttribute(resolve_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, rsmem));
+    attr_set |= 1ull << (dev & 63);
+  }
   map_kernel<<<dim3(kMapColumns, n_chunks), kThreads, msmem, stream>>>(chunks);
   zmoe_status st = launch_status("map_kernel");
   if (st != ZMOE_OK) return st;

@@ -29,6 +29,7 @@
 #include <cuda.h>
 
 #include <mutex>
+#include <unordered_map>
 
 #include "common.cuh"
 
@@ -430,8 +431,46 @@ EncodeTiled encoder() {
   return fn;
 }
 
+// Encoded maps by (base, rows, cols, box rows).  A map holds only an address
+// and a shape, so a cached one stays valid for any buffer at that address;
+// the layer's slot, shared-expert and activation buffers keep their addresses,
+// so after the first steps a launch encodes nothing on the host.
+struct MapKey {
+  uintptr_t base;
+  uint64_t rows, cols;
+  uint32_t box;
+  bool operator==(const MapKey& o) const { return base == o.base && rows == o.rows && cols == o.cols && box == o.box; }
+};
+struct MapKeyHash {
+  size_t operator()(const MapKey& k) const {
+    uint64_t h = k.base * 0x9E3779B97F4A7C15ull;
+    h ^= (k.rows + 0x632BE59BD9B4E019ull) + (h << 6) + (h >> 2);
+    h ^= (k.cols * 31 + k.box + 0x8CB92BA72F3D8DD7ull) + (h << 6) + (h >> 2);
+    return (size_t)h;
+  }
+};
+
+zmoe_status encode_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows);
+
 // 2D bf16 map over a row-major [rows, cols] matrix; box = BK columns x box_rows rows.
 zmoe_status make_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+  static std::mutex mu;
+  static std::unordered_map<MapKey, CUtensorMap, MapKeyHash> cache;
+  const MapKey key{reinterpret_cast<uintptr_t>(base), rows, cols, box_rows};
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find(key);
+  if (it != cache.end()) {
+    *m = it->second;
+    return ZMOE_OK;
+  }
+  zmoe_status st = encode_map(m, base, rows, cols, box_rows);
+  if (st != ZMOE_OK) return st;
+  if (cache.size() >= 8192) cache.clear();         // bounded: callers with ever-new buffers re-encode
+  cache.emplace(key, *m);
+  return ZMOE_OK;
+}
+
+zmoe_status encode_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
   EncodeTiled enc = encoder();
   if (!enc) {
     set_error("cuTensorMapEncodeTiled is not available");
@@ -468,10 +507,15 @@ zmoe_status launch_mode(const zmoe_ffn_args* a, const uint16_t* act, int K, int 
   const int bn = a->offsets ? BN : dense_tile((n_out + BM - 1) / BM, a->rows_total, K, per, sms);
   const bool wide = bn > BN;
   const int smem = wide ? smem_bytes<MODE, BNW>() : smem_bytes<MODE, BN>();
-  if (wide)
-    ZMOE_CUDA_RET(cudaFuncSetAttribute(ffn_tc_kernel<MODE, BNW>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-  else
-    ZMOE_CUDA_RET(cudaFuncSetAttribute(ffn_tc_kernel<MODE, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  static uint64_t attr_set[2] = {0, 0};              // per kernel variant: devices whose attribute is set
+  const uint64_t dbit = 1ull << (dev & 63);
+  if (!(attr_set[wide] & dbit)) {
+    if (wide)
+      ZMOE_CUDA_RET(cudaFuncSetAttribute(ffn_tc_kernel<MODE, BNW>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    else
+      ZMOE_CUDA_RET(cudaFuncSetAttribute(ffn_tc_kernel<MODE, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    attr_set[wide] |= dbit;
+  }
   for (int g0 = 0; g0 < a->G; g0 += gmax) {
     const int gc = a->G - g0 < gmax ? a->G - g0 : gmax;
     memset(&p, 0, sizeof(p));
