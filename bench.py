@@ -412,10 +412,12 @@ def run_ours(args):
         dec_s = st["decode_ns"] * 1e-9
         launches = max(st["decode_timed_launches"], 1)
         achieved = (st["decode_timed_bytes"] / launches) / (dec_s / launches) / 1e9 if dec_s > 0 else 0.0
-        traffic = None
+        traffic, traffic_src = None, None
         tp = os.path.join(ROOT, "profiles", "decode_traffic.json")
-        if os.path.exists(tp):
+        if os.path.exists(tp):          # an ncu figure for this launch, not measured in this run
             traffic = json.load(open(tp)).get("bytes_per_launch")
+            traffic_src = "ncu dram__bytes_read.sum + dram__bytes_write.sum of one 252-chunk launch pair " \
+                          "(profiles/decode_traffic.json), not measured in this run"
         line = {
             "metric": METRIC, "value": world * args.tokens / (ms / 1e3), "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
@@ -426,6 +428,7 @@ def run_ours(args):
                     "h2d_bytes_per_step": x.numel() * 2, "d2h_bytes_per_step": x.numel() * 2},
             "roofline": {"bound": "hbm", "kernel": "map_kernel+resolve_kernel (fused LZ4 decode)", "achieved": achieved,
                          "peak": hbm, "unit": "GB/s", "frac": achieved / hbm, "peak_source": src, "traffic": traffic,
+                         "traffic_source": traffic_src,
                          "algorithmic_bytes_per_launch": st["decode_timed_bytes"] / launches,
                          "kernel_ms_per_launch": dec_s * 1e3 / launches},
             "decode": {"experts_per_step": st["decoded_experts"] / args.steps,
