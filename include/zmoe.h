@@ -264,6 +264,32 @@ int zmoe_lz4_compress_bound(int n);
 int zmoe_lz4_compress(const uint8_t* src, int n, uint8_t* dst, int capacity, int codec, int level);
 
 /* --------------------------------------------------------------------------
+ * Offload-side codec on the GPU.
+ * zmoe_lz4_encode_chunks replaces the LZ4HCcompressor::compress calls
+ * (csrc/tensor_engine/compressors.cpp:105-122) that TensorEngine::PipelineCompress
+ * runs on one CPU thread per exponent chunk: every chunk of a launch is encoded
+ * at once.  The blocks are valid LZ4 blocks (any LZ4 decoder restores the
+ * chunk); they are not byte-identical to liblz4's.
+ * ------------------------------------------------------------------------ */
+typedef struct zmoe_enc_chunk {
+  const uint8_t* src;    /* device: the chunk's exponent bytes */
+  uint8_t* dst;          /* device: the LZ4 block */
+  void* scratch;         /* device, 16-byte aligned: zmoe_lz4_encode_scratch_bytes(src_size) bytes */
+  uint32_t src_size;     /* bytes in src */
+  uint32_t dst_capacity; /* bytes available at dst (zmoe_lz4_compress_bound(src_size) always suffices) */
+} zmoe_enc_chunk;
+
+/* chunks (n_chunks entries) and out_sizes are device arrays.  max_attempts
+ * (1..65536) bounds the hash-chain candidates tried per position, as LZ4HC's
+ * compression level does.  out_sizes[c] = block size, or 0 when the block did
+ * not fit dst_capacity or a pointer of chunk c was null or misaligned. */
+zmoe_status zmoe_lz4_encode_chunks(const zmoe_enc_chunk* chunks, int n_chunks, int max_attempts,
+                                   uint32_t* out_sizes, zmoe_stream_t stream);
+/* Scratch bytes a chunk of src_size bytes needs: chain link, match length
+ * and match offset per input byte. */
+uint64_t zmoe_lz4_encode_scratch_bytes(uint32_t src_size);
+
+/* --------------------------------------------------------------------------
  * MoE-layer engine (opaque handle).
  * Re-targets, for one layer, the reference's runtime around the hot path:
  * ZipMoEPrefetchHandle's stores and pools (csrc/prefetch/zipmoe_prefetch_handle.cpp:33-108),

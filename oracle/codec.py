@@ -18,6 +18,9 @@ CPU restatement of the reference's expert codec:
   osize, osize)`` as ``compressors.cpp:195-211`` does; ``lz4_decompress_restated``
   runs the C restatement in ``oracle/lz4_block.c`` on the same block.
 * ``recombine`` follows ``csrc/kernels/tensor_recover.cu:25-30``.
+* ``lz4_encode_chains`` is a serial statement of the GPU LZ4 encoder (a
+  different encoder from liblz4's LZ4HC, whose blocks any LZ4 decoder reads);
+  it is pinned by liblz4's decoder restoring every block it writes.
 
 liblz4 is the reference's third-party codec (``csrc/CMakeLists.txt:37``; the
 reference pins no version).  The image ships liblz4 1.9.4 as a runtime
@@ -70,6 +73,9 @@ def _oracle_lib() -> ctypes.CDLL:
         lib.zmoe_oracle_lz4_decode.restype = ctypes.c_int
         lib.zmoe_oracle_lz4_decode.argtypes = [
             ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int, ctypes.c_int]
+        lib.zmoe_oracle_lz4_encode_chains.restype = ctypes.c_int
+        lib.zmoe_oracle_lz4_encode_chains.argtypes = [
+            ctypes.c_void_p, ctypes.c_uint32, ctypes.c_void_p, ctypes.c_uint32, ctypes.c_int]
         lib.zmoe_oracle_recombine.restype = None
         lib.zmoe_oracle_recombine.argtypes = [
             ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t]
@@ -148,6 +154,18 @@ def lz4_compress_fast(chunk: np.ndarray, acceleration: int = 5) -> bytes:
     if n <= 0:
         raise RuntimeError("[LZ4] Compression Failed!")
     return dst.raw[:n]
+
+
+def lz4_encode_chains(chunk: np.ndarray, attempts: int = 256) -> bytes:
+    """Serial statement of the GPU encoder's parse (``lz4_block.c``), the
+    bit-exact check of ``zmoe_lz4_encode_chains``'s blocks."""
+    src = np.ascontiguousarray(chunk, dtype=np.uint8)
+    cap = src.size + src.size // 255 + 16
+    dst = np.zeros(max(cap, 1), dtype=np.uint8)
+    n = _oracle_lib().zmoe_oracle_lz4_encode_chains(src.ctypes.data, src.size, dst.ctypes.data, cap, attempts)
+    if n <= 0:
+        raise RuntimeError("oracle lz4 encode failed")
+    return dst[:n].tobytes()
 
 
 def lz4_decompress(block: bytes, original_size: int) -> np.ndarray:

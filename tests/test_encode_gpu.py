@@ -1,0 +1,124 @@
+"""GPU parity of the LZ4 block encoder (zmoe_lz4_encode_chunks): its blocks are
+bit-exact against the oracle's serial statement of the same parse, liblz4
+restores every block (the reference's decoder call), and the ratio is checked
+against LZ4_compress_HC level 9, which the reference's offload runs
+(csrc/tensor_engine/compressors.cpp:105-122)."""
+import ctypes
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import codec
+
+pytestmark = pytest.mark.gpu
+GOLD = os.path.join(os.path.dirname(__file__), "golden", "codec_cases.npz")
+
+
+def _ops():
+    from zmoe import ops
+    return ops
+
+
+def _dev(a: np.ndarray) -> torch.Tensor:
+    return torch.from_numpy(np.ascontiguousarray(a, dtype=np.uint8)).cuda()
+
+
+def _host(t: torch.Tensor) -> bytes:
+    return t.cpu().numpy().tobytes()
+
+
+def _check(chunks, attempts=256):
+    ops = _ops()
+    blocks = ops.lz4_encode_chunks([_dev(c) for c in chunks], attempts)
+    torch.cuda.synchronize()
+    for c, b in zip(chunks, blocks):
+        got = _host(b)
+        assert got == codec.lz4_encode_chains(c, attempts), (c.size, attempts)
+        assert np.array_equal(codec.lz4_decompress(got, c.size), c), c.size
+    return [_host(b) for b in blocks]
+
+
+def test_encode_golden_fixture_chunks():
+    g = np.load(GOLD)
+    ours = hc9 = 0
+    for key in g["names"]:
+        key = str(key)
+        if "__LZ4HC" not in key:
+            continue
+        bits = g[key.split("__")[0] + "__bits"]
+        nc = len(g[key + "__osz"])
+        exp, _ = codec.split_planes(bits)
+        chunks = codec.chunk_exponents(exp, nc)
+        got = _check(chunks)
+        ours += sum(len(b) for b in got)
+        hc9 += int(g[key + "__csz"].sum())
+    assert ours <= 1.01 * hc9, (ours, hc9)          # size tolerance: 1% over LZ4HC-9 on the fixture set
+
+
+@pytest.mark.parametrize("attempts", [1, 16, 256])
+def test_encode_edge_cases(attempts):
+    rng = np.random.default_rng(7)
+    chunks = [np.zeros(n, np.uint8) for n in (0, 1, 4, 11, 12, 13, 31, 32, 33)]
+    chunks += [rng.integers(0, 256, 70000).astype(np.uint8),          # incompressible, beyond the 64 KiB window
+               np.zeros(300000, np.uint8),                             # runs far past the 1024-byte search cap
+               np.tile(np.arange(7, dtype=np.uint8), 40000),          # period 7: overlapping matches
+               rng.integers(118, 125, 200001).astype(np.uint8)]       # exponent-like alphabet, odd size
+    _check(chunks, attempts)
+
+
+def test_encode_qwen_expert_matrix_ratio_and_gpu_decode():
+    """One Qwen1.5-MoE expert matrix (2048 x 1408 BF16): exponent chunks encoded
+    on the GPU, decoded by the GPU decoder into BF16 equal to the input, and
+    no larger than LZ4HC-9's blocks."""
+    ops = _ops()
+    gen = torch.Generator().manual_seed(0)
+    w = (torch.randn(1408, 2048, generator=gen) * 0.02).to(torch.bfloat16)
+    bits = codec.bf16_bits(w)
+    blocks, osz, sm = ops.encode_tensor(w.cuda(), 3, 256)
+    torch.cuda.synchronize()
+    exp, sm_ref = codec.split_planes(bits)
+    chunks = codec.chunk_exponents(exp, 3)
+    assert osz == [c.size for c in chunks]
+    assert np.array_equal(sm.cpu().numpy(), sm_ref)
+    host = [_host(b) for b in blocks]
+    for c, b in zip(chunks, host):
+        assert b == codec.lz4_encode_chains(c, 256)
+    hc9 = sum(len(codec.lz4_compress_hc(c, 9)) for c in chunks)
+    assert sum(len(b) for b in host) <= hc9
+    ct = ops.CompressedTensor(host, osz, sm_ref.tobytes())
+    out, st = ct.decode()
+    torch.cuda.synchronize()
+    assert (st.cpu().numpy() == 0).all()
+    assert np.array_equal(out.view(torch.int16).cpu().numpy().view(np.uint16), bits)
+
+
+def test_encode_reports_overflow_and_bad_descriptors():
+    """A block that does not fit dst_capacity, a null source and misaligned
+    scratch each give size 0 without touching the other chunks."""
+    from zmoe._lib import ZmoeEncChunk, lib
+    rng = np.random.default_rng(1)
+    src = _dev(rng.integers(0, 256, 5000).astype(np.uint8))
+    good = _dev(np.zeros(5000, np.uint8))
+    scr = int(lib.zmoe_lz4_encode_scratch_bytes(5000))
+    scratch = torch.zeros(4 * scr // 16 + 2, 2, dtype=torch.int64, device="cuda")
+    dst = torch.zeros(4, 8192, dtype=torch.uint8, device="cuda")
+    base = scratch.data_ptr()
+    arr = (ZmoeEncChunk * 4)()
+    arr[0] = ZmoeEncChunk(src.data_ptr(), dst[0].data_ptr(), base, 5000, 1000)            # too small
+    arr[1] = ZmoeEncChunk(None, dst[1].data_ptr(), base + scr, 5000, 8192)                # null source
+    arr[2] = ZmoeEncChunk(good.data_ptr(), dst[2].data_ptr(), base + 2 * scr + 8, 5000, 8192)   # misaligned
+    arr[3] = ZmoeEncChunk(good.data_ptr(), dst[3].data_ptr(), base + 3 * scr, 5000, 8192)
+    table = torch.frombuffer(bytearray(bytes(arr)), dtype=torch.uint8).cuda()
+    sizes = torch.full((4,), 7, dtype=torch.int32, device="cuda")
+    rc = lib.zmoe_lz4_encode_chunks(table.data_ptr(), 4, 64, sizes.data_ptr(),
+                                    torch.cuda.current_stream().cuda_stream)
+    assert rc == 0
+    s = sizes.cpu().tolist()
+    assert s[:3] == [0, 0, 0]
+    blk = dst[3, :s[3]].cpu().numpy().tobytes()
+    assert blk == codec.lz4_encode_chains(np.zeros(5000, np.uint8), 64)
+    assert (dst[0, 1000:] == 0).all()                # nothing written past the capacity
+    bad = lib.zmoe_lz4_encode_chunks(table.data_ptr(), 4, 0, sizes.data_ptr(), None)
+    assert bad != 0 and b"max_attempts" in lib.zmoe_last_error()

@@ -95,3 +95,41 @@ def test_restated_decoder_rejects_malformed():
     bad[off_pos + 1] = 0
     rc, _ = codec.lz4_decompress_restated(bytes(bad), exp.size)
     assert rc < 0
+
+
+def test_chain_encoder_statement_round_trips_through_liblz4(gold):
+    """The serial statement of the GPU encoder writes blocks that liblz4's
+    LZ4_decompress_safe_partial (the reference's decoder call) restores.  Size
+    tolerance against LZ4_compress_HC level 9: 2% (+4 bytes) per fixture chunk,
+    1% over the whole fixture set."""
+    ours = hc9 = 0
+    for key, bits, osz, blocks in _cases(gold):
+        if "__LZ4HC" not in key:
+            continue
+        exp, _ = codec.split_planes(bits)
+        chunks = codec.chunk_exponents(exp, len(osz))
+        for c, hc in zip(chunks, blocks):
+            b = codec.lz4_encode_chains(c, 256)
+            assert np.array_equal(codec.lz4_decompress(b, c.size), c), key
+            assert len(b) <= 1.02 * len(hc) + 4, (key, len(b), len(hc))
+            ours += len(b)
+            hc9 += len(hc)
+    assert ours <= 1.01 * hc9, (ours, hc9)
+
+
+def test_chain_encoder_statement_edge_cases():
+    rng = np.random.default_rng(3)
+    cases = [np.zeros(n, np.uint8) for n in (1, 4, 11, 12, 13, 17)]
+    cases += [rng.integers(0, 256, 70000).astype(np.uint8),            # incompressible, beyond the window
+              np.zeros(300000, np.uint8),                               # runs far past the 1024-byte search cap
+              np.tile(np.arange(7, dtype=np.uint8), 40000),            # period 7: overlapping matches
+              rng.integers(118, 125, 200000).astype(np.uint8)]         # exponent-like alphabet
+    for c in cases:
+        for att in (1, 16, 256):
+            b = codec.lz4_encode_chains(c, att)
+            assert np.array_equal(codec.lz4_decompress(b, c.size), c), (c.size, att)
+            assert len(b) <= c.size + c.size // 255 + 16
+    # more attempts never hurt on the exponent-like case
+    c = cases[-1]
+    sizes = [len(codec.lz4_encode_chains(c, a)) for a in (1, 16, 256)]
+    assert sizes[0] >= sizes[1] >= sizes[2]

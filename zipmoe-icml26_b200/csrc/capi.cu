@@ -16,6 +16,7 @@ void set_error(const char* fmt, ...) {
 
 zmoe_status launch_tensor_recover(uint16_t*, const uint8_t*, const uint8_t*, size_t, cudaStream_t);
 zmoe_status launch_decode_chunks(const zmoe_chunk*, int, int32_t*, cudaStream_t);
+zmoe_status launch_encode_chunks(const zmoe_enc_chunk*, int, int, uint32_t*, cudaStream_t);
 zmoe_status launch_router(const zmoe_router_args*, cudaStream_t);
 zmoe_status launch_permute(const zmoe_permute_args*, cudaStream_t);
 zmoe_status launch_combine(const zmoe_combine_args*, cudaStream_t);
@@ -50,6 +51,14 @@ zmoe_status zmoe_decode_chunks(const zmoe_chunk* chunks, int n_chunks, int32_t* 
   ZMOE_CHECK_ARG(n_chunks >= 0, "decode_chunks: negative count");
   ZMOE_CHECK_ARG(n_chunks == 0 || (chunks && status), "decode_chunks: null pointer");
   return zmoe::launch_decode_chunks(chunks, n_chunks, status, reinterpret_cast<cudaStream_t>(stream));
+}
+
+zmoe_status zmoe_lz4_encode_chunks(const zmoe_enc_chunk* chunks, int n_chunks, int max_attempts,
+                                   uint32_t* out_sizes, zmoe_stream_t stream) {
+  ZMOE_CHECK_ARG(n_chunks >= 0, "lz4_encode: negative count");
+  ZMOE_CHECK_ARG(n_chunks == 0 || (chunks && out_sizes), "lz4_encode: null pointer");
+  return zmoe::launch_encode_chunks(chunks, n_chunks, max_attempts, out_sizes,
+                                    reinterpret_cast<cudaStream_t>(stream));
 }
 
 zmoe_status zmoe_router(const zmoe_router_args* a, zmoe_stream_t stream) {

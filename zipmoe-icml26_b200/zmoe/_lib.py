@@ -23,6 +23,11 @@ class ZmoeChunk(ctypes.Structure):
                 ("src_size", c_u32), ("out_size", c_u32), ("n_index", c_u32), ("seg_bytes", c_u32)]
 
 
+class ZmoeEncChunk(ctypes.Structure):
+    _fields_ = [("src", c_void_p), ("dst", c_void_p), ("scratch", c_void_p),
+                ("src_size", c_u32), ("dst_capacity", c_u32)]
+
+
 SLICE_BYTES = 256        # ZMOE_SLICE_BYTES
 MAP_ENTRIES = 65536      # ZMOE_MAP_ENTRIES (per 64 KiB region)
 
@@ -93,6 +98,8 @@ SIGNATURES = {
     "zmoe_lz4_compress_bound": (c_int, [c_int]),
     "zmoe_lz4_compress": (c_int, [c_void_p, c_int, c_void_p, c_int, c_int, c_int]),
     "zmoe_lz4_build_index": (c_int, [c_void_p, c_u32, c_u32, c_u32, c_void_p, c_int]),
+    "zmoe_lz4_encode_chunks": (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p]),
+    "zmoe_lz4_encode_scratch_bytes": (ctypes.c_uint64, [c_u32]),
     "zmoe_layer_create": (c_int, [ctypes.POINTER(LayerConfig), ctypes.POINTER(c_void_p)]),
     "zmoe_layer_destroy": (c_int, [c_void_p]),
     "zmoe_layer_set_router": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p]),

@@ -12,7 +12,7 @@ import numpy as np
 import torch
 
 from . import _lib
-from ._lib import CombineArgs, FfnArgs, PermuteArgs, RouterArgs, ZmoeChunk, check, lib
+from ._lib import CombineArgs, FfnArgs, PermuteArgs, RouterArgs, ZmoeChunk, ZmoeEncChunk, check, lib
 
 ROUTE_QWEN, ROUTE_DEEPSEEK, ROUTE_SWITCH = 0, 1, 2
 
@@ -96,6 +96,58 @@ def decode_chunks(table: torch.Tensor, n: int, status: Optional[torch.Tensor] = 
         status = torch.full((max(n, 1),), -1, dtype=torch.int32, device=table.device)
     check(lib.zmoe_decode_chunks(table.data_ptr(), n, status.data_ptr(), _stream()), "zmoe_decode_chunks")
     return status[:n]
+
+
+def lz4_encode_chunks(chunks: Sequence[torch.Tensor], max_attempts: int = 256) -> List[torch.Tensor]:
+    """LZ4 blocks of uint8 device chunks, all encoded in one zmoe_lz4_encode_chunks
+    launch (replaces LZ4HCcompressor::compress, csrc/tensor_engine/compressors.cpp:105-122,
+    run per chunk on the CPU).  Returns one uint8 device tensor per chunk (views
+    into one buffer); waits once for the block sizes."""
+    if not chunks:
+        return []
+    dev = chunks[0].device
+    for c in chunks:
+        _need(c, torch.uint8, "chunk")
+    caps = [c.numel() + c.numel() // 255 + 16 for c in chunks]
+    scr = [(int(lib.zmoe_lz4_encode_scratch_bytes(c.numel())) + 15) // 16 * 16 for c in chunks]
+    dst = torch.empty(sum(caps), dtype=torch.uint8, device=dev)
+    scratch = torch.empty(max(sum(scr), 16) // 16, 2, dtype=torch.int64, device=dev)   # 16-byte aligned
+    arr = (ZmoeEncChunk * len(chunks))()
+    doff = soff = 0
+    for i, c in enumerate(chunks):
+        arr[i] = ZmoeEncChunk(c.data_ptr(), dst.data_ptr() + doff, scratch.data_ptr() + soff, c.numel(), caps[i])
+        doff += caps[i]
+        soff += scr[i]
+    table = torch.frombuffer(bytearray(bytes(arr)), dtype=torch.uint8).to(dev)
+    sizes = torch.zeros(len(chunks), dtype=torch.int32, device=dev)
+    check(lib.zmoe_lz4_encode_chunks(table.data_ptr(), len(chunks), int(max_attempts), sizes.data_ptr(), _stream()),
+          "zmoe_lz4_encode_chunks")
+    host = sizes.cpu().tolist()
+    out, doff = [], 0
+    for i, n in enumerate(host):
+        if n <= 0:
+            raise _lib.ZmoeError(f"zmoe_lz4_encode_chunks: chunk {i} did not encode")
+        out.append(dst[doff:doff + n])
+        doff += caps[i]
+    return out
+
+
+def encode_tensor(bits: torch.Tensor, num_file_chunks: int = 3, max_attempts: int = 256):
+    """Offload form of one BF16 tensor on the GPU: the exponent plane cut into
+    num_file_chunks LZ4 blocks and the sign+mantissa plane
+    (runtime/model_offload.py:706-726, then TensorEngine::PipelineCompress).
+    bits: BF16 (or its int16 view) on the device.  Returns (blocks as device
+    tensors, original_sizes, sm as a device uint8 tensor)."""
+    if not bits.is_cuda or bits.dtype not in (torch.bfloat16, torch.int16):
+        raise ValueError("encode_tensor: expected a CUDA bfloat16 tensor")
+    u = bits.contiguous().view(torch.int16).reshape(-1).to(torch.int32) & 0xFFFF
+    exp = ((u >> 7) & 0xFF).to(torch.uint8)
+    sm = (((u >> 15) & 1) << 7 | (u & 0x7F)).to(torch.uint8)
+    n = exp.numel()
+    per = -(-n // num_file_chunks)                  # ceil(n / c) bytes per chunk, the last shorter
+    pieces = [exp[min(n, c * per):min(n, (c + 1) * per)] for c in range(num_file_chunks)]
+    blocks = lz4_encode_chunks(pieces, max_attempts)
+    return blocks, [p.numel() for p in pieces], sm
 
 
 class CompressedTensor:
