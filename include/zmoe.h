@@ -286,7 +286,7 @@ typedef struct zmoe_enc_chunk {
 zmoe_status zmoe_lz4_encode_chunks(const zmoe_enc_chunk* chunks, int n_chunks, int max_attempts,
                                    uint32_t* out_sizes, zmoe_stream_t stream);
 /* Scratch bytes a chunk of src_size bytes needs: chain link, match length
- * and match offset per input byte. */
+ * and match offset per input byte, and a 32-byte record per 16 KiB. */
 uint64_t zmoe_lz4_encode_scratch_bytes(uint32_t src_size);
 
 /* --------------------------------------------------------------------------

@@ -95,7 +95,9 @@ void zmoe_oracle_recombine(const uint8_t* exp, const uint8_t* sm, uint16_t* out,
  *            hash = (le32 * 2654435761) >> 17;
  *   match[i] the longest of at most `attempts` chain candidates inside the
  *            64 KiB window (searched up to 1024 bytes; the nearest wins ties),
- *            none reaching into the last 5 bytes, none starting in the last 12;
+ *            none reaching into the last 5 bytes, none starting in the last 12,
+ *            none crossing a 16 KiB segment boundary (the GPU parses the
+ *            segments in parallel);
  *   parse    greedy with one step of lazy evaluation (a match is put off by
  *            one byte when the next position, if it may start a match, has a
  *            longer one); a match searched to 1024 bytes is extended while the
@@ -107,6 +109,7 @@ void zmoe_oracle_recombine(const uint8_t* exp, const uint8_t* sm, uint16_t* out,
 
 #define ENC_NONE 0xFFFFFFFFu
 #define ENC_LEN_CAP 1024u
+#define ENC_SEGMENT 16384u
 
 static uint32_t enc_rd4(const uint8_t* p) {
   return (uint32_t)p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16) | ((uint32_t)p[3] << 24);
@@ -154,9 +157,12 @@ int zmoe_oracle_lz4_encode_chains(const uint8_t* src, uint32_t n, uint8_t* dst, 
   }
   for (uint32_t i = 0; i < n; ++i) {
     uint32_t best = 0, best_off = 0;
-    if (i + 12 <= n) {
+    uint32_t seg_end = (i / ENC_SEGMENT + 1) * ENC_SEGMENT;
+    if (seg_end > n) seg_end = n;
+    if (i + 12 <= n && seg_end - i >= 4) {
       uint32_t max_len = n - 5 - i;
       if (max_len > ENC_LEN_CAP) max_len = ENC_LEN_CAP;
+      if (max_len > seg_end - i) max_len = seg_end - i;
       uint32_t key = enc_rd4(src + i), cand = prev[i];
       for (int a = 0; a < attempts && cand != ENC_NONE; ++a) {
         if (cand >= i || i - cand > 65535) break;
@@ -182,8 +188,11 @@ int zmoe_oracle_lz4_encode_chains(const uint8_t* src, uint32_t n, uint8_t* dst, 
       uint32_t len = mlen[i];
       if (len < 4 || (i + 13 <= n && mlen[i + 1] > len)) { ++i; continue; }
       uint32_t off = moff[i], ml = len;
-      if (ml == ENC_LEN_CAP)
-        while (i + ml < n - 5 && src[i + ml] == src[i + ml - off]) ++ml;
+      if (ml == ENC_LEN_CAP) {
+        uint32_t end = (i / ENC_SEGMENT + 1) * ENC_SEGMENT;
+        if (end > n - 5) end = n - 5;
+        while (i + ml < end && src[i + ml] == src[i + ml - off]) ++ml;
+      }
       enc_sequence(&o, src + anchor, i - anchor, off, ml);
       i += ml;
       anchor = i;
