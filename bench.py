@@ -59,11 +59,16 @@ def parse():
                     help="where the compressed experts live (host: pinned memory, copied in per miss)")
     ap.add_argument("--sm-slots", type=int, default=0,
                     help="host store: experts whose sign+mantissa planes stay in HBM (the SMCACHE pool)")
-    ap.add_argument("--config", default="qwen", choices=["qwen", "decode-sweep", "switch", "deepseek-stack"],
+    ap.add_argument("--matrices", type=int, default=180,
+                    help="encode: expert matrices converted per step (180 = one layer's 60 experts)")
+    ap.add_argument("--attempts", type=int, default=256,
+                    help="encode: hash-chain candidates tried per position (LZ4HC level 9 tries 256)")
+    ap.add_argument("--config", default="qwen", choices=["qwen", "decode-sweep", "switch", "deepseek-stack", "encode"],
                     help="qwen: the Qwen1.5-MoE layer (default; the headline line, with a token-count sweep); "
                          "decode-sweep: decode+recombine GB/s over sizes and weight distributions; "
                          "switch: the Switch-large-128 layer at 4096 tokens; deepseek-stack: 26 "
-                         "DeepSeek-V2-Lite MoE layers at decode batch sizes, with and without next-layer prefetch")
+                         "DeepSeek-V2-Lite MoE layers at decode batch sizes, with and without next-layer prefetch; "
+                         "encode: the offload conversion (plane split + LZ4 encode) of one layer's 60 experts")
     ap.add_argument("--timeline", default=None,
                     help="write the GPU timeline of 3 more steps (kernels and copies per stream, "
                          "torch.profiler over CUPTI) to this text file")
@@ -999,10 +1004,159 @@ def cpu_baseline(args, s, enc, extra):
                       f"{threads} threads, torch CPU BF16 experts)"}
 
 
+ENCODE_METRIC = "expert LZ4 encode GB/s (exponent bytes in)"
+
+
+def encode_config(args):
+    m = args.matrices
+    return {"workload": "qwen1.5-moe-layer-offload" if m == 180 else f"qwen1.5-moe-offload-{m}-matrices",
+            "experts": -(-m // 3), "matrices": m, "matrices_shape": "gate/up 1408 x 2048, down 2048 x 1408",
+            "num_file_chunks": args.chunks, "chunks": m * args.chunks, "exponent_bytes": m * 1408 * 2048,
+            "l2": f"inputs {'larger' if m * 1408 * 2048 > 126e6 else 'smaller'} than L2 "
+                  f"({m * 1408 * 2048 / 1e6:.0f} MB of exponent bytes)"}
+
+
+def cpu_encode_baseline(args, mats, threads):
+    """liblz4 LZ4_compress_HC at the configured level, one exponent chunk per
+    task on every host thread (TensorEngine::PipelineCompress's compute pool),
+    over the chunks of the first 8 matrices."""
+    from concurrent.futures import ThreadPoolExecutor
+    from oracle import codec as oc
+    chunks = []
+    for m in mats[:8]:
+        exp, _ = oc.split_planes(codec_bits(m).numpy().view(np.uint16))
+        chunks += oc.chunk_exponents(exp, args.chunks)
+    t0 = time.perf_counter()
+    with ThreadPoolExecutor(max_workers=threads) as ex:
+        out = list(ex.map(lambda c: len(oc.lz4_compress_hc(c, args.level)), chunks))
+    dt = time.perf_counter() - t0
+    n = sum(c.size for c in chunks)
+    return {"value": n / dt / 1e9, "unit": "GB/s", "cores": threads, "cpu_model": cpu_model(), "kind": "port",
+            "ratio": sum(out) / n,
+            "sample": f"{len(chunks)} exponent chunks of 961,195 B compressed by liblz4 LZ4_compress_HC level "
+                      f"{args.level} on {threads} threads"}
+
+
+def run_encode(args):
+    """Offload conversion of one Qwen1.5-MoE layer's 60 routed experts (180
+    BF16 matrices of 1408 x 2048): per matrix the plane split and its exponent
+    plane cut into 3 chunks, then every chunk LZ4-encoded in one launch
+    (zmoe_lz4_encode_chunks, 256 hash-chain candidates per position, as LZ4HC
+    level 9).  value: exponent bytes per second with the weights resident;
+    e2e: the same through ops.encode_tensors with the BF16 weights copied in
+    from pinned host memory and the blocks and sign+mantissa planes copied
+    back every step."""
+    from zmoe import ops
+    from zmoe import synthetic as syn
+    world, rank, local = dist_env()
+    if rank != 0:
+        return
+    torch.cuda.set_device(local)
+    s = syn.QWEN
+    mats = [t for e in syn.expert_weights(s, 1)[0] for t in e][:args.matrices]
+    dev = [m.cuda() for m in mats]
+    n_exp = sum(m.numel() for m in mats)
+    for _ in range(max(args.warmup, 3)):
+        enc = ops.encode_tensors(dev, args.chunks, args.attempts)
+    torch.cuda.synchronize()
+    # parity of every block of the first matrix against the oracle's statement
+    from oracle import codec as oc
+    exp0, _ = oc.split_planes(codec_bits(mats[0]).numpy().view(np.uint16))
+    for c, b in zip(oc.chunk_exponents(exp0, args.chunks), enc[0][0]):
+        if b.cpu().numpy().tobytes() != oc.lz4_encode_chains(c, args.attempts):
+            raise RuntimeError("GPU LZ4 block differs from the oracle's")
+    out_bytes = sum(b.numel() for e in enc for b in e[0])
+    del enc
+    stream = torch.cuda.current_stream()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        torch.cuda.synchronize()
+        a.record(stream)
+        for i in range(args.steps):
+            clk.probe(i, args.steps)
+            enc = ops.encode_tensors(dev, args.chunks, args.attempts)
+        b.record(stream)
+        torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / args.steps
+    # end to end: pinned host weights in, blocks and sm planes out, every step
+    hw = [m.contiguous().pin_memory() for m in mats]
+    caps = sum(m.numel() + m.numel() // 255 + 16 for m in mats)
+    hb = torch.empty(caps, dtype=torch.uint8).pin_memory()
+    hs = torch.empty(n_exp, dtype=torch.uint8).pin_memory()
+    dw = [torch.empty_like(d) for d in dev]
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    d2h = 0
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(args.steps):
+        for h, d in zip(hw, dw):
+            d.copy_(h, non_blocking=True)
+        enc = ops.encode_tensors(dw, args.chunks, args.attempts)
+        bo = so = 0
+        d2h = 0
+        for blocks, _, sm in enc:
+            for blk in blocks:
+                hb[bo:bo + blk.numel()].copy_(blk, non_blocking=True)
+                bo += blk.numel()
+            hs[so:so + sm.numel()].copy_(sm, non_blocking=True)
+            so += sm.numel()
+        d2h = bo + so
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    threads = os.cpu_count() or 1
+    cpu = None if args.no_cpu_baseline else cpu_encode_baseline(args, mats, threads)
+    hbm, _, src = peaks()
+    alg = n_exp + out_bytes                              # exponent bytes read, block bytes written
+    line = {"metric": ENCODE_METRIC, "value": n_exp / (ms * 1e-3) / 1e9, "unit": "GB/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "u8",
+            "data": "synthetic (seeded N(0,0.02) BF16 weights)", "config": encode_config(args),
+            "attempts": args.attempts, "ratio": out_bytes / n_exp,
+            "e2e": {"value": n_exp / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": 2 * n_exp,
+                    "d2h_bytes_per_step": d2h},
+            "roofline": {"bound": "hbm", "kernel": "chain+match+plan+scan+write (LZ4 encode)",
+                         "achieved": alg / (ms * 1e-3) / 1e9, "peak": hbm, "unit": "GB/s",
+                         "frac": alg / (ms * 1e-3) / 1e9 / hbm, "peak_source": src, "traffic": None,
+                         "note": "the match search is bound by instruction issue in shared memory, not by HBM"},
+            "gpu_launches": 5 * args.steps, "clocks": clk.summary()}
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
+
+
+def run_encode_reference(args):
+    """The reference's offload compression on the host cores: liblz4
+    LZ4_compress_HC per exponent chunk on every thread (oracle bindings; no
+    code of this repository's library)."""
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return
+    from zmoe import synthetic as syn
+    mats = [t for e in syn.expert_weights(syn.QWEN, 1)[0] for t in e][:args.matrices]
+    threads = os.cpu_count() or 1
+    for _ in range(args.warmup):
+        cpu_encode_baseline(args, mats[:1], threads)
+    vals = [cpu_encode_baseline(args, mats, threads) for _ in range(args.steps)]
+    v = statistics.median(x["value"] for x in vals)
+    cb = dict(vals[0], value=v)
+    n = min(8, len(mats)) * 1408 * 2048
+    line = {"impl": "reference", "metric": ENCODE_METRIC, "value": v, "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": n / (v * 1e9) * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8",
+            "data": "synthetic (seeded N(0,0.02) BF16 weights)", "config": encode_config(args),
+            "cpu_baseline": cb, "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
-    if args.impl == "reference":
+    if args.impl == "reference" and args.config == "encode":
+        run_encode_reference(args)
+    elif args.impl == "reference":
         run_reference(args)
+    elif args.config == "encode":
+        run_encode(args)
     elif args.config == "decode-sweep":
         run_decode_sweep(args)
     elif args.config == "switch":

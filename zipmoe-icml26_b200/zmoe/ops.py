@@ -132,22 +132,38 @@ def lz4_encode_chunks(chunks: Sequence[torch.Tensor], max_attempts: int = 256) -
     return out
 
 
+def _split_exponents(bits: torch.Tensor, num_file_chunks: int):
+    """Exponent plane cut into num_file_chunks pieces of ceil(n / c) bytes (the
+    last shorter) and the sign+mantissa plane (runtime/model_offload.py:706-726)."""
+    if not bits.is_cuda or bits.dtype not in (torch.bfloat16, torch.int16):
+        raise ValueError("encode: expected a CUDA bfloat16 tensor")
+    u = bits.contiguous().view(torch.int16).reshape(-1).to(torch.int32) & 0xFFFF
+    exp = ((u >> 7) & 0xFF).to(torch.uint8)
+    sm = (((u >> 15) & 1) << 7 | (u & 0x7F)).to(torch.uint8)
+    n = exp.numel()
+    per = -(-n // num_file_chunks)
+    return [exp[min(n, c * per):min(n, (c + 1) * per)] for c in range(num_file_chunks)], sm
+
+
 def encode_tensor(bits: torch.Tensor, num_file_chunks: int = 3, max_attempts: int = 256):
     """Offload form of one BF16 tensor on the GPU: the exponent plane cut into
     num_file_chunks LZ4 blocks and the sign+mantissa plane
     (runtime/model_offload.py:706-726, then TensorEngine::PipelineCompress).
     bits: BF16 (or its int16 view) on the device.  Returns (blocks as device
     tensors, original_sizes, sm as a device uint8 tensor)."""
-    if not bits.is_cuda or bits.dtype not in (torch.bfloat16, torch.int16):
-        raise ValueError("encode_tensor: expected a CUDA bfloat16 tensor")
-    u = bits.contiguous().view(torch.int16).reshape(-1).to(torch.int32) & 0xFFFF
-    exp = ((u >> 7) & 0xFF).to(torch.uint8)
-    sm = (((u >> 15) & 1) << 7 | (u & 0x7F)).to(torch.uint8)
-    n = exp.numel()
-    per = -(-n // num_file_chunks)                  # ceil(n / c) bytes per chunk, the last shorter
-    pieces = [exp[min(n, c * per):min(n, (c + 1) * per)] for c in range(num_file_chunks)]
-    blocks = lz4_encode_chunks(pieces, max_attempts)
-    return blocks, [p.numel() for p in pieces], sm
+    return encode_tensors([bits], num_file_chunks, max_attempts)[0]
+
+
+def encode_tensors(tensors: Sequence[torch.Tensor], num_file_chunks: int = 3, max_attempts: int = 256):
+    """encode_tensor for many tensors, every chunk of every tensor in one
+    zmoe_lz4_encode_chunks launch (TensorEngine::PipelineCompress's chunks all
+    at once).  Returns [(blocks, original_sizes, sm)] in order."""
+    split = [_split_exponents(t, num_file_chunks) for t in tensors]
+    blocks = lz4_encode_chunks([p for pieces, _ in split for p in pieces], max_attempts)
+    out = []
+    for k, (pieces, sm) in enumerate(split):
+        out.append((blocks[k * num_file_chunks:(k + 1) * num_file_chunks], [p.numel() for p in pieces], sm))
+    return out
 
 
 class CompressedTensor:
