@@ -99,3 +99,35 @@ def test_begin_end_materialise_registered_tensor(tmp_path):
     h.end(0, p)
     assert p.numel() == 1 and not p.is_cuda
     assert h.get_node_default_device([tid]) == torch.cuda.current_device()
+
+
+def test_batch_offload_with_gpu_encoder(tmp_path):
+    """set_gpu_encode(True): batch_offload encodes every LZ4HC chunk of the
+    batch on the GPU.  The file keeps the reference's layout; each block is
+    the oracle's statement of the GPU parse byte for byte, liblz4 restores it,
+    and begin() materialises every tensor exactly."""
+    import numpy as np
+    import ZipMoE
+    from oracle import codec, fmt
+    g = torch.Generator().manual_seed(9)
+    ts = [(torch.randn(96, 256, generator=g) * 0.05).to(torch.bfloat16) for _ in range(6)]
+    h = make_handle(ZipMoE, str(tmp_path), 2, 1, 3, 96 * 256, 1)
+    h.set_gpu_encode(True)
+    ids = list(range(200, 206))
+    chunks, sms = zip(*[split_exp_chunks(t, 3) for t in ts])
+    h.batch_offload(ids, ts, list(chunks), list(sms))
+    h.open_offload_file()
+    metas = fmt.deserialize_index((tmp_path / "zipmoe_index").read_bytes())
+    raw = (tmp_path / "zipmoe_param").read_bytes()
+    for tid, t, cs in zip(ids, ts, chunks):
+        m = metas[tid]
+        for c, off, csz, osz in zip(cs, m.exp_file_offsets, m.compressed_sizes, m.original_sizes):
+            blk = raw[off:off + csz]
+            c = np.ascontiguousarray(c, dtype=np.uint8)
+            assert osz == c.size and blk == codec.lz4_encode_chains(c, 256)
+            assert np.array_equal(codec.lz4_decompress(blk, osz), c)
+        p = torch.nn.Parameter(torch.zeros(1, dtype=torch.bfloat16), requires_grad=False)
+        h.register(p.data, tid)
+        assert h.begin(0, p) == tid
+        assert torch.equal(p.data.cpu().view(torch.int16), t.view(torch.int16))
+        h.end(0, p)

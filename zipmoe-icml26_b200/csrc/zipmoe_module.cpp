@@ -245,6 +245,8 @@ struct Config {
   size_t num_elements_per_expert = 0, num_tensors_per_expert = 3;
   int num_expert_layers = 1, num_experts = 1;
   int lz4_accel = 1, lz4hc_level = 9;
+  bool gpu_encode = false;   // batch_offload encodes LZ4HC chunks on the GPU (zmoe_lz4_encode_chunks)
+  int gpu_encode_attempts = 256;
 };
 
 struct Store {
@@ -396,6 +398,70 @@ std::vector<uint8_t> compress_chunk(const Config& cfg, const uint8_t* src, size_
   return out;
 }
 
+// LZ4 blocks of host chunks, encoded on the current GPU: every chunk of a
+// group of up to 512 MiB goes in one zmoe_lz4_encode_chunks call (replaces
+// the compute pool's per-chunk LZ4HCcompressor::compress,
+// csrc/tensor_engine/tensor_engine.cpp:105-136).
+std::vector<std::vector<uint8_t>> gpu_compress_chunks(const std::vector<std::pair<const uint8_t*, size_t>>& chunks,
+                                                      int attempts) {
+  std::vector<std::vector<uint8_t>> out(chunks.size());
+  const int dev = c10::cuda::current_device();
+  const auto u8 = torch::TensorOptions().dtype(torch::kUInt8);
+  const auto on_dev = u8.device(torch::kCUDA, dev);
+  cudaStream_t stream = c10::cuda::getCurrentCUDAStream(dev).stream();
+  const uint64_t kGroupBytes = 512ull << 20;
+  size_t g0 = 0;
+  while (g0 < chunks.size()) {
+    size_t g1 = g0;
+    uint64_t in_total = 0, cap_total = 0, scr_total = 0;
+    std::vector<uint64_t> in_off, cap_off, scr_off, cap;
+    while (g1 < chunks.size() && g1 - g0 < 65535 && (g1 == g0 || in_total + chunks[g1].second <= kGroupBytes)) {
+      const uint64_t n = chunks[g1].second;
+      if (n > (1u << 30)) fail("exponent chunk too large for the GPU encoder (1 GiB at most)");
+      in_off.push_back(in_total);
+      cap_off.push_back(cap_total);
+      scr_off.push_back(scr_total);
+      cap.push_back(n + n / 255 + 16);
+      in_total += (n + 15) / 16 * 16;
+      cap_total += cap.back();
+      scr_total += (zmoe_lz4_encode_scratch_bytes((uint32_t)n) + 15) / 16 * 16;
+      ++g1;
+    }
+    const size_t k = g1 - g0;
+    torch::Tensor hin = torch::empty({(int64_t)std::max<uint64_t>(in_total, 16)}, u8.pinned_memory(true));
+    for (size_t c = 0; c < k; ++c)
+      if (chunks[g0 + c].second) std::memcpy(hin.data_ptr<uint8_t>() + in_off[c], chunks[g0 + c].first, chunks[g0 + c].second);
+    torch::Tensor din = hin.to(on_dev, /*non_blocking=*/true);
+    torch::Tensor dout = torch::empty({(int64_t)cap_total}, on_dev);
+    torch::Tensor dscr = torch::empty({(int64_t)std::max<uint64_t>(scr_total, 16)}, on_dev);
+    std::vector<zmoe_enc_chunk> desc(k);
+    for (size_t c = 0; c < k; ++c) {
+      desc[c].src = din.data_ptr<uint8_t>() + in_off[c];
+      desc[c].dst = dout.data_ptr<uint8_t>() + cap_off[c];
+      desc[c].scratch = dscr.data_ptr<uint8_t>() + scr_off[c];
+      desc[c].src_size = (uint32_t)chunks[g0 + c].second;
+      desc[c].dst_capacity = (uint32_t)cap[c];
+    }
+    torch::Tensor hdesc = torch::from_blob(desc.data(), {(int64_t)(k * sizeof(zmoe_enc_chunk))}, u8);
+    torch::Tensor ddesc = hdesc.to(on_dev);
+    torch::Tensor dsizes = torch::zeros({(int64_t)k}, on_dev.dtype(torch::kInt32));
+    check(zmoe_lz4_encode_chunks(reinterpret_cast<const zmoe_enc_chunk*>(ddesc.data_ptr()), (int)k, attempts,
+                                 reinterpret_cast<uint32_t*>(dsizes.data_ptr<int32_t>()),
+                                 reinterpret_cast<zmoe_stream_t>(stream)),
+          "zmoe_lz4_encode_chunks");
+    torch::Tensor hsizes = dsizes.cpu();
+    torch::Tensor hout = dout.cpu();
+    for (size_t c = 0; c < k; ++c) {
+      const int32_t got = hsizes.data_ptr<int32_t>()[c];
+      if (got <= 0) fail("GPU LZ4 encoding failed");
+      const uint8_t* b = hout.data_ptr<uint8_t>() + cap_off[c];
+      out[g0 + c].assign(b, b + got);
+    }
+    g0 = g1;
+  }
+  return out;
+}
+
 // ---------------------------------------------------------------------------
 // zipmoe_prefetch_handle
 // ---------------------------------------------------------------------------
@@ -514,12 +580,32 @@ class PrefetchHandle {
     std::lock_guard<std::mutex> g(s_->mu);
     for (size_t i = 0; i < n; ++i)
       if (s_->index.has(tensor_ids[i])) fail("tensor " + std::to_string(tensor_ids[i]) + " is offloaded twice");
+    std::vector<std::vector<uint8_t>> gpu_blocks;   // every chunk of the batch, in order
+    const bool gpu = s_->cfg.gpu_encode && s_->cfg.code_type == "LZ4HC";
+    if (gpu) {
+      std::vector<std::pair<const uint8_t*, size_t>> all;
+      for (auto& a : arrays) all.insert(all.end(), a.chunks.begin(), a.chunks.end());
+      gpu_blocks = gpu_compress_chunks(all, s_->cfg.gpu_encode_attempts);
+    }
+    size_t next = 0;
     for (size_t i = 0; i < n; ++i) {
       Meta m = meta_of(tensor_ids[i], tensors[i], s_->cfg.num_file_chunks);
-      store_sparse(m, arrays[i]);
+      store_sparse(m, arrays[i], gpu ? &gpu_blocks[next] : nullptr);
+      next += arrays[i].chunks.size();
       s_->index.insert(tensor_ids[i], std::move(m));
     }
     write_file(s_->prefix + kIndexName, s_->index.serialize());
+  }
+
+  // Extension (no counterpart in the reference): batch_offload encodes LZ4HC
+  // chunks on the GPU, trying `attempts` hash-chain candidates per position
+  // (256, as LZ4HC level 9).  The blocks are valid LZ4 blocks but not liblz4's
+  // bytes; the file layout and the index are unchanged.
+  void set_gpu_encode(bool on, int attempts) {
+    if (attempts < 1 || attempts > 65536) fail("set_gpu_encode: attempts outside [1, 65536]");
+    std::lock_guard<std::mutex> g(s_->mu);
+    s_->cfg.gpu_encode = on;
+    s_->cfg.gpu_encode_attempts = attempts;
   }
 
   void register_tensor(torch::Tensor& tensor, uint32_t tensor_id) {
@@ -612,7 +698,8 @@ class PrefetchHandle {
   }
   // Compress the chunks on up to num_compute_threads threads, then append
   // chunk by chunk and the sign+mantissa plane (PipelineCompress order).
-  void store_sparse(Meta& m, const ChunkArrays& a) {
+  // blocks: the chunks' LZ4 blocks when already encoded (GPU path), else null
+  void store_sparse(Meta& m, const ChunkArrays& a, const std::vector<uint8_t>* pre = nullptr) {
     const int n = (int)a.chunks.size();
     if (n != m.num_file_chunks)
       fail("tensor " + std::to_string(m.id) + ": " + std::to_string(n) + " exponent chunks, num_file_chunks = " +
@@ -622,13 +709,17 @@ class PrefetchHandle {
     if (total != m.num_elements || a.sm_size != m.num_elements)
       fail("tensor " + std::to_string(m.id) + ": planes do not hold num_elements bytes");
     std::vector<std::vector<uint8_t>> blocks(n);
-    std::vector<std::future<void>> jobs;
-    const int threads = std::min(n, s_->cfg.num_compute_threads);
-    for (int w = 0; w < threads; ++w)
-      jobs.push_back(std::async(std::launch::async, [&, w] {
-        for (int c = w; c < n; c += threads) blocks[c] = compress_chunk(s_->cfg, a.chunks[c].first, a.chunks[c].second);
-      }));
-    for (auto& j : jobs) j.get();
+    if (pre) {
+      for (int c = 0; c < n; ++c) blocks[c] = pre[c];
+    } else {
+      std::vector<std::future<void>> jobs;
+      const int threads = std::min(n, s_->cfg.num_compute_threads);
+      for (int w = 0; w < threads; ++w)
+        jobs.push_back(std::async(std::launch::async, [&, w] {
+          for (int c = w; c < n; c += threads) blocks[c] = compress_chunk(s_->cfg, a.chunks[c].first, a.chunks[c].second);
+        }));
+      for (auto& j : jobs) j.get();
+    }
     for (int c = 0; c < n; ++c) {
       m.original_sizes[c] = a.chunks[c].second;
       m.compressed_sizes[c] = blocks[c].size();
@@ -916,6 +1007,8 @@ PYBIND11_MODULE(ZipMoE, m) {
            "Open the offloaded file after the offloading is completed.")
       .def("offload", &PrefetchHandle::offload, "Offload a tensor.")
       .def("batch_offload", &PrefetchHandle::batch_offload, "Offload tensors in a batch.")
+      .def("set_gpu_encode", &PrefetchHandle::set_gpu_encode, py::arg("on"), py::arg("attempts") = 256,
+           "Encode batch_offload's LZ4HC chunks on the GPU (extension).")
       .def("register", &PrefetchHandle::register_tensor, "Register a buffer under its tensor id.")
       .def("begin", &PrefetchHandle::begin, "Pre hook: materialise the tensor on the GPU; returns its id.")
       .def("end", &PrefetchHandle::end, "Post hook: release the tensor's device copy.")
