@@ -180,7 +180,12 @@ struct Layer {
   zmoe_status experts(const uint16_t* xrows, const int32_t* counts_h, int rows, uint16_t* yrows, cudaStream_t s);
   zmoe_status check_status();
   int choose_victim(const std::vector<char>& active);
-  zmoe_status decode_into(const std::vector<std::pair<int, int>>& jobs, cudaStream_t s);
+  // defer_status: the copy of the chunks' status words to the host waits for
+  // queue_status, so that work queued meanwhile (the FFN over the decoded
+  // experts) follows the decode directly on the stream
+  zmoe_status decode_into(const std::vector<std::pair<int, int>>& jobs, cudaStream_t s, bool defer_status = false);
+  zmoe_status queue_status(cudaStream_t s);
+  std::vector<std::pair<int, int>> status_deferred;   // (base, count) of decodes whose status copy waits
   zmoe_status ffn_over(const std::vector<std::pair<int, int>>& groups, int table, const uint16_t* xrows,
                        const int32_t* offsets_dev, int rows, uint16_t* yrows, cudaStream_t s);
   uint16_t* slot_ptr(int slot, int t) const { return slots + ((size_t)slot * tensors + t) * numel; }
@@ -444,13 +449,17 @@ zmoe_status Layer::check_kernel_error(bool wait) {
 }
 
 // Decode (expert, slot) jobs in one fused launch on stream s (the decode stream).
-zmoe_status Layer::decode_into(const std::vector<std::pair<int, int>>& jobs, cudaStream_t s) {
+zmoe_status Layer::decode_into(const std::vector<std::pair<int, int>>& jobs, cudaStream_t s, bool defer_status) {
   int cnt = 0;
   for (auto [e, slot] : jobs)
     for (int t = 0; t < tensors; ++t) cnt += (int)store[e][t].block_off.size();
   if (cnt == 0) return ZMOE_OK;
   int base = 0;
-  zmoe_status st = alloc_desc(cnt, &base);
+  // a status copy still deferred (an earlier call stopped on an error) is
+  // queued first, so that descriptor reuse sees every decode in flight
+  zmoe_status st = status_deferred.empty() ? ZMOE_OK : queue_status(s);
+  if (st != ZMOE_OK) return st;
+  st = alloc_desc(cnt, &base);
   if (st != ZMOE_OK) return st;
   // host tier: each tensor's packed buffer is copied into the staging area
   // ahead of the decode (stream order keeps the previous decode's reads of the
@@ -557,17 +566,27 @@ zmoe_status Layer::decode_into(const std::vector<std::pair<int, int>>& jobs, cud
   stats.launches += 2;                        // map_kernel + resolve_kernel
   stats.decode_launches++;
   stats.decoded_chunks += cnt;
-  ZMOE_CUDA_RET(cudaMemcpyAsync(status_host + base, status_dev + base, sizeof(int32_t) * cnt,
-                                cudaMemcpyDeviceToHost, s));
-  cudaEvent_t done = nullptr;
-  if (!free_events.empty()) {
-    done = free_events.back();
-    free_events.pop_back();
-  } else {
-    ZMOE_CUDA_RET(cudaEventCreateWithFlags(&done, cudaEventDisableTiming));
+  status_deferred.push_back({base, cnt});
+  return defer_status ? ZMOE_OK : queue_status(s);
+}
+
+// Copies the status words of the deferred decodes to the host on stream s and
+// records when they have landed (checked at the next sync point).
+zmoe_status Layer::queue_status(cudaStream_t s) {
+  for (auto [base, cnt] : status_deferred) {
+    ZMOE_CUDA_RET(cudaMemcpyAsync(status_host + base, status_dev + base, sizeof(int32_t) * cnt,
+                                  cudaMemcpyDeviceToHost, s));
+    cudaEvent_t done = nullptr;
+    if (!free_events.empty()) {
+      done = free_events.back();
+      free_events.pop_back();
+    } else {
+      ZMOE_CUDA_RET(cudaEventCreateWithFlags(&done, cudaEventDisableTiming));
+    }
+    ZMOE_CUDA_RET(cudaEventRecord(done, s));
+    pending.push_back({base, cnt, done});
   }
-  ZMOE_CUDA_RET(cudaEventRecord(done, s));
-  pending.push_back({base, cnt, done});
+  status_deferred.clear();
   return ZMOE_OK;
 }
 
@@ -675,7 +694,8 @@ zmoe_status Layer::run_experts(const uint16_t* xrows, const int32_t* offsets_dev
   // 4. Misses decode on the decode stream, in waves of the transient slots;
   //    the FFN over the cache hits runs on the caller's stream meanwhile, and
   //    the FFN over each decoded wave follows its decode.  Every slot a decode
-  //    overwrites was last read by FFN work queued on s before ev_caller.
+  //    overwrites was last read by FFN work queued on s before ev_caller or
+  //    earlier on the decode stream.
   if (!caller_marked) ZMOE_CUDA_RET(cudaEventRecord(ev_caller, s));
   ZMOE_CUDA_RET(cudaStreamWaitEvent(ds, ev_caller, 0));
   size_t tpos = 0;
@@ -690,7 +710,7 @@ zmoe_status Layer::run_experts(const uint16_t* xrows, const int32_t* offsets_dev
     }
   };
   next_wave();
-  if ((st = decode_into(jobs, ds)) != ZMOE_OK) return st;       // the critical path goes first
+  if ((st = decode_into(jobs, ds, true)) != ZMOE_OK) return st; // the critical path goes first
   if (!hits_slots.empty()) {
     if (prefetch_pending) {                                      // hits may sit in slots a prefetch filled
       ZMOE_CUDA_RET(cudaStreamWaitEvent(s, ev_prefetch, 0));
@@ -698,18 +718,22 @@ zmoe_status Layer::run_experts(const uint16_t* xrows, const int32_t* offsets_dev
     }
     if ((st = ffn_over(hits_slots, table++, xrows, offsets_dev, rows, yrows, s)) != ZMOE_OK) return st;
   }
+  // The FFN over each decoded wave follows its decode on the decode stream, so
+  // it starts the moment the decode ends, beside what the caller's stream
+  // still runs (the tail of the FFN over the hits); the next wave's decode,
+  // which reuses the transient slots, follows that FFN on the same stream.
+  // The two FFN launches write disjoint rows of h and yrows.
   while (!jobs.empty()) {
-    ZMOE_CUDA_RET(cudaEventRecord(ev_decoded, ds));
-    ZMOE_CUDA_RET(cudaStreamWaitEvent(s, ev_decoded, 0));
-    if ((st = ffn_over(jobs, table++, xrows, offsets_dev, rows, yrows, s)) != ZMOE_OK) return st;
+    if ((st = ffn_over(jobs, table++, xrows, offsets_dev, rows, yrows, ds)) != ZMOE_OK) return st;
+    if ((st = queue_status(ds)) != ZMOE_OK) return st;
     jobs.clear();
     next_wave();
     if (jobs.empty()) break;
-    // the next wave reuses the transient slots that this wave's FFN reads
-    ZMOE_CUDA_RET(cudaEventRecord(ev_caller, s));
-    ZMOE_CUDA_RET(cudaStreamWaitEvent(ds, ev_caller, 0));
-    if ((st = decode_into(jobs, ds)) != ZMOE_OK) return st;
+    if ((st = decode_into(jobs, ds, true)) != ZMOE_OK) return st;
   }
+  if ((st = queue_status(ds)) != ZMOE_OK) return st;        // a decode with no FFN after it (none queued)
+  ZMOE_CUDA_RET(cudaEventRecord(ev_decoded, ds));
+  ZMOE_CUDA_RET(cudaStreamWaitEvent(s, ev_decoded, 0));
   return ZMOE_OK;
 }
 
