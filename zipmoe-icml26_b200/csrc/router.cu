@@ -7,8 +7,9 @@
 // One CTA of 16 warps per 4 tokens.  The token rows sit in shared memory (fp32);
 // warp w computes the logits of experts w, w+16, ... for the 4 tokens (each
 // weight load serves all 4) with lane l summing h = 256j + 8l + i (j outer, i
-// inner) in fp32 and an xor-butterfly fold, an order the oracle reproduces
-// exactly (products of two bf16 values are exact in fp32).  Warp w < 4 then
+// inner) in fp32 by fused multiply-adds and an xor-butterfly fold, an order the
+// oracle reproduces exactly (products of two bf16 values are exact in fp32, so
+// fused and unfused multiply-add agree).  Warp w < 4 then
 // applies, for token w, the bias and the mode's rounding, the softmax
 // (exp_poly, strided lane sums, butterfly, IEEE divide) and k rounds of warp
 // arg-max with ties to the lower index.
@@ -53,8 +54,10 @@ __device__ __forceinline__ void dot_add(float (&acc)[kTok], const float* xs, int
       const float4 lo = *reinterpret_cast<const float4*>(xr + pi);
       const float4 hi = *reinterpret_cast<const float4*>(xr + H / 2 + pi);
       const float xf[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+      // the product of two bf16 values is exact in fp32 (when it is not
+      // subnormal), so the fused multiply-add rounds exactly as acc + (x * w)
 #pragma unroll
-      for (int i = 0; i < 8; ++i) acc[tk] = __fadd_rn(acc[tk], __fmul_rn(xf[i], wf[i]));
+      for (int i = 0; i < 8; ++i) acc[tk] = __fmaf_rn(xf[i], wf[i], acc[tk]);
     }
   }
 }
@@ -236,7 +239,15 @@ zmoe_status launch_router(const zmoe_router_args* a, cudaStream_t stream) {
   ZMOE_CHECK_ARG((uintptr_t)a->x % 16 == 0 && (uintptr_t)a->w % 16 == 0, "router: x and w must be 16-byte aligned");
   if (a->T <= 0) return ZMOE_OK;
   const size_t smem = (size_t)kTok * a->H * 4 + (size_t)kTok * (a->E + 1) * 4;
-  ZMOE_CUDA_RET(cudaFuncSetAttribute(router_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  if (smem > 48 * 1024) {                              // the largest size set so far, per device
+    static int set_bytes[64] = {};
+    int dev = 0;
+    ZMOE_CUDA_RET(cudaGetDevice(&dev));
+    if ((int)smem > set_bytes[dev & 63]) {
+      ZMOE_CUDA_RET(cudaFuncSetAttribute(router_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+      set_bytes[dev & 63] = (int)smem;
+    }
+  }
   router_kernel<<<(a->T + kTok - 1) / kTok, kThreads, smem, stream>>>(*a);
   return launch_status("router_kernel");
 }
