@@ -3,7 +3,6 @@ bit-exact against the oracle's serial statement of the same parse, liblz4
 restores every block (the reference's decoder call), and the ratio is checked
 against LZ4_compress_HC level 9, which the reference's offload runs
 (csrc/tensor_engine/compressors.cpp:105-122)."""
-import ctypes
 import os
 
 import numpy as np
@@ -122,3 +121,27 @@ def test_encode_reports_overflow_and_bad_descriptors():
     assert (dst[0, 1000:] == 0).all()                # nothing written past the capacity
     bad = lib.zmoe_lz4_encode_chunks(table.data_ptr(), 4, 0, sizes.data_ptr(), None)
     assert bad != 0 and b"max_attempts" in lib.zmoe_last_error()
+
+
+@pytest.mark.parametrize("attempts", [1, 16])
+def test_gpu_encoder_blocks_through_gpu_decoder(attempts):
+    """Blocks from the GPU encoder (shallow searches, long runs the parse
+    extends past the search cap, overlapping matches) decode on the GPU
+    decoder, with its slice index, back to the exact BF16 tensor."""
+    ops = _ops()
+    gen = torch.Generator().manual_seed(3)
+    tensors = [(torch.randn(512, 2048, generator=gen) * 0.02).to(torch.bfloat16),
+               torch.full((300, 1024), 0.5, dtype=torch.bfloat16),                           # one long run
+               (torch.arange(96 * 1024) % 7).reshape(96, 1024).to(torch.bfloat16)]          # period-7 exponents
+    for w in tensors:
+        bits = codec.bf16_bits(w)
+        blocks, osz, sm = ops.encode_tensor(w.cuda(), 3, attempts)
+        host = [_host(b) for b in blocks]
+        exp, sm_ref = codec.split_planes(bits)
+        for c, b in zip(codec.chunk_exponents(exp, 3), host):
+            assert b == codec.lz4_encode_chains(c, attempts)
+        ct = ops.CompressedTensor(host, osz, sm_ref.tobytes())
+        out, st = ct.decode()
+        torch.cuda.synchronize()
+        assert (st.cpu().numpy() == 0).all()
+        assert np.array_equal(out.view(torch.int16).cpu().numpy().view(np.uint16), bits)
